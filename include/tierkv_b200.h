@@ -1,0 +1,201 @@
+/*
+ * tierkv_b200.h -- C ABI of the B200-native (sm_100a) tiered paged
+ * decode-attention path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as `void*` (NULL = legacy default stream); no framework types cross
+ * this boundary.  Calls are asynchronous on the given stream and never
+ * synchronize.  They return a tkv_status code and never abort the process.
+ * No call retains a pointer after it returns; pools may be reallocated by the
+ * caller between calls.
+ *
+ * The functions replace, one for one, the pieces of xiaoMartintin/Paged_TierKV
+ * that sit on the decode hot path (file:line references are into that
+ * project):
+ *
+ *   tkv_decode_attention   tierkv_triton.py:272-465  tierkv_decode_attention()
+ *                          (kernels tierkv_triton.py:45-145, split + reduce
+ *                          tierkv_triton.py:147-264)
+ *   tkv_merge_partials     tierkv_triton.py:231-264  split-KV LSE reduce,
+ *                          also used after the cross-GPU all-gather
+ *   tkv_block_scores       tierkv_policy.py:1905-1912
+ *                          TieredKVRuntime.block_scores_from_probability_sums()
+ *   tkv_quantize_rows_r    tierkv_policy.py:21-36    quantize_fp16_to_int8()
+ *   tkv_demote_to_warm     tierkv_policy.py:1042-1068 (compact pool) and
+ *                          329-361 (dense pool) demote_to_warm(), batched
+ *   tkv_promote_to_hot     tierkv_policy.py:1087-1115 (compact) and 375-402
+ *                          (dense) promote_to_hot(), batched
+ *
+ * Pool layout (the reference's, tierkv_policy.py:129-135 and 835-841):
+ *   hot_k / hot_v     [hot_slots,  kv_heads, block_size, head_dim] fp16
+ *   warm_k / warm_v   [warm_slots, kv_heads, block_size, head_dim]
+ *                       Format R: uint8 codes (the reference layout)
+ *                       Format S: int8 codes
+ *   k_scale/k_zero/v_scale/v_zero
+ *                       Format R: [warm_slots, kv_heads, block_size(, 1)] fp16
+ *                       Format S: k_scale/v_scale [warm_slots, kv_heads] fp32,
+ *                                 k_zero/v_zero unused (may be NULL)
+ * Tables (per sequence row, `table_stride` int32 apart):
+ *   block_table[b]   slot of logical block b in the HOT pool when
+ *                    block_states[b] == 0, in the WARM pool when == 1;
+ *                    ignored (never dereferenced) for COLD blocks
+ *   block_states[b]  0 HOT, 1 WARM, anything else COLD (evicted)
+ *   block_lengths[b] valid tokens of logical block b (clamped to [0, bs])
+ */
+#ifndef TIERKV_B200_H
+#define TIERKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TKV_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------ */
+#define TKV_OK                 0
+#define TKV_ERR_INVALID        1  /* bad pointer / shape / size   -> ValueError  */
+#define TKV_ERR_UNSUPPORTED    2  /* geometry or format not built -> ValueError  */
+#define TKV_ERR_WORKSPACE      3  /* workspace missing or too small -> ValueError */
+#define TKV_ERR_CUDA           4  /* CUDA driver / launch failure -> RuntimeError */
+#define TKV_ERR_NO_DEVICE      5  /* no usable sm_100 device       -> RuntimeError */
+
+/* ---- enums --------------------------------------------------------------- */
+#define TKV_STATE_HOT   0
+#define TKV_STATE_WARM  1
+#define TKV_STATE_COLD  2
+
+#define TKV_FORMAT_R    0  /* uint8, asymmetric, fp16 scale + zero per token row */
+#define TKV_FORMAT_S    1  /* int8, symmetric absmax, fp32 scale per (block, kv head) */
+
+#define TKV_DTYPE_F16   0
+#define TKV_DTYPE_BF16  1
+#define TKV_DTYPE_F32   2
+
+/* Device-side error bits, reported through tkv_read_device_errors(). */
+#define TKV_DEVERR_BAD_SLOT  0x1u  /* HOT/WARM block whose slot is outside its pool */
+#define TKV_DEVERR_TIMEOUT   0x2u  /* a bounded pipeline wait gave up            */
+
+typedef struct tkv_pools {
+    void*   hot_k;
+    void*   hot_v;
+    void*   warm_k;
+    void*   warm_v;
+    void*   k_scale;
+    void*   k_zero;
+    void*   v_scale;
+    void*   v_zero;
+    int64_t hot_slots;
+    int64_t warm_slots;
+    int32_t kv_heads;
+    int32_t block_size;   /* 16 or 32 */
+    int32_t head_dim;     /* 64 or 128 */
+    int32_t format;       /* TKV_FORMAT_R / TKV_FORMAT_S */
+} tkv_pools;
+
+typedef struct tkv_decode_args {
+    const void*    query;          /* [batch, num_heads, head_dim] (query_len 1) */
+    int32_t        query_dtype;    /* TKV_DTYPE_F16 / TKV_DTYPE_BF16 */
+    int32_t        out_dtype;      /* TKV_DTYPE_F16 / BF16 / F32 */
+    int32_t        batch;
+    int32_t        num_heads;
+    int32_t        num_kv_groups;  /* num_heads / kv_heads, 1..8 */
+    int32_t        max_blocks;     /* columns of score_sums (block_table length) */
+    const int32_t* block_table;    /* [batch, table_stride] */
+    const int32_t* block_states;
+    const int32_t* block_lengths;
+    int64_t        table_stride;
+    const int32_t* num_blocks_dev; /* optional device [batch] block counts */
+    int32_t        num_blocks;     /* uniform count, or upper bound of num_blocks_dev */
+    float          scaling;
+    void*          out;            /* [batch, num_heads, head_dim] out_dtype; with
+                                      out_dtype F32 the row is the normalised
+                                      partial o of a context shard */
+    float*         out_lse;        /* optional [batch, num_heads] natural-log LSE */
+    float*         score_sums;     /* optional [batch, num_heads, max_blocks] */
+    int32_t        num_splits;     /* 0 = automatic */
+    int32_t        flags;          /* reserved, 0 */
+    void*          workspace;      /* zero-filled once by the owner, see below */
+    size_t         workspace_bytes;
+} tkv_decode_args;
+
+/* Library version (TKV_ABI_VERSION) and a static message for a status. */
+int32_t     tkv_get_version(void);
+const char* tkv_status_string(int32_t status);
+
+/* Number of splits the launch will use and the workspace it needs.
+ * The workspace must be zero-filled once when it is allocated; the kernels
+ * leave it in that state (its split counters reset themselves).  Concurrent
+ * calls on different streams need different workspaces.
+ * Replaces the partial-buffer allocations of tierkv_triton.py:316-325. */
+int32_t tkv_decode_plan(const tkv_pools* pools, const tkv_decode_args* args,
+                        int32_t* num_splits_out, size_t* workspace_bytes_out);
+
+/* Tiered paged decode attention, one query token per sequence.
+ * HOT tiles are read as fp16, WARM tiles dequantized in registers, COLD
+ * tiles never read (each valid COLD token adds logit 0 / value 0, as in the
+ * reference).  Optional per-block softmax mass (score_sums) as in
+ * tierkv_triton.py:121-145 (zero for blocks >= num_blocks).
+ * Replaces tierkv_triton.py:272-465. */
+int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* args, void* stream);
+
+/* LSE merge of `parts` normalised partials.  Partial i is the fp32 block
+ * part_o + i * o_part_stride ([rows, head_dim]) with its natural-log LSEs at
+ * part_lse + i * lse_part_stride ([rows], -inf = empty); strides are in
+ * elements, so one all-gathered [parts, rows*head_dim + rows] buffer can be
+ * merged in place.  Writes out [rows, head_dim] (out_dtype) and optionally
+ * out_lse [rows].
+ * Replaces tierkv_triton.py:231-264 (and merges context shards). */
+int32_t tkv_merge_partials(const float* part_o, int64_t o_part_stride, const float* part_lse,
+                           int64_t lse_part_stride, int32_t parts, int32_t rows,
+                           int32_t head_dim, void* out, int32_t out_dtype, float* out_lse,
+                           void* stream);
+
+/* Per-block importance: block_scores[s, b] = mean_h score_sums[s, h, b] /
+ * max(block_lengths[s, b], 1) for b < num_blocks(s), 0 beyond.
+ * score_sums [batch, num_heads, max_blocks]; block_scores [batch, max_blocks].
+ * Replaces tierkv_policy.py:1905-1912. */
+int32_t tkv_block_scores(const float* score_sums, const int32_t* block_lengths,
+                         int64_t table_stride, const int32_t* num_blocks_dev,
+                         int32_t num_blocks, int32_t batch, int32_t num_heads,
+                         int32_t max_blocks, float* block_scores, void* stream);
+
+/* Format R quantization of `rows` contiguous fp16 rows of `dim` values,
+ * bit-exact with quantize_fp16_to_int8 (tierkv_policy.py:21-36):
+ * codes [rows, dim] uint8, scale / zero [rows] fp16. */
+int32_t tkv_quantize_rows_r(const void* x, int64_t rows, int32_t dim, void* codes,
+                            void* scale, void* zero, void* stream);
+
+/* Batched HOT->WARM demotion of whole blocks (all kv heads, K and V):
+ * block i reads HOT slot src_hot_slots[i] rows [0, lengths[i]) and writes
+ * WARM slot dst_warm_slots[i].  Format R: bit-exact with demote_to_warm;
+ * clear_tail != 0 additionally sets rows >= length to code 0 / scale 1 /
+ * zero 0 (dense pool, tierkv_policy.py:350-356); clear_tail == 0 leaves them
+ * (compact pool, tierkv_policy.py:1058-1063).  Format S: one fp32 scale per
+ * (block, kv head) over the valid rows; tail rows get code 0.
+ * Slot lists and lengths are device int32 arrays of `count` entries.
+ * Replaces tierkv_policy.py:1042-1068 / 329-361. */
+int32_t tkv_demote_to_warm(const tkv_pools* pools, const int32_t* src_hot_slots,
+                           const int32_t* dst_warm_slots, const int32_t* lengths,
+                           int32_t count, int32_t clear_tail, void* stream);
+
+/* Batched WARM->HOT promotion (Format R), bit-exact with
+ * dequantize_int8_to_fp16 (tierkv_policy.py:39-44) as used by promote_to_hot
+ * (tierkv_policy.py:1087-1115): rows [0, lengths[i]) of WARM slot
+ * src_warm_slots[i] are written to HOT slot dst_hot_slots[i].
+ * Replaces tierkv_policy.py:1087-1115 / 375-402. */
+int32_t tkv_promote_to_hot(const tkv_pools* pools, const int32_t* src_warm_slots,
+                           const int32_t* dst_hot_slots, const int32_t* lengths,
+                           int32_t count, void* stream);
+
+/* Reads and clears the device error bits (TKV_DEVERR_*) that decode calls
+ * using this workspace have recorded.  Synchronizes the stream. */
+int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TIERKV_B200_H */

@@ -1,0 +1,395 @@
+// tkv_api.cu -- the extern "C" boundary declared in include/tierkv_b200.h.
+//
+// Validates arguments the way the reference wrapper does
+// (tierkv_triton.py:290-304; errors become status codes instead of Python
+// exceptions), plans the split-KV partition, carves the caller's workspace,
+// encodes the TMA descriptors of the four data pools and launches the sm_100a
+// kernels on the caller's stream.  Nothing here allocates device memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "tierkv_b200.h"
+#include "tkv_internal.h"
+
+using namespace tkv;
+
+namespace {
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D tiled map over a pool viewed as [rows, head_dim] elements.
+bool encode_pool_map(CUtensorMap* map, void* base, bool fp16, int64_t rows, int head_dim,
+                     int box_inner, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const int esize = fp16 ? 2 : 1;
+  cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)head_dim * esize};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const int inner_bytes = box_inner * esize;
+  CUtensorMapSwizzle swz = inner_bytes == 128   ? CU_TENSOR_MAP_SWIZZLE_128B
+                           : inner_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                               : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = fn(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                  base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int current_device_sms(int* sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TKV_ERR_NO_DEVICE;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return TKV_ERR_NO_DEVICE;
+  if (major != 10) return TKV_ERR_NO_DEVICE;
+  if (cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return TKV_ERR_NO_DEVICE;
+  return TKV_OK;
+}
+
+int32_t check_pools(const tkv_pools* pl, bool need_meta) {
+  if (!pl) return TKV_ERR_INVALID;
+  if (pl->format != TKV_FORMAT_R && pl->format != TKV_FORMAT_S) return TKV_ERR_UNSUPPORTED;
+  if (pl->head_dim != 64 && pl->head_dim != 128) return TKV_ERR_UNSUPPORTED;
+  if (pl->block_size != 16 && pl->block_size != 32) return TKV_ERR_UNSUPPORTED;
+  if (pl->kv_heads <= 0 || pl->hot_slots <= 0 || pl->warm_slots <= 0) return TKV_ERR_INVALID;
+  if (!pl->hot_k || !pl->hot_v || !pl->warm_k || !pl->warm_v) return TKV_ERR_INVALID;
+  if (!aligned(pl->hot_k, 16) || !aligned(pl->hot_v, 16) || !aligned(pl->warm_k, 16) ||
+      !aligned(pl->warm_v, 16))
+    return TKV_ERR_INVALID;
+  const int64_t max_rows = std::max(pl->hot_slots, pl->warm_slots) * pl->kv_heads * pl->block_size;
+  if (max_rows >= (int64_t(1) << 31)) return TKV_ERR_INVALID;
+  if (need_meta) {
+    if (!pl->k_scale || !pl->v_scale) return TKV_ERR_INVALID;
+    if (pl->format == TKV_FORMAT_R) {
+      if (!pl->k_zero || !pl->v_zero) return TKV_ERR_INVALID;
+      if (!aligned(pl->k_scale, 16) || !aligned(pl->k_zero, 16) || !aligned(pl->v_scale, 16) ||
+          !aligned(pl->v_zero, 16))
+        return TKV_ERR_INVALID;
+    } else if (!aligned(pl->k_scale, 4) || !aligned(pl->v_scale, 4)) {
+      return TKV_ERR_INVALID;
+    }
+  }
+  return TKV_OK;
+}
+
+struct Plan {
+  int splits = 1;
+  size_t off_err = 0, off_counters = 0, off_part_o = 0, off_part_lse = 0, off_lse_final = 0,
+         off_lse_blk = 0, total = 0;
+};
+
+int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
+  int32_t st = check_pools(pl, true);
+  if (st != TKV_OK) return st;
+  if (!a) return TKV_ERR_INVALID;
+  if (a->batch <= 0 || a->num_heads <= 0 || a->num_kv_groups <= 0) return TKV_ERR_INVALID;
+  if (a->num_kv_groups > kMaxGroups) return TKV_ERR_UNSUPPORTED;
+  if ((int64_t)pl->kv_heads * a->num_kv_groups != a->num_heads) return TKV_ERR_INVALID;
+  if (a->query_dtype != TKV_DTYPE_F16 && a->query_dtype != TKV_DTYPE_BF16) return TKV_ERR_UNSUPPORTED;
+  if (a->out_dtype != TKV_DTYPE_F16 && a->out_dtype != TKV_DTYPE_BF16 && a->out_dtype != TKV_DTYPE_F32)
+    return TKV_ERR_UNSUPPORTED;
+  if (a->num_blocks < 0 || a->max_blocks < 0 || a->num_blocks > a->max_blocks) return TKV_ERR_INVALID;
+  if (a->table_stride < a->max_blocks) return TKV_ERR_INVALID;
+  if (a->num_splits < 0 || a->num_splits > kMaxSplits) return TKV_ERR_INVALID;
+  int splits = a->num_splits;
+  if (splits == 0) {
+    int sms = 0;
+    st = current_device_sms(&sms);
+    if (st != TKV_OK) return st;
+    int ctas = 0;
+    if (decode_occupancy(pl->head_dim, pl->block_size, pl->format, a->query_dtype, &ctas) !=
+            cudaSuccess ||
+        ctas <= 0)
+      return TKV_ERR_CUDA;
+    const int64_t slots = (int64_t)sms * ctas;
+    const int64_t units = (int64_t)a->batch * pl->kv_heads;
+    const int nb = std::max(1, a->num_blocks);
+    // cost ~ waves * (blocks per CTA + fixed CTA overhead of ~4 blocks)
+    double best = 1e300;
+    splits = 1;
+    const int max_s = std::min(kMaxSplits, nb);
+    for (int s = 1; s <= max_s; ++s) {
+      const int64_t ctas_total = units * s;
+      const double waves = (double)((ctas_total + slots - 1) / slots);
+      const double per = std::ceil((double)nb / s);
+      const double cost = waves * (per + 4.0);
+      if (cost < best - 1e-9) {
+        best = cost;
+        splits = s;
+      }
+    }
+  }
+  plan->splits = std::max(1, splits);
+  const size_t rows = (size_t)a->batch * a->num_heads;
+  size_t off = 0;
+  plan->off_err = off;
+  off = align_up(off + 16);
+  plan->off_counters = off;
+  off = align_up(off + sizeof(uint32_t) * (size_t)a->batch * pl->kv_heads);
+  if (plan->splits > 1) {
+    plan->off_part_o = off;
+    off = align_up(off + sizeof(float) * rows * plan->splits * pl->head_dim);
+    plan->off_part_lse = off;
+    off = align_up(off + sizeof(float) * rows * plan->splits);
+  }
+  if (a->score_sums) {
+    plan->off_lse_final = off;
+    off = align_up(off + sizeof(float) * rows);
+    plan->off_lse_blk = off;
+    off = align_up(off + sizeof(float) * rows * std::max(1, a->max_blocks));
+  }
+  plan->total = off;
+  return TKV_OK;
+}
+
+inline int32_t cuda_status(cudaError_t e) { return e == cudaSuccess ? TKV_OK : TKV_ERR_CUDA; }
+
+}  // namespace
+
+extern "C" {
+
+int32_t tkv_get_version(void) { return TKV_ABI_VERSION; }
+
+const char* tkv_status_string(int32_t status) {
+  switch (status) {
+    case TKV_OK: return "ok";
+    case TKV_ERR_INVALID: return "invalid argument (pointer, shape, stride or alignment)";
+    case TKV_ERR_UNSUPPORTED: return "unsupported geometry, dtype or WARM format";
+    case TKV_ERR_WORKSPACE: return "workspace missing or smaller than tkv_decode_plan() requires";
+    case TKV_ERR_CUDA: return "CUDA error while encoding or launching";
+    case TKV_ERR_NO_DEVICE: return "no usable sm_100 (B200) device is current";
+    default: return "unknown status";
+  }
+}
+
+int32_t tkv_decode_plan(const tkv_pools* pools, const tkv_decode_args* args,
+                        int32_t* num_splits_out, size_t* workspace_bytes_out) {
+  Plan plan;
+  const int32_t st = make_plan(pools, args, &plan);
+  if (st != TKV_OK) return st;
+  if (num_splits_out) *num_splits_out = plan.splits;
+  if (workspace_bytes_out) *workspace_bytes_out = plan.total;
+  return TKV_OK;
+}
+
+int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, void* stream) {
+  Plan plan;
+  int32_t st = make_plan(pools, a, &plan);
+  if (st != TKV_OK) return st;
+  if (!a->query || !a->out || !aligned(a->query, 4)) return TKV_ERR_INVALID;
+  if (a->max_blocks > 0 && (!a->block_table || !a->block_states || !a->block_lengths))
+    return TKV_ERR_INVALID;
+  if (!a->workspace || a->workspace_bytes < plan.total || !aligned(a->workspace, 256))
+    return TKV_ERR_WORKSPACE;
+  if (pools->hot_slots * pools->kv_heads * pools->block_size >= (int64_t(1) << 31))
+    return TKV_ERR_INVALID;
+  int sms = 0;
+  st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+
+  CUtensorMap maps[4];
+  const int bs = pools->block_size, d = pools->head_dim, hkv = pools->kv_heads;
+  const int64_t hot_rows = pools->hot_slots * hkv * bs;
+  const int64_t warm_rows = pools->warm_slots * hkv * bs;
+  if (!encode_pool_map(&maps[0], pools->hot_k, true, hot_rows, d, 64, bs) ||
+      !encode_pool_map(&maps[1], pools->hot_v, true, hot_rows, d, 64, bs) ||
+      !encode_pool_map(&maps[2], pools->warm_k, false, warm_rows, d, d, bs) ||
+      !encode_pool_map(&maps[3], pools->warm_v, false, warm_rows, d, d, bs))
+    return TKV_ERR_CUDA;
+
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.query = a->query;
+  p.table = a->block_table;
+  p.states = a->block_states;
+  p.lengths = a->block_lengths;
+  p.nb_dev = a->num_blocks_dev;
+  p.k_scale = pools->k_scale;
+  p.k_zero = pools->k_zero;
+  p.v_scale = pools->v_scale;
+  p.v_zero = pools->v_zero;
+  p.out = a->out;
+  p.out_lse = a->out_lse;
+  p.err = reinterpret_cast<uint32_t*>(ws + plan.off_err);
+  p.counters = reinterpret_cast<uint32_t*>(ws + plan.off_counters);
+  if (plan.splits > 1) {
+    p.part_o = reinterpret_cast<float*>(ws + plan.off_part_o);
+    p.part_lse = reinterpret_cast<float*>(ws + plan.off_part_lse);
+  }
+  if (a->score_sums) {
+    p.lse_final = reinterpret_cast<float*>(ws + plan.off_lse_final);
+    p.lse_blk = reinterpret_cast<float*>(ws + plan.off_lse_blk);
+  }
+  p.table_stride = a->table_stride;
+  p.hot_slots = pools->hot_slots;
+  p.warm_slots = pools->warm_slots;
+  p.nb_uniform = a->num_blocks;
+  p.batch = a->batch;
+  p.kv_heads = hkv;
+  p.num_heads = a->num_heads;
+  p.groups = a->num_kv_groups;
+  p.max_blocks = a->max_blocks;
+  p.splits = plan.splits;
+  p.out_dtype = a->out_dtype;
+  p.scale_log2 = a->scaling * kLog2e;
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  st = cuda_status(launch_decode(p, maps, d, bs, pools->format, a->query_dtype, s));
+  if (st != TKV_OK || !a->score_sums) return st;
+  ScoreParams sp;
+  sp.lse_blk = p.lse_blk;
+  sp.lse_final = p.lse_final;
+  sp.nb_dev = a->num_blocks_dev;
+  sp.score_sums = a->score_sums;
+  sp.nb_uniform = a->num_blocks;
+  sp.num_heads = a->num_heads;
+  sp.max_blocks = a->max_blocks;
+  sp.rows = a->batch * a->num_heads;
+  if (a->max_blocks == 0) return TKV_OK;
+  return cuda_status(launch_scores(sp, s));
+}
+
+int32_t tkv_merge_partials(const float* part_o, int64_t o_part_stride, const float* part_lse,
+                           int64_t lse_part_stride, int32_t parts, int32_t rows,
+                           int32_t head_dim, void* out, int32_t out_dtype, float* out_lse,
+                           void* stream) {
+  if (!part_o || !part_lse || !out || parts <= 0 || rows < 0 || head_dim <= 0)
+    return TKV_ERR_INVALID;
+  if (parts > 1 && (o_part_stride < (int64_t)rows * head_dim || lse_part_stride < rows))
+    return TKV_ERR_INVALID;
+  if (out_dtype != TKV_DTYPE_F16 && out_dtype != TKV_DTYPE_BF16 && out_dtype != TKV_DTYPE_F32)
+    return TKV_ERR_UNSUPPORTED;
+  if (rows == 0) return TKV_OK;
+  int sms = 0;
+  int32_t st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+  MergeParams p{part_o, part_lse, o_part_stride, lse_part_stride, out, out_lse,
+                parts, rows, head_dim, out_dtype};
+  return cuda_status(launch_merge(p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int32_t tkv_block_scores(const float* score_sums, const int32_t* block_lengths,
+                         int64_t table_stride, const int32_t* num_blocks_dev, int32_t num_blocks,
+                         int32_t batch, int32_t num_heads, int32_t max_blocks,
+                         float* block_scores, void* stream) {
+  if (!score_sums || !block_lengths || !block_scores || batch <= 0 || num_heads <= 0 ||
+      max_blocks < 0 || num_blocks < 0 || num_blocks > max_blocks || table_stride < max_blocks)
+    return TKV_ERR_INVALID;
+  if (max_blocks == 0) return TKV_OK;
+  int sms = 0;
+  int32_t st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+  BlockScoreParams p{score_sums, block_lengths, num_blocks_dev, block_scores, table_stride,
+                     num_blocks,  batch,         num_heads,      max_blocks};
+  return cuda_status(launch_block_scores(p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int32_t tkv_quantize_rows_r(const void* x, int64_t rows, int32_t dim, void* codes, void* scale,
+                            void* zero, void* stream) {
+  if (rows < 0 || !x || !codes || !scale || !zero) return TKV_ERR_INVALID;
+  if (dim != 16 && dim != 32 && dim != 64 && dim != 128 && dim != 256) return TKV_ERR_UNSUPPORTED;
+  if (!aligned(x, 16) || !aligned(codes, 8) || !aligned(scale, 2) || !aligned(zero, 2))
+    return TKV_ERR_INVALID;
+  if (rows == 0) return TKV_OK;
+  int sms = 0;
+  int32_t st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+  return cuda_status(
+      launch_quantize_rows(x, rows, dim, codes, scale, zero, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+static int32_t fill_demote(const tkv_pools* pl, const int32_t* src, const int32_t* dst,
+                           const int32_t* lengths, int32_t count, int32_t clear_tail,
+                           DemoteParams* p) {
+  int32_t st = check_pools(pl, true);
+  if (st != TKV_OK) return st;
+  if (count < 0) return TKV_ERR_INVALID;
+  if (count > 0 && (!src || !dst || !lengths)) return TKV_ERR_INVALID;
+  p->hot_k = pl->hot_k;
+  p->hot_v = pl->hot_v;
+  p->warm_k = pl->warm_k;
+  p->warm_v = pl->warm_v;
+  p->k_scale = pl->k_scale;
+  p->k_zero = pl->k_zero;
+  p->v_scale = pl->v_scale;
+  p->v_zero = pl->v_zero;
+  p->src = src;
+  p->dst = dst;
+  p->lengths = lengths;
+  p->hot_slots = pl->hot_slots;
+  p->warm_slots = pl->warm_slots;
+  p->count = count;
+  p->kv_heads = pl->kv_heads;
+  p->block_size = pl->block_size;
+  p->head_dim = pl->head_dim;
+  p->clear_tail = clear_tail;
+  return TKV_OK;
+}
+
+int32_t tkv_demote_to_warm(const tkv_pools* pools, const int32_t* src_hot_slots,
+                           const int32_t* dst_warm_slots, const int32_t* lengths, int32_t count,
+                           int32_t clear_tail, void* stream) {
+  DemoteParams p;
+  int32_t st = fill_demote(pools, src_hot_slots, dst_warm_slots, lengths, count, clear_tail, &p);
+  if (st != TKV_OK) return st;
+  if (count == 0) return TKV_OK;
+  int sms = 0;
+  st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+  return cuda_status(launch_demote(p, pools->format, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int32_t tkv_promote_to_hot(const tkv_pools* pools, const int32_t* src_warm_slots,
+                           const int32_t* dst_hot_slots, const int32_t* lengths, int32_t count,
+                           void* stream) {
+  if (pools && pools->format != TKV_FORMAT_R) return TKV_ERR_UNSUPPORTED;
+  DemoteParams p;
+  int32_t st = fill_demote(pools, src_warm_slots, dst_hot_slots, lengths, count, 0, &p);
+  if (st != TKV_OK) return st;
+  if (count == 0) return TKV_OK;
+  int sms = 0;
+  st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+  return cuda_status(launch_promote(p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream) {
+  if (!workspace || !bits_out) return TKV_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t bits = 0;
+  if (cudaMemcpyAsync(&bits, workspace, sizeof(bits), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return TKV_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return TKV_ERR_CUDA;
+  if (cudaMemsetAsync(workspace, 0, sizeof(uint32_t), s) != cudaSuccess) return TKV_ERR_CUDA;
+  *bits_out = bits;
+  return TKV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,866 @@
+// tkv_decode.cu -- tiered paged decode attention for sm_100a.
+//
+// Replaces the Triton kernels of xiaoMartintin/Paged_TierKV
+// (tierkv_triton.py:45-145 single pass + score pass, 147-264 split + reduce).
+//
+// One CTA per (split, kv head, sequence).  Warp 0 is the producer: it reads
+// the block table 32 entries at a time, skips COLD blocks (their valid tokens
+// only add the analytic term n * exp(0 - m) to the softmax denominator), and
+// streams each HOT / WARM block tile of this kv head through a ring of shared
+// memory stages with TMA (128-byte swizzled boxes; no multicast), completing
+// on an mbarrier per stage.  Warps 1..4 consume tiles round-robin: each tile
+// is one logical block (16 or 32 tokens x head_dim) for all query heads of
+// the GQA group, so K/V are read from HBM once per kv head.
+//   S^T[tok, h] = K[tok, :] . Q[h, :]       mma.m16n8k16 (M = tokens, N = heads)
+//   O^T[d, h]  += V^T[d, tok] . P^T[tok, h] mma.m16n8k16 (M = head_dim rows)
+// HOT tiles feed ldmatrix directly; WARM tiles (uint8 codes) are expanded in
+// registers with byte permutes into exact fp16 (code - zero) values, the
+// per-token scale being applied to the logits (K) and folded into P (V).
+// Online softmax runs in the log2 domain in fp32.  Each consumer keeps its own
+// (m, l, acc); the CTA merges them, then either writes the output (one split)
+// or a normalised partial plus its LSE; the last CTA of a (sequence, kv head)
+// merges the splits (split tickets reset themselves).
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "tkv_internal.h"
+#include "tkv_ptx.cuh"
+
+namespace tkv {
+
+struct TileInfo {
+  int32_t state;  // 0 HOT, 1 WARM, -1 end of stream
+  int32_t len;    // valid tokens (1..bs)
+  int32_t block;  // logical block index
+  float ks;       // Format S: K scale of the tile
+  float vs;       // Format S: V scale of the tile
+  int32_t pad[3];
+};
+
+template <int D, int BS, int FMT, int QT>
+struct DecodeCfg {
+  static constexpr int kConsumers = 4;
+  static constexpr int kThreads = 32 * (kConsumers + 1);
+  static constexpr int kHotBytes = BS * D * 2;            // one K (or V) HOT tile
+  static constexpr int kStageBytes = 2 * kHotBytes;       // K + V, multiple of 1024
+  static constexpr int kStages = (kStageBytes <= 8192) ? 8 : 4;
+  static constexpr int kMetaBytes = (FMT == kFmtR) ? 4 * BS * 2 : 16;
+  static constexpr int kKS = D / 16;                      // 16-wide steps over head_dim
+  static constexpr int kSub = BS / 16;                    // 16-token sub-tiles per block
+  static constexpr int kWarmSwz = (D == 128) ? 7 : 3;     // SWIZZLE_128B / SWIZZLE_64B
+  // layout of dynamic shared memory (after aligning the base to 1024)
+  static constexpr int kOffBars = kStages * kStageBytes;
+  static constexpr int kOffInfo = kOffBars + 2 * kStages * 8;
+  static constexpr int kOffMeta = kOffInfo + kStages * (int)sizeof(TileInfo);
+  static constexpr int kOffMisc = kOffMeta + kStages * kMetaBytes;
+  static constexpr int kSmemBytes = 1024 + kOffMisc + 64;
+  // the end-of-kernel merge scratch aliases the stage ring
+  static constexpr int kMergeFloats = kConsumers * (2 * kMaxGroups + kMaxGroups * D);
+  static_assert(kMergeFloats * 4 <= kStages * kStageBytes, "merge scratch must fit the ring");
+  static_assert(kMaxGroups * kMaxSplits * 4 <= kStages * kStageBytes, "split scratch must fit");
+};
+
+__device__ __forceinline__ void store_out(void* out, int dtype, size_t idx, float v) {
+  if (dtype == kDtF16) {
+    reinterpret_cast<__half*>(out)[idx] = __float2half_rn(v);
+  } else if (dtype == kDtBF16) {
+    reinterpret_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<float*>(out)[idx] = v;
+  }
+}
+
+__device__ __forceinline__ uint32_t ld_u32(const void* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+
+// Query fragments of one consumer warp.  Lane (g, t) supplies column n = g
+// (query head kvh*G + g) of the B operand.
+//  qh: standard layout for ldmatrix-fed HOT K:   d = 16ks + 2t + {0,1}, +8
+//  qw: layout of the register-expanded WARM K:   d = t*D/4 + 4s + {0,1}, {2,3}
+// bf16 queries are rescaled per head by 2^-e (exact) so they fit fp16; the
+// factor 2^e is folded into qmul.
+template <int D, int QT>
+__device__ __forceinline__ void load_query(const DecodeParams& p, int seq, int kvh, int lane,
+                                           uint32_t (&qh)[D / 16][2], uint32_t (&qw)[D / 16][2],
+                                           float (&qmul)[2]) {
+  const int g = lane >> 2, t = lane & 3;
+  const bool valid = g < p.groups;
+  const size_t row = (size_t)seq * p.num_heads + (size_t)kvh * p.groups + (valid ? g : 0);
+  int e = 0;
+  if (QT == kDtF16) {
+    const __half* q = reinterpret_cast<const __half*>(p.query) + row * D;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      qh[ks][0] = valid ? ld_u32(q + 16 * ks + 2 * t) : 0u;
+      qh[ks][1] = valid ? ld_u32(q + 16 * ks + 2 * t + 8) : 0u;
+      qw[ks][0] = valid ? ld_u32(q + t * (D / 4) + 4 * ks) : 0u;
+      qw[ks][1] = valid ? ld_u32(q + t * (D / 4) + 4 * ks + 2) : 0u;
+    }
+  } else {
+    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.query) + row * D;
+    float amax = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t])));
+      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t + 1])));
+      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t + 8])));
+      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t + 9])));
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    int k = 0;
+    frexpf(amax, &k);          // amax < 2^k
+    e = valid ? max(0, k - 15) : 0;
+    const float f = ldexpf(1.f, -e);
+    auto cv = [&](int d) -> uint32_t {
+      if (!valid) return 0u;
+      return pack_half2(__bfloat162float(q[d]) * f, __bfloat162float(q[d + 1]) * f);
+    };
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      qh[ks][0] = cv(16 * ks + 2 * t);
+      qh[ks][1] = cv(16 * ks + 2 * t + 8);
+      qw[ks][0] = cv(t * (D / 4) + 4 * ks);
+      qw[ks][1] = cv(t * (D / 4) + 4 * ks + 2);
+    }
+  }
+  // logits of heads 2t and 2t+1 live in this lane; fetch those heads' factors
+  const int e0 = __shfl_sync(0xffffffffu, e, (2 * t) * 4);
+  const int e1 = __shfl_sync(0xffffffffu, e, (2 * t + 1) * 4);
+  qmul[0] = ldexpf(p.scale_log2, e0);
+  qmul[1] = ldexpf(p.scale_log2, e1);
+}
+
+constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0
+
+template <int D, int BS, int FMT, int QT>
+__global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, 2)
+    decode_kernel(const __grid_constant__ DecodeParams p,
+                  const __grid_constant__ CUtensorMap tm_hk,
+                  const __grid_constant__ CUtensorMap tm_hv,
+                  const __grid_constant__ CUtensorMap tm_wk,
+                  const __grid_constant__ CUtensorMap tm_wv) {
+  using Cfg = DecodeCfg<D, BS, FMT, QT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
+  uint64_t* empty_bar = full_bar + Cfg::kStages;
+  TileInfo* info = reinterpret_cast<TileInfo*>(smem + Cfg::kOffInfo);
+  uint8_t* meta = smem + Cfg::kOffMeta;
+  int* misc = reinterpret_cast<int*>(smem + Cfg::kOffMisc);  // [0] cold tokens, [1] last-CTA flag
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int seq = blockIdx.z;
+  const int G = p.groups;
+  const int Hq = p.num_heads;
+
+  int nb = p.nb_dev ? p.nb_dev[seq] : p.nb_uniform;
+  nb = max(0, min(nb, p.max_blocks));
+  const int per = (nb + p.splits - 1) / p.splits;
+  const int b0 = min(nb, split * per);
+  const int b1 = min(nb, b0 + per);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    misc[0] = 0;
+    misc[1] = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_hk);
+      prefetch_tensormap(&tm_hv);
+      prefetch_tensormap(&tm_wk);
+      prefetch_tensormap(&tm_wv);
+    }
+    const int32_t* trow = p.table + (size_t)seq * p.table_stride;
+    const int32_t* srow = p.states + (size_t)seq * p.table_stride;
+    const int32_t* lrow = p.lengths + (size_t)seq * p.table_stride;
+    int tile = 0;
+    int cold = 0;
+    bool fail = false;
+    // software-pipelined table reads: entries of the next 32-block chunk are
+    // requested before the current chunk's tiles are issued
+    int nslot = -1, nstate = 2, nlen = 0;
+    if (b0 + lane < b1) {
+      nslot = __ldg(trow + b0 + lane);
+      nstate = __ldg(srow + b0 + lane);
+      nlen = __ldg(lrow + b0 + lane);
+    }
+    for (int base = b0; base < b1 && !fail; base += 32) {
+      const int i = base + lane;
+      const int slot = nslot;
+      const int st = nstate;
+      const int len = max(0, min(nlen, BS));
+      if (base + 32 + lane < b1) {
+        nslot = __ldg(trow + base + 32 + lane);
+        nstate = __ldg(srow + base + 32 + lane);
+        nlen = __ldg(lrow + base + 32 + lane);
+      }
+      bool issue = (i < b1) && (st == 0 || st == 1) && len > 0;
+      if (issue) {
+        const int64_t cap = (st == 0) ? p.hot_slots : p.warm_slots;
+        if (slot < 0 || (int64_t)slot >= cap) {
+          issue = false;  // out-of-pool slot: read as zeros, reported
+          atomicOr(p.err, 0x1u);
+        }
+      }
+      if (i < b1 && !issue) {
+        cold += len;
+        if (p.lse_blk != nullptr) {
+          const float v = len > 0 ? logf((float)len) : -INFINITY;
+          for (int h = 0; h < G; ++h)
+            p.lse_blk[((size_t)seq * Hq + (size_t)kvh * G + h) * p.max_blocks + i] = v;
+        }
+      }
+      float ks = 1.f, vs = 1.f;
+      if (FMT == kFmtS && issue && st == 1) {
+        const size_t mi = (size_t)slot * p.kv_heads + kvh;
+        ks = __ldg(reinterpret_cast<const float*>(p.k_scale) + mi);
+        vs = __ldg(reinterpret_cast<const float*>(p.v_scale) + mi);
+      }
+      uint32_t mask = __ballot_sync(0xffffffffu, issue);
+      while (mask != 0u) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const int jslot = __shfl_sync(0xffffffffu, slot, j);
+        const int jst = __shfl_sync(0xffffffffu, st, j);
+        const int jlen = __shfl_sync(0xffffffffu, len, j);
+        const float jks = __shfl_sync(0xffffffffu, ks, j);
+        const float jvs = __shfl_sync(0xffffffffu, vs, j);
+        int ok = 1;
+        if (lane == 0) {
+          const int s = tile % Cfg::kStages;
+          const uint32_t ph = (uint32_t)(tile / Cfg::kStages) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
+            ok = 0;
+          } else {
+            TileInfo ti;
+            ti.state = jst;
+            ti.len = jlen;
+            ti.block = base + j;
+            ti.ks = jks;
+            ti.vs = jvs;
+            info[s] = ti;
+            const int32_t row = (jslot * p.kv_heads + kvh) * BS;
+            uint8_t* kdst = stages + s * Cfg::kStageBytes;
+            uint8_t* vdst = kdst + Cfg::kHotBytes;
+            if (jst == 0) {
+              mbar_arrive_expect_tx(&full_bar[s], 2 * Cfg::kHotBytes);
+#pragma unroll
+              for (int hh = 0; hh < D / 64; ++hh) {
+                tma_load_2d(kdst + hh * BS * 128, &tm_hk, hh * 64, row, &full_bar[s]);
+                tma_load_2d(vdst + hh * BS * 128, &tm_hv, hh * 64, row, &full_bar[s]);
+              }
+            } else {
+              const uint32_t mbytes = (FMT == kFmtR) ? 4 * BS * 2 : 0;
+              mbar_arrive_expect_tx(&full_bar[s], 2 * BS * D + mbytes);
+              tma_load_2d(kdst, &tm_wk, 0, row, &full_bar[s]);
+              tma_load_2d(vdst, &tm_wv, 0, row, &full_bar[s]);
+              if (FMT == kFmtR) {
+                uint8_t* md = meta + s * Cfg::kMetaBytes;
+                const __half* src[4] = {reinterpret_cast<const __half*>(p.k_scale),
+                                        reinterpret_cast<const __half*>(p.k_zero),
+                                        reinterpret_cast<const __half*>(p.v_scale),
+                                        reinterpret_cast<const __half*>(p.v_zero)};
+#pragma unroll
+                for (int m = 0; m < 4; ++m)
+                  bulk_load(md + m * BS * 2, src[m] + row, BS * 2, &full_bar[s]);
+              }
+            }
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          fail = true;
+          break;
+        }
+        ++tile;
+      }
+    }
+    // one end-of-stream marker per consumer warp
+    if (lane == 0 && !fail) {
+      for (int c = 0; c < Cfg::kConsumers; ++c) {
+        const int s = tile % Cfg::kStages;
+        const uint32_t ph = (uint32_t)(tile / Cfg::kStages) & 1u;
+        if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
+          fail = true;
+          break;
+        }
+        info[s].state = -1;
+        mbar_arrive(&full_bar[s]);
+        ++tile;
+      }
+    }
+    fail = __shfl_sync(0xffffffffu, (int)fail, 0) != 0;
+    if (fail && lane == 0) atomicOr(p.err, 0x2u);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) cold += __shfl_xor_sync(0xffffffffu, cold, off);
+    if (lane == 0) misc[0] = cold;
+  }
+
+  // ------------------------------------------------------------ consumers
+  float m2[2] = {-INFINITY, -INFINITY};  // running max (log2 domain), heads 2t, 2t+1
+  float l[2] = {0.f, 0.f};               // this lane's share of the denominator
+  float acc_h[Cfg::kKS][4];              // O^T from HOT tiles   (standard d layout)
+  float acc_w[Cfg::kKS][4];              // O^T from WARM tiles  (expanded d layout)
+#pragma unroll
+  for (int i = 0; i < Cfg::kKS; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc_h[i][j] = acc_w[i][j] = 0.f;
+
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  if (warp > 0) {
+    const int cw = warp - 1;
+    uint32_t qh[Cfg::kKS][2], qw[Cfg::kKS][2];
+    float qmul[2];
+    load_query<D, QT>(p, seq, kvh, lane, qh, qw, qmul);
+
+    for (int it = cw;; it += Cfg::kConsumers) {
+      const int s = it % Cfg::kStages;
+      const uint32_t ph = (uint32_t)(it / Cfg::kStages) & 1u;
+      if (!mbar_wait(&full_bar[s], ph)) {
+        if (lane == 0) atomicOr(p.err, 0x2u);
+        break;
+      }
+      const TileInfo ti = info[s];
+      if (ti.state < 0) break;
+      const uint32_t kb = smem_u32(stages + s * Cfg::kStageBytes);
+      const uint32_t vb = kb + Cfg::kHotBytes;
+      const __half* ms = reinterpret_cast<const __half*>(meta + s * Cfg::kMetaBytes);
+      const bool hot = ti.state == 0;
+
+      // ---- logits S^T[token, head] for this block
+      float x[Cfg::kSub][4];
+#pragma unroll
+      for (int u = 0; u < Cfg::kSub; ++u) x[u][0] = x[u][1] = x[u][2] = x[u][3] = 0.f;
+      if (hot) {
+#pragma unroll
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          const int r = 16 * u + (lane & 7) + (((lane >> 3) & 1) << 3);
+          float xa[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < Cfg::kKS; ++ks) {
+            const int ch = 2 * ks + (lane >> 4);
+            const uint32_t addr =
+                kb + (ch >> 3) * (BS * 128) + r * 128 + ((((ch & 7) ^ (lane & 7))) << 4);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(addr, a0, a1, a2, a3);
+            if (ks & 1)
+              mma_16816(xa, a0, a1, a2, a3, qh[ks][0], qh[ks][1]);
+            else
+              mma_16816(x[u], a0, a1, a2, a3, qh[ks][0], qh[ks][1]);
+          }
+          x[u][0] = (x[u][0] + xa[0]) * qmul[0];
+          x[u][1] = (x[u][1] + xa[1]) * qmul[1];
+          x[u][2] = (x[u][2] + xa[2]) * qmul[0];
+          x[u][3] = (x[u][3] + xa[3]) * qmul[1];
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          const int r0 = 16 * u + g;
+          const int r1 = r0 + 8;
+          float sc0, sc1;
+          uint32_t z0, z1;
+          if (FMT == kFmtR) {
+            sc0 = __half2float(ms[r0]);
+            sc1 = __half2float(ms[r1]);
+            const __half o1024 = __float2half_rn(1024.f);
+            const __half h0 = __hadd(ms[BS + r0], o1024);
+            const __half h1 = __hadd(ms[BS + r1], o1024);
+            z0 = (uint32_t)__half_as_ushort(h0) * 0x10001u;
+            z1 = (uint32_t)__half_as_ushort(h1) * 0x10001u;
+          } else {
+            sc0 = sc1 = ti.ks;
+            z0 = z1 = 0x64806480u;  // (1152, 1152): 1024 + 128 offset of flipped int8
+          }
+          uint32_t w0[Cfg::kKS], w1[Cfg::kKS];
+#pragma unroll
+          for (int j = 0; j < D / 64; ++j) {
+            const uint32_t c = (D == 128) ? (2 * t + j) : t;
+            const uint4 v0 = lds128(kb + swz<Cfg::kWarmSwz>(r0 * D + c * 16));
+            const uint4 v1 = lds128(kb + swz<Cfg::kWarmSwz>(r1 * D + c * 16));
+            w0[4 * j + 0] = v0.x; w0[4 * j + 1] = v0.y; w0[4 * j + 2] = v0.z; w0[4 * j + 3] = v0.w;
+            w1[4 * j + 0] = v1.x; w1[4 * j + 1] = v1.y; w1[4 * j + 2] = v1.z; w1[4 * j + 3] = v1.w;
+          }
+          float xa[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < Cfg::kKS; ++ks) {
+            uint32_t c0 = w0[ks], c1 = w1[ks];
+            if (FMT == kFmtS) {
+              c0 ^= 0x80808080u;
+              c1 ^= 0x80808080u;
+            }
+            const uint32_t a0 = hsub2_u32(__byte_perm(c0, kMagic, 0x4140), z0);
+            const uint32_t a2 = hsub2_u32(__byte_perm(c0, kMagic, 0x4342), z0);
+            const uint32_t a1 = hsub2_u32(__byte_perm(c1, kMagic, 0x4140), z1);
+            const uint32_t a3 = hsub2_u32(__byte_perm(c1, kMagic, 0x4342), z1);
+            if (ks & 1)
+              mma_16816(xa, a0, a1, a2, a3, qw[ks][0], qw[ks][1]);
+            else
+              mma_16816(x[u], a0, a1, a2, a3, qw[ks][0], qw[ks][1]);
+          }
+          x[u][0] = (x[u][0] + xa[0]) * (qmul[0] * sc0);
+          x[u][1] = (x[u][1] + xa[1]) * (qmul[1] * sc0);
+          x[u][2] = (x[u][2] + xa[2]) * (qmul[0] * sc1);
+          x[u][3] = (x[u][3] + xa[3]) * (qmul[1] * sc1);
+        }
+      }
+
+      // ---- mask tokens >= len, online softmax (log2 domain)
+      float mt[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int u = 0; u < Cfg::kSub; ++u) {
+        if (16 * u + g >= ti.len) x[u][0] = x[u][1] = -INFINITY;
+        if (16 * u + g + 8 >= ti.len) x[u][2] = x[u][3] = -INFINITY;
+        mt[0] = fmaxf(mt[0], fmaxf(x[u][0], x[u][2]));
+        mt[1] = fmaxf(mt[1], fmaxf(x[u][1], x[u][3]));
+      }
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mt[0] = fmaxf(mt[0], __shfl_xor_sync(0xffffffffu, mt[0], off));
+        mt[1] = fmaxf(mt[1], __shfl_xor_sync(0xffffffffu, mt[1], off));
+      }
+      float mnew[2], alpha[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        mnew[j] = fmaxf(m2[j], mt[j]);
+        alpha[j] = ex2(m2[j] - mnew[j]);
+        m2[j] = mnew[j];
+      }
+      float pr[Cfg::kSub][4];
+      float ps[2] = {0.f, 0.f};
+#pragma unroll
+      for (int u = 0; u < Cfg::kSub; ++u) {
+        pr[u][0] = ex2(x[u][0] - mnew[0]);
+        pr[u][1] = ex2(x[u][1] - mnew[1]);
+        pr[u][2] = ex2(x[u][2] - mnew[0]);
+        pr[u][3] = ex2(x[u][3] - mnew[1]);
+        ps[0] += pr[u][0] + pr[u][2];
+        ps[1] += pr[u][1] + pr[u][3];
+      }
+      l[0] = l[0] * alpha[0] + ps[0];
+      l[1] = l[1] * alpha[1] + ps[1];
+      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+        for (int i = 0; i < Cfg::kKS; ++i) {
+          acc_h[i][0] *= alpha[0]; acc_h[i][1] *= alpha[1];
+          acc_h[i][2] *= alpha[0]; acc_h[i][3] *= alpha[1];
+          acc_w[i][0] *= alpha[0]; acc_w[i][1] *= alpha[1];
+          acc_w[i][2] *= alpha[0]; acc_w[i][3] *= alpha[1];
+        }
+      }
+      if (p.lse_blk != nullptr) {
+        float bsum[2] = {ps[0], ps[1]};
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          bsum[0] += __shfl_xor_sync(0xffffffffu, bsum[0], off);
+          bsum[1] += __shfl_xor_sync(0xffffffffu, bsum[1], off);
+        }
+        if (g == 0) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int h = 2 * t + j;
+            if (h < G)
+              p.lse_blk[((size_t)seq * Hq + (size_t)kvh * G + h) * p.max_blocks + ti.block] =
+                  (mnew[j] + lg2(bsum[j])) * kLn2;
+          }
+        }
+      }
+
+      // ---- O^T += V^T P^T
+      if (hot) {
+        uint32_t pb[Cfg::kSub][2];
+#pragma unroll
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          pb[u][0] = movmatrix_t(pack_half2(pr[u][0], pr[u][1]));
+          pb[u][1] = movmatrix_t(pack_half2(pr[u][2], pr[u][3]));
+        }
+        const int mj = lane >> 3;
+#pragma unroll
+        for (int i = 0; i < Cfg::kKS; ++i) {
+#pragma unroll
+          for (int u = 0; u < Cfg::kSub; ++u) {
+            const int r = 16 * u + (lane & 7) + ((mj >> 1) << 3);
+            const int ch = 2 * i + (mj & 1);
+            const uint32_t addr =
+                vb + (ch >> 3) * (BS * 128) + r * 128 + ((((ch & 7) ^ (lane & 7))) << 4);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_t(addr, a0, a1, a2, a3);
+            mma_16816(acc_h[i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+          }
+        }
+      } else {
+        uint32_t pb[Cfg::kSub][2];
+#pragma unroll
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          float vs0, vs1;
+          if (FMT == kFmtR) {
+            vs0 = __half2float(ms[2 * BS + 16 * u + g]);
+            vs1 = __half2float(ms[2 * BS + 16 * u + g + 8]);
+          } else {
+            vs0 = vs1 = ti.vs;
+          }
+          pb[u][0] = movmatrix_t(pack_half2(pr[u][0] * vs0, pr[u][1] * vs0));
+          pb[u][1] = movmatrix_t(pack_half2(pr[u][2] * vs1, pr[u][3] * vs1));
+        }
+#pragma unroll
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          const int r0 = 16 * u + 2 * t;
+          uint32_t z01, z23;
+          if (FMT == kFmtR) {
+            const __half o1024 = __float2half_rn(1024.f);
+            const __half* vz = ms + 3 * BS;
+            z01 = (uint32_t)__half_as_ushort(__hadd(vz[r0], o1024)) |
+                  ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 1], o1024)) << 16);
+            z23 = (uint32_t)__half_as_ushort(__hadd(vz[r0 + 8], o1024)) |
+                  ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 9], o1024)) << 16);
+          } else {
+            z01 = z23 = 0x64806480u;
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 64; ++kk) {
+            const int lo = 64 * kk + 4 * g;
+            const int hi = lo + 32;
+            uint32_t wl0 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 0) * D + lo));
+            uint32_t wl1 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 1) * D + lo));
+            uint32_t wl2 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 8) * D + lo));
+            uint32_t wl3 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 9) * D + lo));
+            uint32_t wh0 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 0) * D + hi));
+            uint32_t wh1 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 1) * D + hi));
+            uint32_t wh2 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 8) * D + hi));
+            uint32_t wh3 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 9) * D + hi));
+            if (FMT == kFmtS) {
+              wl0 ^= 0x80808080u; wl1 ^= 0x80808080u; wl2 ^= 0x80808080u; wl3 ^= 0x80808080u;
+              wh0 ^= 0x80808080u; wh1 ^= 0x80808080u; wh2 ^= 0x80808080u; wh3 ^= 0x80808080u;
+            }
+            // interleave the two tokens of each k pair byte by byte
+            const uint32_t xl[2] = {__byte_perm(wl0, wl1, 0x5140), __byte_perm(wl0, wl1, 0x7362)};
+            const uint32_t xh[2] = {__byte_perm(wh0, wh1, 0x5140), __byte_perm(wh0, wh1, 0x7362)};
+            const uint32_t yl[2] = {__byte_perm(wl2, wl3, 0x5140), __byte_perm(wl2, wl3, 0x7362)};
+            const uint32_t yh[2] = {__byte_perm(wh2, wh3, 0x5140), __byte_perm(wh2, wh3, 0x7362)};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t sel = (i & 1) ? 0x4342u : 0x4140u;
+              const uint32_t a0 = hsub2_u32(__byte_perm(xl[i >> 1], kMagic, sel), z01);
+              const uint32_t a1 = hsub2_u32(__byte_perm(xh[i >> 1], kMagic, sel), z01);
+              const uint32_t a2 = hsub2_u32(__byte_perm(yl[i >> 1], kMagic, sel), z23);
+              const uint32_t a3 = hsub2_u32(__byte_perm(yh[i >> 1], kMagic, sel), z23);
+              mma_16816(acc_w[4 * kk + i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+    }
+  }
+
+  // ------------------------------------------------------------ CTA merge
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l[0] += __shfl_xor_sync(0xffffffffu, l[0], off);
+    l[1] += __shfl_xor_sync(0xffffffffu, l[1], off);
+  }
+  __syncthreads();  // every stage is drained: the ring becomes merge scratch
+  float* sm_m = reinterpret_cast<float*>(stages);
+  float* sm_l = sm_m + Cfg::kConsumers * kMaxGroups;
+  float* sm_acc = sm_l + Cfg::kConsumers * kMaxGroups;
+  if (warp > 0) {
+    const int cw = warp - 1;
+    if (g == 0) {
+      sm_m[cw * kMaxGroups + 2 * t] = m2[0];
+      sm_m[cw * kMaxGroups + 2 * t + 1] = m2[1];
+      sm_l[cw * kMaxGroups + 2 * t] = l[0];
+      sm_l[cw * kMaxGroups + 2 * t + 1] = l[1];
+    }
+    float* a = sm_acc + (size_t)cw * kMaxGroups * D;
+#pragma unroll
+    for (int i = 0; i < Cfg::kKS; ++i) {
+      a[(2 * t) * D + 16 * i + g] = acc_h[i][0];
+      a[(2 * t + 1) * D + 16 * i + g] = acc_h[i][1];
+      a[(2 * t) * D + 16 * i + 8 + g] = acc_h[i][2];
+      a[(2 * t + 1) * D + 16 * i + 8 + g] = acc_h[i][3];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int kk = 0; kk < D / 64; ++kk) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int dlo = 64 * kk + 4 * g + i;
+        const int dhi = dlo + 32;
+        a[(2 * t) * D + dlo] += acc_w[4 * kk + i][0];
+        a[(2 * t + 1) * D + dlo] += acc_w[4 * kk + i][1];
+        a[(2 * t) * D + dhi] += acc_w[4 * kk + i][2];
+        a[(2 * t + 1) * D + dhi] += acc_w[4 * kk + i][3];
+      }
+    }
+  }
+  __syncthreads();
+  const int cold = misc[0];
+  const int nsplit = p.splits;
+  for (int e = threadIdx.x; e < G * D; e += Cfg::kThreads) {
+    const int h = e / D;
+    const int d = e - h * D;
+    float M = cold > 0 ? 0.f : -INFINITY;
+#pragma unroll
+    for (int c = 0; c < Cfg::kConsumers; ++c) M = fmaxf(M, sm_m[c * kMaxGroups + h]);
+    float L = 0.f, o = 0.f;
+#pragma unroll
+    for (int c = 0; c < Cfg::kConsumers; ++c) {
+      const float mc = sm_m[c * kMaxGroups + h];
+      if (mc != -INFINITY) {
+        const float w = ex2(mc - M);
+        L += sm_l[c * kMaxGroups + h] * w;
+        o += sm_acc[((size_t)c * kMaxGroups + h) * D + d] * w;
+      }
+    }
+    if (cold > 0) L += (float)cold * ex2(-M);
+    const float on = L > 0.f ? o / L : 0.f;
+    const float lse = L > 0.f ? (M + lg2(L)) * kLn2 : -INFINITY;
+    const size_t row = (size_t)seq * Hq + (size_t)kvh * G + h;
+    if (nsplit == 1) {
+      store_out(p.out, p.out_dtype, row * D + d, on);
+      if (d == 0) {
+        if (p.out_lse) p.out_lse[row] = lse;
+        if (p.lse_final) p.lse_final[row] = lse;
+      }
+    } else {
+      p.part_o[(row * nsplit + split) * D + d] = on;
+      if (d == 0) p.part_lse[row * nsplit + split] = lse;
+    }
+  }
+  if (nsplit == 1) return;
+
+  // ------------------------------------------------------------ split merge
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&p.counters[(size_t)seq * p.kv_heads + kvh], 1u);
+    misc[1] = (prev == (uint32_t)(nsplit - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (misc[1] == 0) return;
+  if (threadIdx.x == 0) atomicExch(&p.counters[(size_t)seq * p.kv_heads + kvh], 0u);
+  __threadfence();
+  float* wsl = reinterpret_cast<float*>(stages);          // [G][nsplit] weights
+  float* hm = wsl + kMaxGroups * kMaxSplits;              // [G] max, [G] sum
+  const size_t row0 = (size_t)seq * Hq + (size_t)kvh * G;
+  for (int e = threadIdx.x; e < G * nsplit; e += Cfg::kThreads)
+    wsl[e] = __ldcg(p.part_lse + row0 * nsplit + e);
+  __syncthreads();
+  for (int h = warp; h < G; h += Cfg::kThreads / 32) {
+    float M = -INFINITY;
+    for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, wsl[h * nsplit + sp]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float S = 0.f;
+    if (M != -INFINITY)
+      for (int sp = lane; sp < nsplit; sp += 32) S += ex2((wsl[h * nsplit + sp] - M) * kLog2e);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
+    if (lane == 0) {
+      hm[h] = M;
+      hm[kMaxGroups + h] = S;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * nsplit; e += Cfg::kThreads) {
+    const int h = e / nsplit;
+    const float M = hm[h], S = hm[kMaxGroups + h];
+    wsl[e] = (M != -INFINITY && S > 0.f) ? ex2((wsl[e] - M) * kLog2e) / S : 0.f;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += Cfg::kThreads) {
+    const int h = e / D;
+    const int d = e - h * D;
+    const size_t row = row0 + h;
+    float o = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float w = wsl[h * nsplit + sp];
+      if (w != 0.f) o += w * __ldcg(p.part_o + (row * nsplit + sp) * D + d);
+    }
+    store_out(p.out, p.out_dtype, row * D + d, o);
+    if (d == 0) {
+      const float M = hm[h], S = hm[kMaxGroups + h];
+      const float lse = (M != -INFINITY && S > 0.f) ? M + logf(S) : -INFINITY;
+      if (p.out_lse) p.out_lse[row] = lse;
+      if (p.lse_final) p.lse_final[row] = lse;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- dispatch
+template <int D, int BS, int FMT, int QT>
+static cudaError_t launch_one(const DecodeParams& p, const CUtensorMap maps[4],
+                              cudaStream_t stream) {
+  using Cfg = DecodeCfg<D, BS, FMT, QT>;
+  auto kern = decode_kernel<D, BS, FMT, QT>;
+  static bool attr_set = false;  // per-process; the attribute is per function
+  if (!attr_set) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  dim3 grid(p.splits, p.kv_heads, p.batch);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p, maps[0], maps[1], maps[2], maps[3]);
+  return cudaGetLastError();
+}
+
+template <int D, int BS, int FMT, int QT>
+static cudaError_t occupancy_one(int* ctas) {
+  using Cfg = DecodeCfg<D, BS, FMT, QT>;
+  auto kern = decode_kernel<D, BS, FMT, QT>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, kern, Cfg::kThreads, Cfg::kSmemBytes);
+}
+
+#define TKV_DISPATCH(FN, ...)                                                       \
+  do {                                                                              \
+    const int key = ((head_dim == 128) << 3) | ((block_size == 32) << 2) |          \
+                    ((format == kFmtS) << 1) | (query_dtype == kDtBF16);             \
+    switch (key) {                                                                  \
+      case 0: return FN<64, 16, kFmtR, kDtF16>(__VA_ARGS__);                        \
+      case 1: return FN<64, 16, kFmtR, kDtBF16>(__VA_ARGS__);                       \
+      case 2: return FN<64, 16, kFmtS, kDtF16>(__VA_ARGS__);                        \
+      case 3: return FN<64, 16, kFmtS, kDtBF16>(__VA_ARGS__);                       \
+      case 4: return FN<64, 32, kFmtR, kDtF16>(__VA_ARGS__);                        \
+      case 5: return FN<64, 32, kFmtR, kDtBF16>(__VA_ARGS__);                       \
+      case 6: return FN<64, 32, kFmtS, kDtF16>(__VA_ARGS__);                        \
+      case 7: return FN<64, 32, kFmtS, kDtBF16>(__VA_ARGS__);                       \
+      case 8: return FN<128, 16, kFmtR, kDtF16>(__VA_ARGS__);                       \
+      case 9: return FN<128, 16, kFmtR, kDtBF16>(__VA_ARGS__);                      \
+      case 10: return FN<128, 16, kFmtS, kDtF16>(__VA_ARGS__);                      \
+      case 11: return FN<128, 16, kFmtS, kDtBF16>(__VA_ARGS__);                     \
+      case 12: return FN<128, 32, kFmtR, kDtF16>(__VA_ARGS__);                      \
+      case 13: return FN<128, 32, kFmtR, kDtBF16>(__VA_ARGS__);                     \
+      case 14: return FN<128, 32, kFmtS, kDtF16>(__VA_ARGS__);                      \
+      default: return FN<128, 32, kFmtS, kDtBF16>(__VA_ARGS__);                     \
+    }                                                                               \
+  } while (0)
+
+cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap maps[4], int head_dim,
+                          int block_size, int format, int query_dtype, cudaStream_t stream) {
+  TKV_DISPATCH(launch_one, p, maps, stream);
+}
+
+cudaError_t decode_occupancy(int head_dim, int block_size, int format, int query_dtype,
+                             int* ctas_per_sm) {
+  TKV_DISPATCH(occupancy_one, ctas_per_sm);
+}
+
+// ---------------------------------------------------------------- merge (K2)
+// One warp per row: LSE merge of `parts` normalised partials.
+__global__ void merge_kernel(const MergeParams p) {
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= p.rows) return;
+  float M = -INFINITY;
+  for (int i = lane; i < p.parts; i += 32) M = fmaxf(M, p.part_lse[(size_t)i * p.lse_stride + row]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float S = 0.f;
+  if (M != -INFINITY)
+    for (int i = lane; i < p.parts; i += 32)
+      S += ex2((p.part_lse[(size_t)i * p.lse_stride + row] - M) * kLog2e);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
+  const bool empty = !(M != -INFINITY && S > 0.f);
+  for (int d = lane; d < p.head_dim; d += 32) {
+    float o = 0.f;
+    if (!empty) {
+      for (int i = 0; i < p.parts; ++i) {
+        const float l = p.part_lse[(size_t)i * p.lse_stride + row];
+        if (l != -INFINITY)
+          o += ex2((l - M) * kLog2e) * p.part_o[(size_t)i * p.o_stride + (size_t)row * p.head_dim + d];
+      }
+      o /= S;
+    }
+    store_out(p.out, p.out_dtype, (size_t)row * p.head_dim + d, o);
+  }
+  if (lane == 0 && p.out_lse) p.out_lse[row] = empty ? -INFINITY : M + logf(S);
+}
+
+cudaError_t launch_merge(const MergeParams& p, cudaStream_t stream) {
+  const int warps = 8;
+  const int grid = (p.rows + warps - 1) / warps;
+  merge_kernel<<<grid, warps * 32, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- scores (K3)
+// score_sums[row, b] = exp(lse_blk[row, b] - lse_final[row]) for b < nb, else 0
+// (the per-block softmax mass of tierkv_triton.py:121-145 without a second K pass).
+__global__ void scores_kernel(const ScoreParams p) {
+  const int row = blockIdx.y;
+  const int seq = row / p.num_heads;
+  int nb = p.nb_dev ? p.nb_dev[seq] : p.nb_uniform;
+  nb = max(0, min(nb, p.max_blocks));
+  const float lf = p.lse_final[row];
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < p.max_blocks;
+       b += gridDim.x * blockDim.x) {
+    float v = 0.f;
+    if (b < nb && lf != -INFINITY) {
+      const float lb = p.lse_blk[(size_t)row * p.max_blocks + b];
+      v = (lb == -INFINITY) ? 0.f : ex2((lb - lf) * kLog2e);
+    }
+    p.score_sums[(size_t)row * p.max_blocks + b] = v;
+  }
+}
+
+cudaError_t launch_scores(const ScoreParams& p, cudaStream_t stream) {
+  const int threads = 256;
+  int gx = (p.max_blocks + threads - 1) / threads;
+  gx = max(1, min(gx, 64));
+  dim3 grid(gx, p.rows);
+  scores_kernel<<<grid, threads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- block scores (a8)
+__global__ void block_scores_kernel(const BlockScoreParams p) {
+  const int seq = blockIdx.y;
+  int nb = p.nb_dev ? p.nb_dev[seq] : p.nb_uniform;
+  nb = max(0, min(nb, p.max_blocks));
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < p.max_blocks;
+       b += gridDim.x * blockDim.x) {
+    float v = 0.f;
+    if (b < nb) {
+      float s = 0.f;
+      for (int h = 0; h < p.num_heads; ++h)
+        s += p.score_sums[((size_t)seq * p.num_heads + h) * p.max_blocks + b];
+      const int len = max(p.lengths[(size_t)seq * p.table_stride + b], 1);
+      v = (s / (float)p.num_heads) / (float)len;
+    }
+    p.block_scores[(size_t)seq * p.max_blocks + b] = v;
+  }
+}
+
+cudaError_t launch_block_scores(const BlockScoreParams& p, cudaStream_t stream) {
+  const int threads = 256;
+  int gx = (p.max_blocks + threads - 1) / threads;
+  gx = max(1, min(gx, 64));
+  dim3 grid(gx, p.batch);
+  block_scores_kernel<<<grid, threads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace tkv

@@ -1,0 +1,124 @@
+// tkv_internal.h -- parameter blocks shared by the host launchers and the
+// sm_100a kernels of the tiered decode path (not part of the public ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tkv {
+
+constexpr int kFmtR = 0;
+constexpr int kFmtS = 1;
+constexpr int kDtF16 = 0;
+constexpr int kDtBF16 = 1;
+constexpr int kDtF32 = 2;
+constexpr int kMaxGroups = 8;      // query heads per KV head handled by one CTA (mma N = 8)
+constexpr int kMaxSplits = 512;    // split-KV partitions per (sequence, kv head)
+constexpr float kLn2 = 0.693147180559945309f;
+constexpr float kLog2e = 1.442695040888963387f;
+
+// Everything one decode launch needs besides the four TMA descriptors.
+struct DecodeParams {
+  const void* query;          // [batch, num_heads, D]
+  const int32_t* table;       // [batch, table_stride]
+  const int32_t* states;
+  const int32_t* lengths;
+  const int32_t* nb_dev;      // optional [batch]
+  const void* k_scale;        // Format R: fp16 [warm_slots*kv_heads*bs]; Format S: fp32 [warm_slots*kv_heads]
+  const void* k_zero;
+  const void* v_scale;
+  const void* v_zero;
+  void* out;                  // [batch, num_heads, D] out dtype
+  float* out_lse;             // optional [batch, num_heads]
+  float* part_o;              // [batch*num_heads, splits, D] (splits > 1)
+  float* part_lse;            // [batch*num_heads, splits]
+  uint32_t* counters;         // [batch*kv_heads] self-resetting split tickets
+  float* lse_blk;             // optional [batch*num_heads, max_blocks]: per-block LSE
+  float* lse_final;           // optional [batch*num_heads]: final LSE for the score pass
+  uint32_t* err;              // device error bits
+  int64_t table_stride;
+  int64_t hot_slots;
+  int64_t warm_slots;
+  int32_t nb_uniform;
+  int32_t batch;
+  int32_t kv_heads;
+  int32_t num_heads;
+  int32_t groups;
+  int32_t max_blocks;
+  int32_t splits;
+  int32_t out_dtype;
+  float scale_log2;           // scaling * log2(e)
+};
+
+struct MergeParams {
+  const float* part_o;        // part i at part_o + i * o_stride: [rows, D]
+  const float* part_lse;      // part i at part_lse + i * lse_stride: [rows]
+  int64_t o_stride;
+  int64_t lse_stride;
+  void* out;
+  float* out_lse;
+  int32_t parts;
+  int32_t rows;
+  int32_t head_dim;
+  int32_t out_dtype;
+};
+
+struct ScoreParams {
+  const float* lse_blk;       // [batch*num_heads, max_blocks]
+  const float* lse_final;     // [batch*num_heads]
+  const int32_t* nb_dev;
+  float* score_sums;          // [batch*num_heads, max_blocks]
+  int32_t nb_uniform;
+  int32_t num_heads;
+  int32_t max_blocks;
+  int32_t rows;               // batch * num_heads
+};
+
+struct BlockScoreParams {
+  const float* score_sums;    // [batch, num_heads, max_blocks]
+  const int32_t* lengths;     // [batch, table_stride]
+  const int32_t* nb_dev;
+  float* block_scores;        // [batch, max_blocks]
+  int64_t table_stride;
+  int32_t nb_uniform;
+  int32_t batch;
+  int32_t num_heads;
+  int32_t max_blocks;
+};
+
+struct DemoteParams {
+  const void* hot_k;
+  const void* hot_v;
+  void* warm_k;
+  void* warm_v;
+  void* k_scale;
+  void* k_zero;
+  void* v_scale;
+  void* v_zero;
+  const int32_t* src;         // HOT slots (demote) / WARM slots (promote)
+  const int32_t* dst;         // WARM slots (demote) / HOT slots (promote)
+  const int32_t* lengths;
+  int64_t hot_slots;
+  int64_t warm_slots;
+  int32_t count;
+  int32_t kv_heads;
+  int32_t block_size;
+  int32_t head_dim;
+  int32_t clear_tail;
+};
+
+// Host launchers (defined in the .cu files, called by tkv_api.cu).
+cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap maps[4], int head_dim,
+                          int block_size, int format, int query_dtype, cudaStream_t stream);
+cudaError_t decode_occupancy(int head_dim, int block_size, int format, int query_dtype,
+                             int* ctas_per_sm);
+cudaError_t launch_merge(const MergeParams& p, cudaStream_t stream);
+cudaError_t launch_scores(const ScoreParams& p, cudaStream_t stream);
+cudaError_t launch_block_scores(const BlockScoreParams& p, cudaStream_t stream);
+cudaError_t launch_quantize_rows(const void* x, int64_t rows, int dim, void* codes, void* scale,
+                                 void* zero, cudaStream_t stream);
+cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream);
+cudaError_t launch_promote(const DemoteParams& p, cudaStream_t stream);
+
+}  // namespace tkv

@@ -1,0 +1,234 @@
+"""GPU parity of the sm_100a decode-attention path against the oracle.
+
+Tolerance (stated by the benchmark's north star): attention outputs within
+2e-3 absolute / 1e-2 relative of an fp32-or-better evaluation; here the
+oracle runs in float64.  Golden fixtures (outputs of the reference's own
+``_eager_reference_decode``) are checked at the same tolerance.
+"""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import tierkv_oracle as orc  # noqa: E402
+from tierkv_cases import make_case, oracle_decode, to_device  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from paged_tierkv_b200 import _native
+    _native.load(build_if_missing=True)
+
+
+def _run(case, **kw):
+    from paged_tierkv_b200 import ops
+    d = to_device(case)
+    nb = kw.pop("num_blocks", d["num_blocks"])
+    out, scores, lse = ops.decode_attention(
+        d["query"], d["block_table"], d["block_states"], d["block_lengths"], d["pools"], nb,
+        case["groups"], case["scaling"], **kw)
+    torch.cuda.synchronize()
+    return out, scores, lse
+
+
+def _close(out, ref, atol=ATOL, rtol=RTOL):
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got, ref, atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("block_size", [16, 32])
+@pytest.mark.parametrize("fmt", ["R", "S"])
+@pytest.mark.parametrize("groups", [1, 4, 8])
+def test_mixed_tiers_match_oracle(head_dim, block_size, fmt, groups):
+    kv = 2 if groups == 8 else 4
+    case = make_case(seed=head_dim + block_size + groups, batch=2, q_heads=kv * groups, kv_heads=kv,
+                     head_dim=head_dim, block_size=block_size, num_blocks=21, fmt=fmt)
+    ref, ref_lse, ref_scores = oracle_decode(case)
+    out, scores, lse = _run(case, return_scores=True, return_lse=True)
+    _close(out, ref)
+    np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=1e-3, rtol=1e-4)
+    np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-4, rtol=1e-3)
+
+
+@pytest.mark.parametrize("num_blocks", [1, 2, 4, 5, 127, 128, 129])
+@pytest.mark.parametrize("splits", [0, 1, 3])
+def test_block_counts_and_splits(num_blocks, splits):
+    case = make_case(seed=num_blocks * 7 + splits, batch=1, q_heads=32, kv_heads=8, head_dim=128,
+                     block_size=16, num_blocks=num_blocks)
+    ref, _, ref_scores = oracle_decode(case)
+    out, scores, _ = _run(case, num_splits=min(splits, num_blocks), return_scores=True)
+    _close(out, ref)
+    np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-4, rtol=1e-3)
+
+
+def test_all_cold_and_empty():
+    case = make_case(seed=5, batch=3, q_heads=8, kv_heads=2, head_dim=64, num_blocks=6,
+                     states=[2] * 6, nb_per_seq=[6, 0, 3])
+    ref, ref_lse, ref_scores = oracle_decode(case)
+    out, scores, lse = _run(case, return_scores=True, return_lse=True)
+    _close(out, ref)  # values are 0 (all-cold) -> mean of zero vectors
+    assert np.all(out[1].float().cpu().numpy() == 0)
+    assert np.isneginf(lse[1].cpu().numpy()).all()
+    np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-5)
+
+
+def test_zero_length_and_partial_blocks():
+    lengths = [16, 0, 7, 16, 1, 0, 16, 9]
+    states = [0, 0, 1, 2, 1, 1, 0, 2]
+    case = make_case(seed=9, batch=1, q_heads=16, kv_heads=4, head_dim=128, num_blocks=8,
+                     states=states, lengths=lengths)
+    ref, _, ref_scores = oracle_decode(case)
+    out, scores, _ = _run(case, return_scores=True)
+    _close(out, ref)
+    np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-4, rtol=1e-3)
+
+
+def test_per_sequence_block_counts():
+    case = make_case(seed=11, batch=4, q_heads=32, kv_heads=8, head_dim=128, num_blocks=40,
+                     nb_per_seq=[40, 1, 17, 33], max_blocks=48)
+    ref, _, _ = oracle_decode(case)
+    out, _, _ = _run(case)
+    _close(out, ref)
+
+
+def test_bf16_query_and_outputs():
+    from paged_tierkv_b200 import ops
+    case = make_case(seed=13, batch=2, q_heads=32, kv_heads=8, head_dim=128, num_blocks=30)
+    case["query"] = (case["query"].astype(np.float32) * 3.0).astype(np.float16)
+    ref, _, _ = oracle_decode(case)
+    d = to_device(case)
+    q = d["query"].to(torch.bfloat16)
+    # the oracle sees the bf16-rounded query
+    case_b = dict(case, query=q.float().cpu().numpy())
+    ref_b, _, _ = oracle_decode(case_b)
+    out, _, _ = ops.decode_attention(q, d["block_table"], d["block_states"], d["block_lengths"],
+                                     d["pools"], d["num_blocks"], case["groups"], case["scaling"])
+    torch.cuda.synchronize()
+    assert out.dtype == torch.bfloat16
+    _close(out, ref_b, atol=4e-3, rtol=1.6e-2)  # + bf16 output rounding (2^-9)
+    out32, _, _ = ops.decode_attention(d["query"], d["block_table"], d["block_states"],
+                                       d["block_lengths"], d["pools"], d["num_blocks"],
+                                       case["groups"], case["scaling"], out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _close(out32, ref, atol=1e-3, rtol=5e-3)
+
+
+def test_large_magnitudes():
+    case = make_case(seed=17, batch=1, q_heads=32, kv_heads=8, head_dim=128, num_blocks=64,
+                     value_scale=8.0)
+    ref, _, _ = oracle_decode(case)
+    out, _, _ = _run(case)
+    _close(out, ref, atol=ATOL * 8, rtol=RTOL)
+
+
+def test_out_of_pool_slot_reads_as_zero_and_is_reported():
+    from paged_tierkv_b200 import ops
+    case = make_case(seed=19, batch=1, q_heads=8, kv_heads=2, head_dim=64, num_blocks=6,
+                     states=[0, 1, 0, 0, 1, 0])
+    bad = case["block_table"].copy()
+    bad[0, 2] = case["hot_k"].shape[0] + 100  # HOT slot past the pool
+    ref_case = dict(case, block_states=case["block_states"].copy())
+    ref_case["block_states"][0, 2] = orc.COLD_STATE  # reads as zeros with valid tokens
+    ref, _, _ = oracle_decode(ref_case)
+    ops.read_device_errors()  # clear
+    out, _, _ = _run(dict(case, block_table=bad))
+    _close(out, ref)
+    assert ops.read_device_errors() & 0x1
+
+
+DECODE_CASES = sorted(os.path.basename(p)[7:-4] for p in glob.glob(os.path.join(GOLDEN, "decode_*.npz")))
+
+
+@pytest.mark.parametrize("case_name", DECODE_CASES)
+def test_reference_golden_through_shim(case_name):
+    """The reference-signature shim on pools built by the reference's own code."""
+    from paged_tierkv_b200 import tierkv_triton as shim
+    g = np.load(os.path.join(GOLDEN, f"decode_{case_name}.npz"))
+    if g["hot_k_pool"].shape[-1] not in (64, 128):
+        with pytest.raises(ValueError):
+            _shim_call(shim, g, False)
+        pytest.skip("head_dim outside {64, 128} is rejected with ValueError")
+    out, scores = _shim_call(shim, g, True)
+    torch.cuda.synchronize()
+    hq, d = g["query"].shape
+    assert tuple(out.shape) == (1, 1, hq, d)
+    assert scores.shape == (hq, g["block_table"].shape[0])
+    ref = g["out"].astype(np.float32)
+    _close(out[0, 0], ref)
+    nb = int(g["num_blocks"])
+    s = scores.cpu().numpy()
+    np.testing.assert_allclose(s[:, :nb].sum(-1), 1.0, atol=1e-4)
+    assert np.all(s[:, nb:] == 0)
+    out2, none = _shim_call(shim, g, False)
+    assert none is None
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out2.cpu().numpy(), out.cpu().numpy())
+
+
+def _shim_call(shim, g, return_scores):
+    c = lambda k: torch.from_numpy(np.ascontiguousarray(g[k])).cuda()  # noqa: E731
+    q = c("query")[None, :, None, :]
+    return shim.tierkv_decode_attention(
+        q, c("block_table"), c("block_states"), c("block_lengths"), c("hot_k_pool"), c("hot_v_pool"),
+        c("warm_k_pool"), c("warm_v_pool"), c("k_scale"), c("k_zero"), c("v_scale"), c("v_zero"),
+        num_blocks=int(g["num_blocks"]), num_key_value_groups=int(g["groups"]),
+        scaling=float(g["scaling"]), return_scores=return_scores)
+
+
+def test_shim_validation_errors_match_reference():
+    from paged_tierkv_b200 import tierkv_triton as shim
+    g = np.load(os.path.join(GOLDEN, "decode_pres_mixed.npz"))
+    c = lambda k: torch.from_numpy(np.ascontiguousarray(g[k])).cuda()  # noqa: E731
+    args = [c("block_table"), c("block_states"), c("block_lengths"), c("hot_k_pool"), c("hot_v_pool"),
+            c("warm_k_pool"), c("warm_v_pool"), c("k_scale"), c("k_zero"), c("v_scale"), c("v_zero")]
+    q = c("query")[None, :, None, :]
+    with pytest.raises(ValueError):
+        shim.tierkv_decode_attention(q[0], *args, num_blocks=5, num_key_value_groups=2, scaling=0.1)
+    with pytest.raises(ValueError):
+        shim.tierkv_decode_attention(q.expand(2, -1, -1, -1), *args, num_blocks=5,
+                                     num_key_value_groups=2, scaling=0.1)
+    with pytest.raises(ValueError):
+        shim.tierkv_decode_attention(q.expand(1, -1, 2, -1), *args, num_blocks=5,
+                                     num_key_value_groups=2, scaling=0.1)
+    with pytest.raises(ValueError):
+        shim.tierkv_decode_attention(q.cpu(), *args, num_blocks=5, num_key_value_groups=2, scaling=0.1)
+    with pytest.raises(ValueError):
+        shim.tierkv_decode_attention(q.float(), *args, num_blocks=5, num_key_value_groups=2, scaling=0.1)
+    with pytest.raises(ValueError):
+        shim.tierkv_decode_attention(q, *args, num_blocks=0, num_key_value_groups=2, scaling=0.1)
+    with pytest.raises(ValueError):
+        shim.tierkv_decode_attention(q, *args, num_blocks=999, num_key_value_groups=2, scaling=0.1)
+
+
+def test_c1_config_against_reference_golden():
+    """Benchmark configuration 1 (B=4, 32/8 heads, D=128, 2048 tokens) vs the
+    reference's own eager output; WARM blocks quantized by the GPU kernel."""
+    from c1_inputs import c1_inputs
+    from paged_tierkv_b200 import ops
+    g = np.load(os.path.join(GOLDEN, "c1_out.npz"))
+    inp = c1_inputs(seed=0)
+    dev = "cuda"
+    wk, ks, kz = ops.quantize_fp16_to_int8(torch.from_numpy(inp["warm_src_k"]).to(dev))
+    wv, vs, vz = ops.quantize_fp16_to_int8(torch.from_numpy(inp["warm_src_v"]).to(dev))
+    pools = ops.TieredPools(torch.from_numpy(inp["hot_k"]).to(dev), torch.from_numpy(inp["hot_v"]).to(dev),
+                            wk, wv, ks, kz, vs, vz)
+    t = lambda k: torch.from_numpy(inp[k]).to(dev)  # noqa: E731
+    for splits in (0, 1, 4):
+        out, _, _ = ops.decode_attention(t("query"), t("block_table"), t("block_states"),
+                                         t("block_lengths"), pools, inp["num_blocks"],
+                                         inp["q_heads"] // inp["kv_heads"], inp["scaling"],
+                                         num_splits=splits)
+        torch.cuda.synchronize()
+        _close(out, g["out"].astype(np.float32))
