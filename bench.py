@@ -1,0 +1,401 @@
+"""Benchmark of the tiered paged decode-attention path (one JSON line on rank 0).
+
+Workload (benchmark configuration 5, Llama-3-8B attention shape, 32k context):
+batch 32 sequences x 32768 tokens, 32 query / 8 KV heads, head_dim 128, block
+16, HOT fraction 0.25 with the rest split 2:1 WARM:COLD (Format R, the
+reference's uint8 layout).  One step = one decode-attention call for the
+whole batch.  Inputs are seeded synthetic N(0, 1) data; the pools (2+ GB) are
+far larger than the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--hot-frac H] [--block-size BS] [--sweep]
+
+For N > 1 the script runs under torchrun: each rank owns its own batch of 32
+sequences (data-parallel, no collective on the data path; weak scaling) and
+`value` is the bytes of all ranks over the slowest rank's device time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "tiered decode-attn HBM GB/s (Llama-3-8B attention shape, 32k ctx)"
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--hot-frac", type=float, default=0.25)
+    ap.add_argument("--block-size", type=int, default=16)
+    ap.add_argument("--sweep", action="store_true",
+                    help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 10.0:  # wait for the first sample
+            time.sleep(0.05)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- helpers
+def hbm_peak():
+    try:
+        with open(PEAKS) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(key: str):
+    try:
+        with open(TRAFFIC) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+def workload_key(a) -> str:
+    return f"c5_b{a.batch}_ctx{a.ctx}_h{a.hot_frac:g}_bs{a.block_size}"
+
+
+def build_workload(a, seed, device):
+    from paged_tierkv_b200 import workloads
+    return workloads.make_workload(batch=a.batch, q_heads=32, kv_heads=8, head_dim=128,
+                                   block_size=a.block_size, ctx_tokens=a.ctx,
+                                   hot_frac=a.hot_frac, seed=seed, device=device)
+
+
+def time_device(wl, steps, warmup, dist_on):
+    """Device time of `steps` decode calls (events on the launching stream)."""
+    from paged_tierkv_b200 import workloads
+    stream = torch.cuda.current_stream()
+    out = torch.empty(wl.query.shape, dtype=torch.float16, device=wl.query.device)
+    for _ in range(warmup):
+        workloads.decode(wl, out=out)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    total0 = torch.cuda.Event(enable_timing=True)
+    total1 = torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    total0.record(stream)
+    for i in range(steps):
+        starts[i].record(stream)
+        workloads.decode(wl, out=out)
+        ends[i].record(stream)
+    total1.record(stream)
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    total_ms = total0.elapsed_time(total1)
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    return total_ms, per, out
+
+
+def time_e2e(wl, steps, warmup):
+    """Same metric through the public API with host buffers: per step the query
+    and the three block tables go host->device from pinned memory and the output
+    comes back device->host, all inside the timed region."""
+    from paged_tierkv_b200 import ops
+    stream = torch.cuda.current_stream()
+    h_q = wl.query.cpu().pin_memory()
+    h_t = wl.block_table.cpu().pin_memory()
+    h_s = wl.block_states.cpu().pin_memory()
+    h_l = wl.block_lengths.cpu().pin_memory()
+    h_out = torch.empty(wl.query.shape, dtype=torch.float16).pin_memory()
+    d_q, d_t, d_s, d_l = (torch.empty_like(x, device=wl.query.device) for x in (h_q, h_t, h_s, h_l))
+    d_out = torch.empty(wl.query.shape, dtype=torch.float16, device=wl.query.device)
+
+    def step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_t.copy_(h_t, non_blocking=True)
+        d_s.copy_(h_s, non_blocking=True)
+        d_l.copy_(h_l, non_blocking=True)
+        ops.decode_attention(d_q, d_t, d_s, d_l, wl.pools, wl.num_blocks, wl.groups, wl.scaling,
+                             out=d_out)
+        h_out.copy_(d_out, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    h2d = sum(x.numel() * x.element_size() for x in (h_q, h_t, h_s, h_l))
+    d2h = h_out.numel() * h_out.element_size()
+    return e0.elapsed_time(e1), h2d, d2h
+
+
+def host_sample(wl, seqs):
+    """Host copies of the pools/tables of the first `seqs` sequences (slots remapped)."""
+    table = wl.block_table[:seqs].cpu().numpy()
+    states = wl.block_states[:seqs].cpu().numpy()
+    lengths = wl.block_lengths[:seqs].cpu().numpy()
+    hot_ids = np.unique(table[states == 0])
+    warm_ids = np.unique(table[states == 1])
+    remap = table.copy()
+    hmap = {int(s): i for i, s in enumerate(hot_ids)}
+    wmap = {int(s): i for i, s in enumerate(warm_ids)}
+    for idx in zip(*np.nonzero(states == 0)):
+        remap[idx] = hmap[int(table[idx])]
+    for idx in zip(*np.nonzero(states == 1)):
+        remap[idx] = wmap[int(table[idx])]
+    p = wl.pools
+    hi = torch.from_numpy(hot_ids.astype(np.int64)).to(p.device)
+    wi = torch.from_numpy(warm_ids.astype(np.int64)).to(p.device)
+    g = lambda t, i: t.index_select(0, i).cpu().numpy()  # noqa: E731
+    return dict(query=wl.query[:seqs].cpu().numpy(), table=remap, states=states, lengths=lengths,
+                hot_k=g(p.hot_k, hi), hot_v=g(p.hot_v, hi), warm_k=g(p.warm_k, wi),
+                warm_v=g(p.warm_v, wi), k_scale=g(p.k_scale, wi), k_zero=g(p.k_zero, wi),
+                v_scale=g(p.v_scale, wi), v_zero=g(p.v_zero, wi))
+
+
+def cpu_oracle_rate(wl, seconds, seqs=1):
+    """GB/s of the CPU restatement of the reference path on a bounded sample."""
+    from oracle import tierkv_oracle as orc
+    s = host_sample(wl, seqs)
+    bytes_per_call = wl.algorithmic_bytes() * seqs / wl.batch
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        orc.decode_attention(s["query"], s["table"], s["states"], s["lengths"], wl.num_blocks,
+                             s["hot_k"], s["hot_v"], s["warm_k"], s["warm_v"], s["k_scale"],
+                             s["k_zero"], s["v_scale"], s["v_zero"], wl.groups, wl.scaling,
+                             dtype=np.float32)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and reps >= 2:
+            break
+    return bytes_per_call * reps / el / 1e9, el / reps, reps
+
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        return max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# --------------------------------------------------------------------------- arms
+def run_reference(a, rank):
+    """The reference arm: the CPU restatement of the reference's PyTorch tiered
+    path (the reference itself is Python and cannot travel), on host cores."""
+    if rank != 0:
+        return
+    wl = build_workload(a, seed=1234, device="cuda")
+    from oracle import tierkv_oracle as orc
+    s = host_sample(wl, 1)
+    bytes_per_step = wl.algorithmic_bytes() / wl.batch
+
+    def once():
+        orc.decode_attention(s["query"], s["table"], s["states"], s["lengths"], wl.num_blocks,
+                             s["hot_k"], s["hot_v"], s["warm_k"], s["warm_v"], s["k_scale"],
+                             s["k_zero"], s["v_scale"], s["v_zero"], wl.groups, wl.scaling,
+                             dtype=np.float32)
+    for _ in range(a.warmup):
+        once()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        once()
+    el = time.perf_counter() - t0
+    gbs = bytes_per_step * a.steps / el / 1e9
+    cores = blas_threads()
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(el / a.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded N(0,1) K/V/query)", "impl": "reference",
+        "config": {"workload": workload_key(a), **wl.info, "sample": "1 sequence per step"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": "1 of 32 sequences per step, all 8 kv heads, full 32k context"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(a, rank, world, dist_on, device):
+    from paged_tierkv_b200 import _native, ops
+    _native.load(build_if_missing=True)
+    wl = build_workload(a, seed=1234 + rank, device=device)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    total_ms, per, _ = time_device(wl, a.steps, a.warmup, dist_on)
+    clocks = sampler.stop() if sampler else None
+    e2e_ms, h2d, d2h = time_e2e(wl, a.steps, a.warmup)
+    splits = ops.plan_splits(wl.pools, wl.batch, wl.query.shape[1], wl.groups, wl.num_blocks,
+                             wl.num_blocks)
+    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    total_ms, e2e_ms = float(t[0]), float(t[1])
+    bytes_step = wl.algorithmic_bytes()
+    all_bytes = bytes_step * world * a.steps
+    value = all_bytes / (total_ms * 1e-3) / 1e9
+    e2e_val = all_bytes / (e2e_ms * 1e-3) / 1e9
+    sweep = None
+    if a.sweep:
+        sweep = []
+        for bs in (16, 32):
+            for h in (1.0, 0.5, 0.25, 0.1):
+                a2 = argparse.Namespace(**{**vars(a), "hot_frac": h, "block_size": bs})
+                w2 = build_workload(a2, seed=99 + rank, device=device)
+                tm, pl, _ = time_device(w2, a.steps, a.warmup, dist_on)
+                b2 = w2.algorithmic_bytes()
+                gbs = b2 / (statistics.mean(pl) * 1e-3) / 1e9
+                sweep.append({"block_size": bs, "hot_frac": h, "bytes_per_call": b2,
+                              "ms_per_call": round(statistics.mean(pl), 4), "GBps": round(gbs, 1)})
+                del w2
+                torch.cuda.empty_cache()
+    if rank != 0:
+        return
+    peak, peak_kind = hbm_peak()
+    kernel_ms = statistics.mean(per)
+    achieved = bytes_step / (kernel_ms * 1e-3) / 1e9
+    cpu = None
+    if not a.no_cpu_baseline:
+        gbs, sec_per, reps = cpu_oracle_rate(wl, a.cpu_seconds)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": blas_threads(), "kind": "port",
+               "sample": f"1 of {wl.batch} sequences (8 kv heads, full context), {reps} reps, "
+                         f"{sec_per:.2f} s each"}
+    tr = ncu_traffic(workload_key(a))
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(total_ms / a.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) K/V/query; WARM blocks demoted on device)",
+        "config": {"workload": workload_key(a), **wl.info, "warm_format": "R (uint8 + fp16 scale/zero)",
+                   "parallelism": f"dp{world} (independent batches, no collective)",
+                   "splits": splits, "l2": "inputs >> 126 MB L2; no flush needed",
+                   "bytes_per_step_per_gpu": bytes_step},
+        "tokens_per_s": round(wl.batch * world / (32 * total_ms / a.steps * 1e-3), 1),
+        "tokens_per_s_note": "attention-only decode tokens/s for a 32-layer model (batch / (32 x step))",
+        "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": a.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": tr, "kernel": "tkv::decode_kernel<128,16,R,f16>",
+                     "kernel_ms": round(kernel_ms, 4)},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+    }
+    if sweep is not None:
+        line["sweep"] = sweep
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1 and a.impl == "ours"
+    if a.impl == "reference" and rank != 0:
+        return  # the reference arm runs on rank 0's host cores only
+    if dist_on:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    a.gpus = world
+    try:
+        if a.impl == "reference":
+            run_reference(a, rank)
+        else:
+            run_ours(a, rank, world, dist_on, device)
+    finally:
+        if dist_on:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

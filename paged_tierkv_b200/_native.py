@@ -91,7 +91,8 @@ _LIB = None
 
 
 def library_path() -> str:
-    return _build.lib_path()
+    """The in-tree build, or the file named by TIERKV_B200_LIBRARY."""
+    return os.environ.get("TIERKV_B200_LIBRARY") or _build.lib_path()
 
 
 def load(build_if_missing: bool = False) -> ctypes.CDLL:

@@ -42,9 +42,12 @@ def _stale(out: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(verbose_ptxas: bool = False, force: bool = False) -> str:
+def build(verbose_ptxas: bool = False, force: bool = False, defines: tuple[str, ...] = (),
+          out: str | None = None, objdir: str | None = None) -> str:
+    """Compile and link; `defines` (e.g. "TKV_STAGES_8K=12") select a variant,
+    `out` / `objdir` place it elsewhere than the in-tree library."""
     os.makedirs(LIBDIR, exist_ok=True)
-    objdir = os.path.join(HERE, "_build")
+    objdir = objdir or os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers.append(os.path.join(ROOT, "include", "tierkv_b200.h"))
@@ -53,6 +56,7 @@ def build(verbose_ptxas: bool = False, force: bool = False) -> str:
               "-I", os.path.join(ROOT, "include"), "-I", CSRC, *ARCH]
     if verbose_ptxas:
         common += ["-Xptxas", "-v"]
+    common += [f"-D{d}" for d in defines]
     objs = []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
@@ -61,7 +65,7 @@ def build(verbose_ptxas: bool = False, force: bool = False) -> str:
         if force or verbose_ptxas or _stale(o, [s] + headers):
             cmd = [nvcc, *common, "-c", s, "-o", o]
             subprocess.run(cmd, check=True)
-    out = lib_path()
+    out = out or lib_path()
     if force or _stale(out, objs):
         tmp = out + ".tmp"
         cmd = [nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-cudart", "static", *objs, "-o", tmp]

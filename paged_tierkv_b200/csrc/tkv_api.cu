@@ -98,6 +98,22 @@ int32_t check_pools(const tkv_pools* pl, bool need_meta) {
   return TKV_OK;
 }
 
+// 3-D tiled map over an fp16 HOT pool: dims {64, rows, head_dim/64} with
+// strides {head_dim*2, 128} bytes, box {64, bs, head_dim/64}.  One box is a
+// whole [bs, head_dim] tile landing as [head_dim/64][bs][64] in shared memory.
+bool encode_hot_map_3d(CUtensorMap* map, void* base, int64_t rows, int head_dim, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(head_dim / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)(head_dim / 64)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 struct Plan {
   int splits = 1;
   size_t off_err = 0, off_counters = 0, off_part_o = 0, off_part_lse = 0, off_lse_final = 0,
@@ -217,8 +233,14 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   const int bs = pools->block_size, d = pools->head_dim, hkv = pools->kv_heads;
   const int64_t hot_rows = pools->hot_slots * hkv * bs;
   const int64_t warm_rows = pools->warm_slots * hkv * bs;
-  if (!encode_pool_map(&maps[0], pools->hot_k, true, hot_rows, d, 64, bs) ||
-      !encode_pool_map(&maps[1], pools->hot_v, true, hot_rows, d, 64, bs) ||
+#if TKV_HOT_3D
+  const bool hot_ok = encode_hot_map_3d(&maps[0], pools->hot_k, hot_rows, d, bs) &&
+                      encode_hot_map_3d(&maps[1], pools->hot_v, hot_rows, d, bs);
+#else
+  const bool hot_ok = encode_pool_map(&maps[0], pools->hot_k, true, hot_rows, d, 64, bs) &&
+                      encode_pool_map(&maps[1], pools->hot_v, true, hot_rows, d, 64, bs);
+#endif
+  if (!hot_ok ||
       !encode_pool_map(&maps[2], pools->warm_k, false, warm_rows, d, d, bs) ||
       !encode_pool_map(&maps[3], pools->warm_v, false, warm_rows, d, d, bs))
     return TKV_ERR_CUDA;

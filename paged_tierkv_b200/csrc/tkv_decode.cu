@@ -37,13 +37,29 @@ struct TileInfo {
   int32_t pad[3];
 };
 
+// Pipeline shape: consumer warps per CTA, ring depth for stages of <= 8 KB and
+// of 16 KB, and the CTAs per SM the register budget is sized for.
+#ifndef TKV_CONSUMERS
+#define TKV_CONSUMERS 4
+#endif
+#ifndef TKV_STAGES_8K
+#define TKV_STAGES_8K 12
+#endif
+#ifndef TKV_STAGES_16K
+#define TKV_STAGES_16K 4
+#endif
+#ifndef TKV_MIN_CTAS
+#define TKV_MIN_CTAS 2
+#endif
+
 template <int D, int BS, int FMT, int QT>
 struct DecodeCfg {
-  static constexpr int kConsumers = 4;
+  static constexpr int kConsumers = TKV_CONSUMERS;
   static constexpr int kThreads = 32 * (kConsumers + 1);
   static constexpr int kHotBytes = BS * D * 2;            // one K (or V) HOT tile
   static constexpr int kStageBytes = 2 * kHotBytes;       // K + V, multiple of 1024
-  static constexpr int kStages = (kStageBytes <= 8192) ? 8 : 4;
+  static constexpr int kStages = (kStageBytes <= 8192) ? TKV_STAGES_8K : TKV_STAGES_16K;
+  static_assert(kStages % kConsumers == 0, "each consumer must own a fixed subset of stages");
   static constexpr int kMetaBytes = (FMT == kFmtR) ? 4 * BS * 2 : 16;
   static constexpr int kKS = D / 16;                      // 16-wide steps over head_dim
   static constexpr int kSub = BS / 16;                    // 16-token sub-tiles per block
@@ -135,7 +151,7 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, int seq, int k
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0
 
 template <int D, int BS, int FMT, int QT>
-__global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, 2)
+__global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_CTAS)
     decode_kernel(const __grid_constant__ DecodeParams p,
                   const __grid_constant__ CUtensorMap tm_hk,
                   const __grid_constant__ CUtensorMap tm_hv,
@@ -231,39 +247,46 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, 2)
         ks = __ldg(reinterpret_cast<const float*>(p.k_scale) + mi);
         vs = __ldg(reinterpret_cast<const float*>(p.v_scale) + mi);
       }
-      uint32_t mask = __ballot_sync(0xffffffffu, issue);
-      while (mask != 0u) {
-        const int j = __ffs(mask) - 1;
-        mask &= mask - 1;
-        const int jslot = __shfl_sync(0xffffffffu, slot, j);
-        const int jst = __shfl_sync(0xffffffffu, st, j);
-        const int jlen = __shfl_sync(0xffffffffu, len, j);
-        const float jks = __shfl_sync(0xffffffffu, ks, j);
-        const float jvs = __shfl_sync(0xffffffffu, vs, j);
+      // Lane-parallel issue: the tiles of this chunk take consecutive ring
+      // positions in block order; every issuing lane handles its own tile, at
+      // most kStages lanes (distinct stages) per round.
+      const uint32_t mask = __ballot_sync(0xffffffffu, issue);
+      const int n_issue = __popc(mask);
+      const int rank = __popc(mask & ((1u << lane) - 1u));
+      for (int r0 = 0; r0 < n_issue; r0 += Cfg::kStages) {
         int ok = 1;
-        if (lane == 0) {
-          const int s = tile % Cfg::kStages;
-          const uint32_t ph = (uint32_t)(tile / Cfg::kStages) & 1u;
+        if (issue && rank >= r0 && rank < r0 + Cfg::kStages) {
+          const int my = tile + rank;
+          const int s = my % Cfg::kStages;
+          const uint32_t ph = (uint32_t)(my / Cfg::kStages) & 1u;
           if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
             ok = 0;
           } else {
+            const int jst = st, jlen = len, jslot = slot;
             TileInfo ti;
             ti.state = jst;
             ti.len = jlen;
-            ti.block = base + j;
-            ti.ks = jks;
-            ti.vs = jvs;
+            ti.block = i;
+            ti.ks = ks;
+            ti.vs = vs;
             info[s] = ti;
             const int32_t row = (jslot * p.kv_heads + kvh) * BS;
             uint8_t* kdst = stages + s * Cfg::kStageBytes;
             uint8_t* vdst = kdst + Cfg::kHotBytes;
             if (jst == 0) {
               mbar_arrive_expect_tx(&full_bar[s], 2 * Cfg::kHotBytes);
+#if TKV_HOT_3D
+              // one box {64, BS, D/64}: smem [D/64][BS][64], the same layout as
+              // the per-half 2-D boxes below
+              tma_load_3d(kdst, &tm_hk, 0, row, 0, &full_bar[s]);
+              tma_load_3d(vdst, &tm_hv, 0, row, 0, &full_bar[s]);
+#else
 #pragma unroll
               for (int hh = 0; hh < D / 64; ++hh) {
                 tma_load_2d(kdst + hh * BS * 128, &tm_hk, hh * 64, row, &full_bar[s]);
                 tma_load_2d(vdst + hh * BS * 128, &tm_hv, hh * 64, row, &full_bar[s]);
               }
+#endif
             } else {
               const uint32_t mbytes = (FMT == kFmtR) ? 4 * BS * 2 : 0;
               mbar_arrive_expect_tx(&full_bar[s], 2 * BS * D + mbytes);
@@ -282,29 +305,26 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, 2)
             }
           }
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
+        if (!__all_sync(0xffffffffu, ok)) {
           fail = true;
           break;
         }
-        ++tile;
       }
+      tile += n_issue;
     }
-    // one end-of-stream marker per consumer warp
-    if (lane == 0 && !fail) {
-      for (int c = 0; c < Cfg::kConsumers; ++c) {
-        const int s = tile % Cfg::kStages;
-        const uint32_t ph = (uint32_t)(tile / Cfg::kStages) & 1u;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
-          fail = true;
-          break;
-        }
+    // one end-of-stream marker per consumer warp (kConsumers <= kStages lanes)
+    if (!fail && lane < Cfg::kConsumers) {
+      const int my = tile + lane;
+      const int s = my % Cfg::kStages;
+      const uint32_t ph = (uint32_t)(my / Cfg::kStages) & 1u;
+      if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
+        fail = true;
+      } else {
         info[s].state = -1;
         mbar_arrive(&full_bar[s]);
-        ++tile;
       }
     }
-    fail = __shfl_sync(0xffffffffu, (int)fail, 0) != 0;
+    fail = __any_sync(0xffffffffu, fail);
     if (fail && lane == 0) atomicOr(p.err, 0x2u);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) cold += __shfl_xor_sync(0xffffffffu, cold, off);

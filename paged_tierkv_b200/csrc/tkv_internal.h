@@ -6,6 +6,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// HOT tiles: one 3-D TMA box per K/V tile instead of head_dim/64 2-D boxes.
+#ifndef TKV_HOT_3D
+#define TKV_HOT_3D 1
+#endif
+
 namespace tkv {
 
 constexpr int kFmtR = 0;

@@ -159,9 +159,14 @@ def _as_table(t: torch.Tensor, batch: int, name: str) -> torch.Tensor:
         t = t.unsqueeze(0)
     if t.ndim != 2 or t.shape[0] != batch:
         raise ValueError(f"{name} must have shape [batch, max_blocks].")
-    if t.stride(1) != 1:
+    if t.stride(1) != 1 or (batch > 1 and t.stride(0) < t.shape[1]):
         t = t.contiguous()
     return t
+
+
+def _row_stride(t: torch.Tensor) -> int:
+    """Row stride of a [batch, max_blocks] table; a single row may carry any stride."""
+    return int(t.stride(0)) if t.shape[0] > 1 else int(t.shape[1])
 
 
 def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_states: torch.Tensor,
@@ -193,7 +198,7 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
     table = _as_table(block_table, batch, "block_table")
     states = _as_table(block_states, batch, "block_states")
     lengths = _as_table(block_lengths, batch, "block_lengths")
-    if not (table.stride(0) == states.stride(0) == lengths.stride(0)):
+    if not (_row_stride(table) == _row_stride(states) == _row_stride(lengths)):
         table, states, lengths = table.contiguous(), states.contiguous(), lengths.contiguous()
     max_blocks = int(table.shape[1])
     nb_dev = None
@@ -216,7 +221,7 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
     pstruct = pools.as_struct()
     args = N.TkvDecodeArgs(
         _ptr(query), _DTYPE[query.dtype], _DTYPE[odt], batch, num_heads, int(num_key_value_groups),
-        max_blocks, _ptr(table), _ptr(states), _ptr(lengths), int(table.stride(0)), _ptr(nb_dev),
+        max_blocks, _ptr(table), _ptr(states), _ptr(lengths), _row_stride(table), _ptr(nb_dev),
         nb_uniform, float(scaling), _ptr(out), _ptr(lse), _ptr(scores), int(num_splits), 0, None, 0)
     splits = ctypes.c_int32()
     nbytes = ctypes.c_size_t()
@@ -299,7 +304,7 @@ def block_scores(score_sums: torch.Tensor, block_lengths: torch.Tensor, num_bloc
         nb = t
     else:
         nb = int(num_blocks)
-    N.check(N.load().tkv_block_scores(score_sums.data_ptr(), lengths.data_ptr(), lengths.stride(0),
+    N.check(N.load().tkv_block_scores(score_sums.data_ptr(), lengths.data_ptr(), _row_stride(lengths),
                                       _ptr(nb_dev), nb, b, hq, t, out.data_ptr(), _stream(stream)),
             "tkv_block_scores")
     return out[0] if squeeze else out
