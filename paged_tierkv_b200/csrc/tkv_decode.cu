@@ -8,7 +8,7 @@
 // only add the analytic term n * exp(0 - m) to the softmax denominator), and
 // streams each HOT / WARM block tile of this kv head through a ring of shared
 // memory stages with TMA (128-byte swizzled boxes; no multicast), completing
-// on an mbarrier per stage.  Warps 1..4 consume tiles round-robin: each tile
+// on an mbarrier per stage.  The other warps consume tiles round-robin: each tile
 // is one logical block (16 or 32 tokens x head_dim) for all query heads of
 // the GQA group, so K/V are read from HBM once per kv head.
 //   S^T[tok, h] = K[tok, :] . Q[h, :]       mma.m16n8k16 (M = tokens, N = heads)
@@ -40,16 +40,16 @@ struct TileInfo {
 // Pipeline shape: consumer warps per CTA, ring depth for stages of <= 8 KB and
 // of 16 KB, and the CTAs per SM the register budget is sized for.
 #ifndef TKV_CONSUMERS
-#define TKV_CONSUMERS 4
+#define TKV_CONSUMERS 3
 #endif
 #ifndef TKV_STAGES_8K
-#define TKV_STAGES_8K 12
+#define TKV_STAGES_8K 6
 #endif
 #ifndef TKV_STAGES_16K
-#define TKV_STAGES_16K 4
+#define TKV_STAGES_16K 3
 #endif
 #ifndef TKV_MIN_CTAS
-#define TKV_MIN_CTAS 2
+#define TKV_MIN_CTAS 4
 #endif
 
 template <int D, int BS, int FMT, int QT>
@@ -69,7 +69,12 @@ struct DecodeCfg {
   static constexpr int kOffInfo = kOffBars + 2 * kStages * 8;
   static constexpr int kOffMeta = kOffInfo + kStages * (int)sizeof(TileInfo);
   static constexpr int kOffMisc = kOffMeta + kStages * kMetaBytes;
-  static constexpr int kSmemBytes = 1024 + kOffMisc + 64;
+  // query of the GQA group, fp16, twice: standard d order (HOT K) and the
+  // permuted order of the register-expanded WARM K; rows padded by 16 bytes
+  static constexpr int kQStride = D + 8;
+  static constexpr int kOffQ = kOffMisc + 64;
+  static constexpr int kQBytes = kMaxGroups * kQStride * 2;
+  static constexpr int kSmemBytes = 1024 + kOffQ + 2 * kQBytes;
   // the end-of-kernel merge scratch aliases the stage ring
   static constexpr int kMergeFloats = kConsumers * (2 * kMaxGroups + kMaxGroups * D);
   static_assert(kMergeFloats * 4 <= kStages * kStageBytes, "merge scratch must fit the ring");
@@ -90,62 +95,68 @@ __device__ __forceinline__ uint32_t ld_u32(const void* p) {
   return *reinterpret_cast<const uint32_t*>(p);
 }
 
-// Query fragments of one consumer warp.  Lane (g, t) supplies column n = g
-// (query head kvh*G + g) of the B operand.
-//  qh: standard layout for ldmatrix-fed HOT K:   d = 16ks + 2t + {0,1}, +8
-//  qw: layout of the register-expanded WARM K:   d = t*D/4 + 4s + {0,1}, {2,3}
+// Stages the query heads of this kv head in shared memory (all threads of the
+// CTA take part; ends with __syncthreads).  Rows n >= G are zero.
+//  sqh[n][d]        standard d order, for ldmatrix-fed HOT K fragments
+//  sqw[n][pw(d)]    permuted so that a standard ldmatrix of k-step s hands lane
+//                   t the dims t*D/4 + 4s + {0,1} (b0) and + {2,3} (b1), the
+//                   order of the register-expanded WARM K codes
 // bf16 queries are rescaled per head by 2^-e (exact) so they fit fp16; the
-// factor 2^e is folded into qmul.
-template <int D, int QT>
-__device__ __forceinline__ void load_query(const DecodeParams& p, int seq, int kvh, int lane,
-                                           uint32_t (&qh)[D / 16][2], uint32_t (&qw)[D / 16][2],
-                                           float (&qmul)[2]) {
-  const int g = lane >> 2, t = lane & 3;
-  const bool valid = g < p.groups;
-  const size_t row = (size_t)seq * p.num_heads + (size_t)kvh * p.groups + (valid ? g : 0);
-  int e = 0;
-  if (QT == kDtF16) {
-    const __half* q = reinterpret_cast<const __half*>(p.query) + row * D;
+// factor 2^e is returned through sexp and folded into the logit scale.
+template <int D, int QT, int NT>
+__device__ __forceinline__ void stage_query(const DecodeParams& p, int seq, int kvh,
+                                            __half* sqh, __half* sqw, int* sexp) {
+  constexpr int QS = D + 8;
+  const int G = p.groups;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t row0 = (size_t)seq * p.num_heads + (size_t)kvh * G;
+  if (QT == kDtBF16) {
+    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.query);
+    for (int n = warp; n < kMaxGroups; n += NT / 32) {
+      float amax = 0.f;
+      if (n < G)
+        for (int d = lane; d < D; d += 32)
+          amax = fmaxf(amax, fabsf(__bfloat162float(q[(row0 + n) * D + d])));
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      qh[ks][0] = valid ? ld_u32(q + 16 * ks + 2 * t) : 0u;
-      qh[ks][1] = valid ? ld_u32(q + 16 * ks + 2 * t + 8) : 0u;
-      qw[ks][0] = valid ? ld_u32(q + t * (D / 4) + 4 * ks) : 0u;
-      qw[ks][1] = valid ? ld_u32(q + t * (D / 4) + 4 * ks + 2) : 0u;
+      for (int off = 16; off > 0; off >>= 1)
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      int k = 0;
+      frexpf(amax, &k);  // amax < 2^k
+      if (lane == 0) sexp[n] = max(0, k - 15);
     }
-  } else {
-    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.query) + row * D;
-    float amax = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t])));
-      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t + 1])));
-      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t + 8])));
-      amax = fmaxf(amax, fabsf(__bfloat162float(q[16 * ks + 2 * t + 9])));
-    }
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    int k = 0;
-    frexpf(amax, &k);          // amax < 2^k
-    e = valid ? max(0, k - 15) : 0;
-    const float f = ldexpf(1.f, -e);
-    auto cv = [&](int d) -> uint32_t {
-      if (!valid) return 0u;
-      return pack_half2(__bfloat162float(q[d]) * f, __bfloat162float(q[d + 1]) * f);
-    };
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      qh[ks][0] = cv(16 * ks + 2 * t);
-      qh[ks][1] = cv(16 * ks + 2 * t + 8);
-      qw[ks][0] = cv(t * (D / 4) + 4 * ks);
-      qw[ks][1] = cv(t * (D / 4) + 4 * ks + 2);
-    }
+  } else if (threadIdx.x < kMaxGroups) {
+    sexp[threadIdx.x] = 0;
   }
-  // logits of heads 2t and 2t+1 live in this lane; fetch those heads' factors
-  const int e0 = __shfl_sync(0xffffffffu, e, (2 * t) * 4);
-  const int e1 = __shfl_sync(0xffffffffu, e, (2 * t + 1) * 4);
-  qmul[0] = ldexpf(p.scale_log2, e0);
-  qmul[1] = ldexpf(p.scale_log2, e1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < kMaxGroups * D; e += NT) {
+    const int n = e / D;
+    const int d = e - n * D;
+    float v = 0.f;
+    if (n < G) {
+      if (QT == kDtF16)
+        v = __half2float(reinterpret_cast<const __half*>(p.query)[(row0 + n) * D + d]);
+      else
+        v = ldexpf(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.query)[(row0 + n) * D + d]),
+                   -sexp[n]);
+    }
+    const __half h = __float2half_rn(v);
+    sqh[n * QS + d] = h;
+    const int tq = d / (D / 4);
+    const int s = (d % (D / 4)) / 4;
+    const int j = d & 3;
+    sqw[n * QS + 16 * s + 2 * tq + (j & 1) + 8 * (j >> 1)] = h;
+  }
+  __syncthreads();
+}
+
+// B fragments (k = head_dim, n = query head) of k-steps 2m and 2m+1 from a
+// staged query block: lane (g, t) receives rows n = g, dims 16ks + 2t (+8).
+template <int D>
+__device__ __forceinline__ void load_qfrag(uint32_t sq, int lane, int m, uint32_t& b00,
+                                           uint32_t& b01, uint32_t& b10, uint32_t& b11) {
+  constexpr int QS = D + 8;
+  const uint32_t addr = sq + ((lane & 7) * QS + 32 * m + 8 * (lane >> 3)) * 2;
+  ldsm_x4(addr, b00, b01, b10, b11);
 }
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0
@@ -166,7 +177,9 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   uint64_t* empty_bar = full_bar + Cfg::kStages;
   TileInfo* info = reinterpret_cast<TileInfo*>(smem + Cfg::kOffInfo);
   uint8_t* meta = smem + Cfg::kOffMeta;
-  int* misc = reinterpret_cast<int*>(smem + Cfg::kOffMisc);  // [0] cold tokens, [1] last-CTA flag
+  int* misc = reinterpret_cast<int*>(smem + Cfg::kOffMisc);  // [0] cold, [1] last CTA, [8..16) exp
+  __half* sqh = reinterpret_cast<__half*>(smem + Cfg::kOffQ);
+  __half* sqw = reinterpret_cast<__half*>(smem + Cfg::kOffQ + Cfg::kQBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     misc[1] = 0;
     fence_mbar_init();
   }
-  __syncthreads();
+  stage_query<D, QT, Cfg::kThreads>(p, seq, kvh, sqh, sqw, misc + 8);  // ends with __syncthreads
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -334,20 +347,23 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   // ------------------------------------------------------------ consumers
   float m2[2] = {-INFINITY, -INFINITY};  // running max (log2 domain), heads 2t, 2t+1
   float l[2] = {0.f, 0.f};               // this lane's share of the denominator
-  float acc_h[Cfg::kKS][4];              // O^T from HOT tiles   (standard d layout)
-  float acc_w[Cfg::kKS][4];              // O^T from WARM tiles  (expanded d layout)
+  // O^T accumulator; m-tile 4kk+i holds rows d = 64kk + 4g + i (row g) and
+  // 64kk + 32 + 4g + i (row g+8), columns = heads 2t, 2t+1
+  float acc[Cfg::kKS][4];
 #pragma unroll
   for (int i = 0; i < Cfg::kKS; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc_h[i][j] = acc_w[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
   const int g = lane >> 2;
   const int t = lane & 3;
   if (warp > 0) {
     const int cw = warp - 1;
-    uint32_t qh[Cfg::kKS][2], qw[Cfg::kKS][2];
-    float qmul[2];
-    load_query<D, QT>(p, seq, kvh, lane, qh, qw, qmul);
+    const uint32_t sqh_u = smem_u32(sqh);
+    const uint32_t sqw_u = smem_u32(sqw);
+    float qmul[2];  // logit scale (log2 domain) of heads 2t, 2t+1
+    qmul[0] = ldexpf(p.scale_log2, misc[8 + 2 * t]);
+    qmul[1] = ldexpf(p.scale_log2, misc[8 + 2 * t + 1]);
 
     for (int it = cw;; it += Cfg::kConsumers) {
       const int s = it % Cfg::kStages;
@@ -373,16 +389,22 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           const int r = 16 * u + (lane & 7) + (((lane >> 3) & 1) << 3);
           float xa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int ks = 0; ks < Cfg::kKS; ++ks) {
-            const int ch = 2 * ks + (lane >> 4);
-            const uint32_t addr =
-                kb + (ch >> 3) * (BS * 128) + r * 128 + ((((ch & 7) ^ (lane & 7))) << 4);
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(addr, a0, a1, a2, a3);
-            if (ks & 1)
-              mma_16816(xa, a0, a1, a2, a3, qh[ks][0], qh[ks][1]);
-            else
-              mma_16816(x[u], a0, a1, a2, a3, qh[ks][0], qh[ks][1]);
+          for (int m = 0; m < Cfg::kKS / 2; ++m) {
+            uint32_t b00, b01, b10, b11;
+            load_qfrag<D>(sqh_u, lane, m, b00, b01, b10, b11);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const int ks = 2 * m + kk;
+              const int ch = 2 * ks + (lane >> 4);
+              const uint32_t addr =
+                  kb + (ch >> 3) * (BS * 128) + r * 128 + ((((ch & 7) ^ (lane & 7))) << 4);
+              uint32_t a0, a1, a2, a3;
+              ldsm_x4(addr, a0, a1, a2, a3);
+              if (kk)
+                mma_16816(xa, a0, a1, a2, a3, b10, b11);
+              else
+                mma_16816(x[u], a0, a1, a2, a3, b00, b01);
+            }
           }
           x[u][0] = (x[u][0] + xa[0]) * qmul[0];
           x[u][1] = (x[u][1] + xa[1]) * qmul[1];
@@ -419,20 +441,26 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           }
           float xa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int ks = 0; ks < Cfg::kKS; ++ks) {
-            uint32_t c0 = w0[ks], c1 = w1[ks];
-            if (FMT == kFmtS) {
-              c0 ^= 0x80808080u;
-              c1 ^= 0x80808080u;
+          for (int m = 0; m < Cfg::kKS / 2; ++m) {
+            uint32_t bq[2][2];
+            load_qfrag<D>(sqw_u, lane, m, bq[0][0], bq[0][1], bq[1][0], bq[1][1]);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const int ks = 2 * m + kk;
+              uint32_t c0 = w0[ks], c1 = w1[ks];
+              if (FMT == kFmtS) {
+                c0 ^= 0x80808080u;
+                c1 ^= 0x80808080u;
+              }
+              const uint32_t a0 = hsub2_u32(__byte_perm(c0, kMagic, 0x4140), z0);
+              const uint32_t a2 = hsub2_u32(__byte_perm(c0, kMagic, 0x4342), z0);
+              const uint32_t a1 = hsub2_u32(__byte_perm(c1, kMagic, 0x4140), z1);
+              const uint32_t a3 = hsub2_u32(__byte_perm(c1, kMagic, 0x4342), z1);
+              if (kk)
+                mma_16816(xa, a0, a1, a2, a3, bq[1][0], bq[1][1]);
+              else
+                mma_16816(x[u], a0, a1, a2, a3, bq[0][0], bq[0][1]);
             }
-            const uint32_t a0 = hsub2_u32(__byte_perm(c0, kMagic, 0x4140), z0);
-            const uint32_t a2 = hsub2_u32(__byte_perm(c0, kMagic, 0x4342), z0);
-            const uint32_t a1 = hsub2_u32(__byte_perm(c1, kMagic, 0x4140), z1);
-            const uint32_t a3 = hsub2_u32(__byte_perm(c1, kMagic, 0x4342), z1);
-            if (ks & 1)
-              mma_16816(xa, a0, a1, a2, a3, qw[ks][0], qw[ks][1]);
-            else
-              mma_16816(x[u], a0, a1, a2, a3, qw[ks][0], qw[ks][1]);
           }
           x[u][0] = (x[u][0] + xa[0]) * (qmul[0] * sc0);
           x[u][1] = (x[u][1] + xa[1]) * (qmul[1] * sc0);
@@ -478,10 +506,8 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
         for (int i = 0; i < Cfg::kKS; ++i) {
-          acc_h[i][0] *= alpha[0]; acc_h[i][1] *= alpha[1];
-          acc_h[i][2] *= alpha[0]; acc_h[i][3] *= alpha[1];
-          acc_w[i][0] *= alpha[0]; acc_w[i][1] *= alpha[1];
-          acc_w[i][2] *= alpha[0]; acc_w[i][3] *= alpha[1];
+          acc[i][0] *= alpha[0]; acc[i][1] *= alpha[1];
+          acc[i][2] *= alpha[0]; acc[i][3] *= alpha[1];
         }
       }
       if (p.lse_blk != nullptr) {
@@ -510,18 +536,31 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           pb[u][0] = movmatrix_t(pack_half2(pr[u][0], pr[u][1]));
           pb[u][1] = movmatrix_t(pack_half2(pr[u][2], pr[u][3]));
         }
-        const int mj = lane >> 3;
+        // V tile in shared memory: [D/64][BS][64] fp16, 128-byte swizzled lines.
+        // Lane (g, t) reads 4 dims of tokens 2t, 2t+1, 2t+8, 2t+9 with one
+        // 8-byte load each and pairs the tokens with byte permutes.
 #pragma unroll
-        for (int i = 0; i < Cfg::kKS; ++i) {
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          const int r0 = 16 * u + 2 * t;
 #pragma unroll
-          for (int u = 0; u < Cfg::kSub; ++u) {
-            const int r = 16 * u + (lane & 7) + ((mj >> 1) << 3);
-            const int ch = 2 * i + (mj & 1);
-            const uint32_t addr =
-                vb + (ch >> 3) * (BS * 128) + r * 128 + ((((ch & 7) ^ (lane & 7))) << 4);
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4_t(addr, a0, a1, a2, a3);
-            mma_16816(acc_h[i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+          for (int kk = 0; kk < D / 64; ++kk) {
+            const uint32_t line = kk * BS;
+            auto ld = [&](int r, int off) -> uint2 {
+              return lds64(vb + swz<7>((line + r) * 128 + off));
+            };
+            const uint2 l0 = ld(r0, 8 * g), l1 = ld(r0 + 1, 8 * g);
+            const uint2 l2 = ld(r0 + 8, 8 * g), l3 = ld(r0 + 9, 8 * g);
+            const uint2 h0 = ld(r0, 64 + 8 * g), h1 = ld(r0 + 1, 64 + 8 * g);
+            const uint2 h2 = ld(r0 + 8, 64 + 8 * g), h3 = ld(r0 + 9, 64 + 8 * g);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+              const uint32_t a0 = __byte_perm(i < 2 ? l0.x : l0.y, i < 2 ? l1.x : l1.y, sel);
+              const uint32_t a1 = __byte_perm(i < 2 ? h0.x : h0.y, i < 2 ? h1.x : h1.y, sel);
+              const uint32_t a2 = __byte_perm(i < 2 ? l2.x : l2.y, i < 2 ? l3.x : l3.y, sel);
+              const uint32_t a3 = __byte_perm(i < 2 ? h2.x : h2.y, i < 2 ? h3.x : h3.y, sel);
+              mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+            }
           }
         }
       } else {
@@ -580,7 +619,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
               const uint32_t a1 = hsub2_u32(__byte_perm(xh[i >> 1], kMagic, sel), z01);
               const uint32_t a2 = hsub2_u32(__byte_perm(yl[i >> 1], kMagic, sel), z23);
               const uint32_t a3 = hsub2_u32(__byte_perm(yh[i >> 1], kMagic, sel), z23);
-              mma_16816(acc_w[4 * kk + i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+              mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
             }
           }
         }
@@ -610,23 +649,15 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     }
     float* a = sm_acc + (size_t)cw * kMaxGroups * D;
 #pragma unroll
-    for (int i = 0; i < Cfg::kKS; ++i) {
-      a[(2 * t) * D + 16 * i + g] = acc_h[i][0];
-      a[(2 * t + 1) * D + 16 * i + g] = acc_h[i][1];
-      a[(2 * t) * D + 16 * i + 8 + g] = acc_h[i][2];
-      a[(2 * t + 1) * D + 16 * i + 8 + g] = acc_h[i][3];
-    }
-    __syncwarp();
-#pragma unroll
     for (int kk = 0; kk < D / 64; ++kk) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int dlo = 64 * kk + 4 * g + i;
         const int dhi = dlo + 32;
-        a[(2 * t) * D + dlo] += acc_w[4 * kk + i][0];
-        a[(2 * t + 1) * D + dlo] += acc_w[4 * kk + i][1];
-        a[(2 * t) * D + dhi] += acc_w[4 * kk + i][2];
-        a[(2 * t + 1) * D + dhi] += acc_w[4 * kk + i][3];
+        a[(2 * t) * D + dlo] = acc[4 * kk + i][0];
+        a[(2 * t + 1) * D + dlo] = acc[4 * kk + i][1];
+        a[(2 * t) * D + dhi] = acc[4 * kk + i][2];
+        a[(2 * t + 1) * D + dhi] = acc[4 * kk + i][3];
       }
     }
   }
