@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--sweep", action="store_true",
                     help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
+    ap.add_argument("--config", choices=["c5", "c4"], default="c5",
+                    help="c5: data-parallel batches (default); c4: one 131k-token context "
+                         "over 32 layers, sharded by block range across the GPUs")
+    ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -372,6 +376,75 @@ def run_ours(a, rank, world, dist_on, device):
     print(json.dumps(line), flush=True)
 
 
+def run_c4(a, rank, world, dist_on, device):
+    """Configuration 4: batch 1, 131072 tokens, 32 layers, 10 % HOT / 60 % WARM /
+    30 % COLD; every layer's blocks are split into byte-balanced contiguous
+    ranges, one per GPU; per layer one decode launch, one all-gather of the
+    packed (o, LSE) partials and one merge launch.  Strong scaling."""
+    from paged_tierkv_b200 import _native, sharding, workloads
+    _native.load(build_if_missing=True)
+    ctx, bs, d, hkv, hq = 131072, a.block_size, 128, 8, 32
+    nb = ctx // bs
+    n_hot, n_warm, _ = workloads.tier_counts(nb, 0.10, 0.60)
+    layers = []
+    total_bytes = 0
+    for layer in range(a.layers):
+        states = workloads.assign_tiers(1, nb, n_hot, n_warm, seed=5000 + layer)
+        lengths = torch.full((1, nb), bs, dtype=torch.int32)
+        ranges = workloads.balanced_block_ranges(states, world, bs, d)
+        s, e = ranges[rank]
+        wl = workloads.materialize(states[:, s:e].contiguous(), lengths[:, s:e].contiguous(),
+                                   q_heads=hq, kv_heads=hkv, head_dim=d, block_size=bs,
+                                   seed=7000 + 97 * layer + rank, device=device)
+        layers.append(wl)
+        total_bytes += wl.algorithmic_bytes()
+    dec = sharding.ContextShardedDecode()
+    out = torch.empty((1, hq, d), dtype=torch.float16, device=device)
+
+    def step():
+        for wl in layers:
+            if world == 1:
+                workloads.decode(wl, out=out)
+            else:
+                dec(wl.query, wl.block_table, wl.block_states, wl.block_lengths, wl.pools,
+                    wl.num_blocks, wl.groups, wl.scaling)
+
+    for _ in range(a.warmup):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    t = torch.tensor([e0.elapsed_time(e1), float(total_bytes)], dtype=torch.float64, device=device)
+    if dist_on:
+        tb = t.clone()
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(tb, op=torch.distributed.ReduceOp.SUM)
+        t[1] = tb[1]
+    ms = float(t[0]) / a.steps
+    if rank != 0:
+        return
+    line = {
+        "metric": "tiered decode tokens/s (C4: 131072-token context, 32 layers, block-range sharded)",
+        "value": round(1000.0 / ms, 2), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": f"c4_ctx{ctx}_bs{bs}_l{a.layers}", "hot_blocks": n_hot,
+                   "warm_blocks": n_warm, "partition": "byte-balanced contiguous block ranges",
+                   "exchange": "NCCL all_gather of packed (o, lse) per layer" if world > 1 else "none"},
+        "GBps_all_gpus": round(float(t[1]) / (ms * 1e-3) / 1e9, 1),
+        "gpu_launches": a.steps * a.layers * (1 if world == 1 else 2),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -390,6 +463,8 @@ def main():
     try:
         if a.impl == "reference":
             run_reference(a, rank)
+        elif a.config == "c4":
+            run_c4(a, rank, world, dist_on, device)
         else:
             run_ours(a, rank, world, dist_on, device)
     finally:

@@ -214,8 +214,13 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
         raise ValueError("out must be a contiguous [batch, num_heads, head_dim] tensor.")
     scores = (torch.empty((batch, num_heads, max_blocks), dtype=torch.float32, device=query.device)
               if return_scores else None)
-    lse = (torch.empty((batch, num_heads), dtype=torch.float32, device=query.device)
-           if return_lse else None)
+    if isinstance(return_lse, torch.Tensor):
+        lse = return_lse  # caller-provided [batch, num_heads] fp32 destination
+        if lse.dtype != torch.float32 or lse.numel() != batch * num_heads or not lse.is_contiguous():
+            raise ValueError("the LSE destination must be a contiguous fp32 [batch, num_heads] tensor.")
+    else:
+        lse = (torch.empty((batch, num_heads), dtype=torch.float32, device=query.device)
+               if return_lse else None)
     lib = N.load()
     st = _stream(stream)
     pstruct = pools.as_struct()

@@ -1,0 +1,118 @@
+"""Multi-GPU partitioning of the tiered decode path (one process per GPU).
+
+The reference runs on one GPU; these are the two ways the path is spread over
+the GPUs of one node:
+
+* data parallel: each rank owns whole sequences (``dp_slice``).  Sequences
+  are independent, so there is no collective on the data path.
+* context parallel: one long context is split into contiguous logical-block
+  ranges (``block_range``); rank r keeps the KV blocks of its range in its
+  own pools.  Each rank runs the decode kernel on its range and produces a
+  normalised partial (o fp32, LSE); one all-gather of the packed
+  [o | LSE] buffer (NCCL over NVLink) and the LSE-merge kernel give every rank
+  the full-context output.  Block scores need no second exchange:
+  p_global = p_local * exp(lse_local - lse_global).
+
+COLD blocks stay exact under sharding: each rank adds the analytic
+``n * exp(0 - m)`` term of the COLD tokens in its own range.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+
+from . import ops
+
+
+def dp_slice(batch: int, rank: int, world: int) -> slice:
+    """Contiguous share of ``batch`` sequences for ``rank`` (sizes differ by <= 1)."""
+    base, extra = divmod(int(batch), int(world))
+    start = rank * base + min(rank, extra)
+    return slice(start, start + base + (1 if rank < extra else 0))
+
+
+def block_range(num_blocks: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous logical-block range [start, end) of ``rank``; the sink block
+    is on rank 0 and the most recent blocks on the last rank."""
+    per = -(-int(num_blocks) // int(world)) if num_blocks > 0 else 0
+    start = min(rank * per, num_blocks)
+    return start, min(start + per, num_blocks)
+
+
+@dataclass
+class ShardResult:
+    out: torch.Tensor                   # [batch, num_heads, head_dim]
+    lse: torch.Tensor                   # [batch, num_heads] global natural-log LSE
+    score_sums: torch.Tensor | None     # [batch, num_heads, local_blocks] global mass
+
+
+def _local_cuda(query, table, states, lengths, pools, num_blocks, groups, scaling, o_out, lse_out,
+                return_scores):
+    _, scores, _ = ops.decode_attention(query, table, states, lengths, pools, num_blocks, groups,
+                                        scaling, out=o_out, out_dtype=torch.float32,
+                                        return_lse=lse_out, return_scores=return_scores)
+    return scores
+
+
+def _merge_cuda(part_o, part_lse, out_dtype):
+    return ops.merge_partials(part_o, part_lse, out_dtype=out_dtype, return_lse=True)
+
+
+class ContextShardedDecode:
+    """Decode of context-sharded sequences over a process group.
+
+    ``local_fn(query, table, states, lengths, pools, num_blocks, groups,
+    scaling, o_out, lse_out, return_scores) -> score_sums or None`` fills the
+    rank's normalised partial; ``merge_fn(part_o [P,R,D], part_lse [P,R],
+    out_dtype) -> (out [R,D], lse [R])`` merges gathered partials.  The
+    defaults are the sm_100a kernels; tests substitute CPU stand-ins to check
+    the partitioning and exchange logic over gloo.
+    """
+
+    def __init__(self, group=None, local_fn: Callable | None = None,
+                 merge_fn: Callable | None = None):
+        self.group = group
+        self.local_fn = local_fn or _local_cuda
+        self.merge_fn = merge_fn or _merge_cuda
+        self._bufs: dict = {}
+
+    def _buffers(self, rows: int, d: int, world: int, device):
+        key = (rows, d, world, str(device))
+        b = self._bufs.get(key)
+        if b is None:
+            n = rows * (d + 1)
+            b = (torch.empty(n, dtype=torch.float32, device=device),
+                 torch.empty(world * n, dtype=torch.float32, device=device))
+            self._bufs[key] = b
+        return b
+
+    def __call__(self, query: torch.Tensor, block_table: torch.Tensor, block_states: torch.Tensor,
+                 block_lengths: torch.Tensor, pools, num_blocks, num_key_value_groups: int,
+                 scaling: float, *, out_dtype=torch.float16, return_scores: bool = False) -> ShardResult:
+        """``query`` [B, Hq, D]; the tables hold only this rank's block range
+        ([B, local_T]) and ``num_blocks`` counts the valid local blocks."""
+        import torch.distributed as dist
+        world = dist.get_world_size(self.group)
+        b, hq, d = query.shape
+        rows = b * hq
+        local, gathered = self._buffers(rows, d, world, query.device)
+        o_local = local[:rows * d].view(b, hq, d)
+        lse_local = local[rows * d:].view(b, hq)
+        scores = self.local_fn(query, block_table, block_states, block_lengths, pools, num_blocks,
+                               num_key_value_groups, scaling, o_local, lse_local, return_scores)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, local, group=self.group)
+            parts = gathered.view(world, rows * (d + 1))
+        else:
+            parts = local.view(1, rows * (d + 1))
+        out, lse = self.merge_fn(parts[:, :rows * d].view(world, rows, d), parts[:, rows * d:],
+                                 out_dtype)
+        lse = lse.view(b, hq)
+        if scores is not None:
+            w = torch.exp(lse_local - lse)
+            w = torch.where(torch.isfinite(lse_local), w, torch.zeros_like(w))
+            scores = scores * w.unsqueeze(-1)
+        return ShardResult(out=out.view(b, hq, d), lse=lse, score_sums=scores)

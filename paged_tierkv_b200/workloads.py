@@ -63,32 +63,41 @@ class Workload:
         return self.batch * (hkv * per_seq_head + tables + qo)
 
 
-def make_workload(*, batch: int, q_heads: int, kv_heads: int, head_dim: int, block_size: int,
-                  ctx_tokens: int, hot_frac: float, warm_frac: float | None = None, seed: int = 0,
-                  device="cuda", fmt: int = ops.FORMAT_R, chunk_blocks: int = 2048) -> Workload:
-    device = torch.device(device)
-    nb = math.ceil(ctx_tokens / block_size)
-    n_hot, n_warm, n_cold = tier_counts(nb, hot_frac, warm_frac)
+def assign_tiers(batch: int, num_blocks: int, n_hot: int, n_warm: int, seed: int) -> torch.Tensor:
+    """States [batch, num_blocks]: HOT = block 0 + the last n_hot - 1 blocks,
+    WARM = n_warm middle blocks chosen by a seeded permutation, COLD = rest."""
     cpu = torch.Generator().manual_seed(seed)
-    states = torch.full((batch, nb), ops.COLD_STATE, dtype=torch.int32)
-    table = torch.full((batch, nb), -1, dtype=torch.int32)
-    lengths = torch.full((batch, nb), block_size, dtype=torch.int32)
-    tail = ctx_tokens - (nb - 1) * block_size
-    lengths[:, nb - 1] = tail
-    hot_perm = torch.randperm(max(1, batch * n_hot), generator=cpu).to(torch.int32)
-    warm_perm = torch.randperm(max(1, batch * n_warm), generator=cpu).to(torch.int32)
+    states = torch.full((batch, num_blocks), ops.COLD_STATE, dtype=torch.int32)
     for s in range(batch):
         hot_blocks = torch.cat([torch.zeros(1, dtype=torch.long),
-                                torch.arange(nb - (n_hot - 1), nb, dtype=torch.long)]) if n_hot > 1 \
-            else torch.zeros(1, dtype=torch.long)
-        middle = torch.arange(1, nb - (n_hot - 1), dtype=torch.long)
+                                torch.arange(num_blocks - (n_hot - 1), num_blocks, dtype=torch.long)]) \
+            if n_hot > 1 else torch.zeros(1, dtype=torch.long)
+        middle = torch.arange(1, num_blocks - (n_hot - 1), dtype=torch.long)
         warm_blocks = middle[torch.randperm(middle.numel(), generator=cpu)[:n_warm]]
         states[s, hot_blocks] = ops.HOT_STATE
         states[s, warm_blocks] = ops.WARM_STATE
-        table[s, hot_blocks] = hot_perm[s * n_hot:(s + 1) * n_hot]
-        table[s, warm_blocks.sort().values] = warm_perm[s * n_warm:(s + 1) * n_warm]
-    hot_slots = max(1, batch * n_hot)
-    warm_slots = max(1, batch * n_warm)
+    return states
+
+
+def materialize(states: torch.Tensor, lengths: torch.Tensor, *, q_heads: int, kv_heads: int,
+                head_dim: int, block_size: int, seed: int = 0, device="cuda",
+                fmt: int = ops.FORMAT_R, chunk_blocks: int = 2048) -> Workload:
+    """Pools, tables and a query for the given per-sequence tier states.
+
+    Slots are handed out in a seeded random order; HOT data is fp16 N(0, 1)
+    and WARM blocks are demoted on the device from fp16 N(0, 1) staging data."""
+    device = torch.device(device)
+    batch, nb = states.shape
+    cpu = torch.Generator().manual_seed(seed)
+    is_hot = states == ops.HOT_STATE
+    is_warm = states == ops.WARM_STATE
+    n_hot_all = int(is_hot.sum())
+    n_warm_all = int(is_warm.sum())
+    table = torch.full((batch, nb), -1, dtype=torch.int32)
+    table[is_hot] = torch.randperm(max(1, n_hot_all), generator=cpu)[:n_hot_all].to(torch.int32)
+    table[is_warm] = torch.randperm(max(1, n_warm_all), generator=cpu)[:n_warm_all].to(torch.int32)
+    hot_slots = max(1, n_hot_all)
+    warm_slots = max(1, n_warm_all)
     pools = ops.TieredPools.allocate(hot_slots, warm_slots, kv_heads, block_size, head_dim,
                                      device, fmt=fmt)
     gen = torch.Generator(device=device).manual_seed(seed + 1)
@@ -96,12 +105,13 @@ def make_workload(*, batch: int, q_heads: int, kv_heads: int, head_dim: int, blo
         n = min(chunk_blocks, hot_slots - start)
         pools.hot_k[start:start + n].normal_(generator=gen)
         pools.hot_v[start:start + n].normal_(generator=gen)
-    if batch * n_warm > 0:
-        shape = (chunk_blocks, kv_heads, block_size, head_dim)
+    if n_warm_all > 0:
+        cb = min(chunk_blocks, warm_slots)
+        shape = (cb, kv_heads, block_size, head_dim)
         stage_k = torch.empty(shape, dtype=torch.float16, device=device)
         stage_v = torch.empty(shape, dtype=torch.float16, device=device)
-        for start in range(0, warm_slots, chunk_blocks):
-            n = min(chunk_blocks, warm_slots - start)
+        for start in range(0, warm_slots, cb):
+            n = min(cb, warm_slots - start)
             stage_k.normal_(generator=gen)
             stage_v.normal_(generator=gen)
             staging = ops.TieredPools(stage_k, stage_v, pools.warm_k, pools.warm_v, pools.k_scale,
@@ -112,15 +122,52 @@ def make_workload(*, batch: int, q_heads: int, kv_heads: int, head_dim: int, blo
         del stage_k, stage_v
     query = torch.randn((batch, q_heads, head_dim), generator=gen, device=device,
                         dtype=torch.float32).to(torch.float16)
-    wl = Workload(pools=pools, query=query, block_table=table.to(device),
-                  block_states=states.to(device), block_lengths=lengths.to(device),
-                  num_blocks=nb, groups=q_heads // kv_heads, scaling=head_dim ** -0.5,
-                  n_hot=n_hot, n_warm=n_warm, n_cold=n_cold)
+    per_seq = lambda m: int(m.sum()) // max(1, batch)  # noqa: E731
+    return Workload(pools=pools, query=query, block_table=table.to(device),
+                    block_states=states.to(device), block_lengths=lengths.to(device),
+                    num_blocks=nb, groups=q_heads // kv_heads, scaling=head_dim ** -0.5,
+                    n_hot=per_seq(is_hot), n_warm=per_seq(is_warm),
+                    n_cold=nb - per_seq(is_hot) - per_seq(is_warm))
+
+
+def make_workload(*, batch: int, q_heads: int, kv_heads: int, head_dim: int, block_size: int,
+                  ctx_tokens: int, hot_frac: float, warm_frac: float | None = None, seed: int = 0,
+                  device="cuda", fmt: int = ops.FORMAT_R, chunk_blocks: int = 2048) -> Workload:
+    """Benchmark workload: ``batch`` sequences of ``ctx_tokens`` with the tier mix
+    of :func:`tier_counts`."""
+    nb = math.ceil(ctx_tokens / block_size)
+    n_hot, n_warm, n_cold = tier_counts(nb, hot_frac, warm_frac)
+    states = assign_tiers(batch, nb, n_hot, n_warm, seed)
+    lengths = torch.full((batch, nb), block_size, dtype=torch.int32)
+    lengths[:, nb - 1] = ctx_tokens - (nb - 1) * block_size
+    wl = materialize(states, lengths, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim,
+                     block_size=block_size, seed=seed, device=device, fmt=fmt,
+                     chunk_blocks=chunk_blocks)
     wl.info = dict(batch=batch, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim,
                    block_size=block_size, ctx_tokens=ctx_tokens, hot_frac=hot_frac,
                    blocks_per_seq=nb, hot_blocks=n_hot, warm_blocks=n_warm, cold_blocks=n_cold,
                    seed=seed, warm_format="R" if fmt == ops.FORMAT_R else "S")
     return wl
+
+
+def balanced_block_ranges(states: torch.Tensor, world: int, block_size: int, head_dim: int):
+    """Contiguous block ranges whose HBM bytes (HOT 4*D, WARM 2*D + 8 per token,
+    COLD only its table entry) are as equal as possible across ``world`` ranks;
+    the LSE merge does not depend on where the boundaries fall."""
+    st = states.reshape(-1, states.shape[-1])[0].tolist()
+    cost = [block_size * (4 * head_dim if s == ops.HOT_STATE else
+                          (2 * head_dim + 8) if s == ops.WARM_STATE else 0) + 12 for s in st]
+    total = float(sum(cost))
+    bounds, acc, r = [0], 0.0, 1
+    for i, c in enumerate(cost):
+        acc += c
+        while r < world and acc >= total * r / world:
+            bounds.append(i + 1)
+            r += 1
+    while len(bounds) < world + 1:
+        bounds.append(len(st))
+    bounds[-1] = len(st)
+    return [(bounds[k], bounds[k + 1]) for k in range(world)]
 
 
 def decode(wl: Workload, **kw):
