@@ -54,6 +54,8 @@ def parse():
                     help="c5: data-parallel batches (default); c4: one 131k-token context "
                          "over 32 layers, sharded by block range across the GPUs")
     ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--no-graph", action="store_true",
+                    help="c4: launch every layer from Python instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -409,19 +411,38 @@ def run_c4(a, rank, world, dist_on, device):
                 dec(wl.query, wl.block_table, wl.block_states, wl.block_lengths, wl.pools,
                     wl.num_blocks, wl.groups, wl.scaling)
 
-    for _ in range(a.warmup):
-        step()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The whole 32-layer step (decode launches, all-gathers, merges) is captured
+    # once in a CUDA graph on a dedicated stream and replayed; warm-up runs on
+    # that stream first so no allocation happens during capture.
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(1, a.warmup)):
+            step()
+    torch.cuda.synchronize()
+    graph = None
+    if not a.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
+    with torch.cuda.stream(side):
+        for _ in range(a.warmup):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        if dist_on:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0.record(side)
+        for _ in range(a.steps):
+            run()
+        e1.record(side)
+        torch.cuda.synchronize()
     if dist_on:
         torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(a.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    if dist_on:
-        torch.distributed.barrier()
+    del graph
     t = torch.tensor([e0.elapsed_time(e1), float(total_bytes)], dtype=torch.float64, device=device)
     if dist_on:
         tb = t.clone()
@@ -438,7 +459,8 @@ def run_c4(a, rank, world, dist_on, device):
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": f"c4_ctx{ctx}_bs{bs}_l{a.layers}", "hot_blocks": n_hot,
                    "warm_blocks": n_warm, "partition": "byte-balanced contiguous block ranges",
-                   "exchange": "NCCL all_gather of packed (o, lse) per layer" if world > 1 else "none"},
+                   "exchange": "NCCL all_gather of packed (o, lse) per layer" if world > 1 else "none",
+                   "cuda_graph": not a.no_graph},
         "GBps_all_gpus": round(float(t[1]) / (ms * 1e-3) / 1e9, 1),
         "gpu_launches": a.steps * a.layers * (1 if world == 1 else 2),
     }

@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -60,16 +61,48 @@ bool encode_pool_map(CUtensorMap* map, void* base, bool fp16, int64_t rows, int 
   return r == CUDA_SUCCESS;
 }
 
+constexpr int kMaxDevices = 64;
+
+// SM count of the current device, cached per device (0 = not an sm_100 part).
 int current_device_sms(int* sms) {
+  static std::atomic<int> cache[kMaxDevices];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return TKV_ERR_NO_DEVICE;
+  if (dev >= 0 && dev < kMaxDevices) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) {
+      *sms = c;
+      return TKV_OK;
+    }
+  }
   int major = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
     return TKV_ERR_NO_DEVICE;
   if (major != 10) return TKV_ERR_NO_DEVICE;
   if (cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return TKV_ERR_NO_DEVICE;
+  if (dev >= 0 && dev < kMaxDevices) cache[dev].store(*sms, std::memory_order_relaxed);
   return TKV_OK;
+}
+
+// CTAs per SM of one decode kernel instance, cached per (device, instance).
+bool cached_occupancy(int head_dim, int block_size, int format, int query_dtype, int* ctas) {
+  static std::atomic<int> cache[kMaxDevices][16];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const int key = ((head_dim == 128) << 3) | ((block_size == 32) << 2) |
+                  ((format == TKV_FORMAT_S) << 1) | (query_dtype == TKV_DTYPE_BF16);
+  const bool cacheable = dev >= 0 && dev < kMaxDevices;
+  if (cacheable) {
+    const int c = cache[dev][key].load(std::memory_order_relaxed);
+    if (c > 0) {
+      *ctas = c;
+      return true;
+    }
+  }
+  if (decode_occupancy(head_dim, block_size, format, query_dtype, ctas) != cudaSuccess) return false;
+  if (cacheable && *ctas > 0) cache[dev][key].store(*ctas, std::memory_order_relaxed);
+  return true;
 }
 
 int32_t check_pools(const tkv_pools* pl, bool need_meta) {
@@ -139,22 +172,22 @@ int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
     st = current_device_sms(&sms);
     if (st != TKV_OK) return st;
     int ctas = 0;
-    if (decode_occupancy(pl->head_dim, pl->block_size, pl->format, a->query_dtype, &ctas) !=
-            cudaSuccess ||
+    if (!cached_occupancy(pl->head_dim, pl->block_size, pl->format, a->query_dtype, &ctas) ||
         ctas <= 0)
       return TKV_ERR_CUDA;
     const int64_t slots = (int64_t)sms * ctas;
     const int64_t units = (int64_t)a->batch * pl->kv_heads;
-    const int nb = std::max(1, a->num_blocks);
-    // cost ~ waves * (blocks per CTA + fixed CTA overhead of ~4 blocks)
+    // splits own interleaved 32-block chunks; cost ~ waves * (blocks per CTA
+    // + a fixed per-CTA overhead: prologue, pipeline fill and drain, merge)
+    const int chunks = std::max(1, (a->num_blocks + 31) / 32);
     double best = 1e300;
     splits = 1;
-    const int max_s = std::min(kMaxSplits, nb);
+    const int max_s = std::min(kMaxSplits, chunks);
     for (int s = 1; s <= max_s; ++s) {
       const int64_t ctas_total = units * s;
       const double waves = (double)((ctas_total + slots - 1) / slots);
-      const double per = std::ceil((double)nb / s);
-      const double cost = waves * (per + 4.0);
+      const double per = 32.0 * ((chunks + s - 1) / s);
+      const double cost = waves * (per + (double)TKV_CTA_OVERHEAD_BLOCKS);
       if (cost < best - 1e-9) {
         best = cost;
         splits = s;
@@ -166,8 +199,8 @@ int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
   size_t off = 0;
   plan->off_err = off;
   off = align_up(off + 16);
-  plan->off_counters = off;
-  off = align_up(off + sizeof(uint32_t) * (size_t)a->batch * pl->kv_heads);
+  plan->off_counters = off;  // split tickets, then chunk counters, one per (sequence, kv head)
+  off = align_up(off + 2 * sizeof(uint32_t) * (size_t)a->batch * pl->kv_heads);
   if (plan->splits > 1) {
     plan->off_part_o = off;
     off = align_up(off + sizeof(float) * rows * plan->splits * pl->head_dim);

@@ -3,8 +3,9 @@
 // Replaces the Triton kernels of xiaoMartintin/Paged_TierKV
 // (tierkv_triton.py:45-145 single pass + score pass, 147-264 split + reduce).
 //
-// One CTA per (split, kv head, sequence).  Warp 0 is the producer: it reads
-// the block table 32 entries at a time, skips COLD blocks (their valid tokens
+// One CTA per (split, kv head, sequence); split s owns the 32-block chunks
+// s, s + splits, ...  Warp 0 is the producer: it reads the block table one
+// chunk (32 entries) at a time, skips COLD blocks (their valid tokens
 // only add the analytic term n * exp(0 - m) to the softmax denominator), and
 // streams each HOT / WARM block tile of this kv head through a ring of shared
 // memory stages with TMA (128-byte swizzled boxes; no multicast), completing
@@ -22,6 +23,8 @@
 // merges the splits (split tickets reset themselves).
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+
+#include <atomic>
 
 #include "tkv_internal.h"
 #include "tkv_ptx.cuh"
@@ -191,9 +194,34 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
 
   int nb = p.nb_dev ? p.nb_dev[seq] : p.nb_uniform;
   nb = max(0, min(nb, p.max_blocks));
-  const int per = (nb + p.splits - 1) / p.splits;
-  const int b0 = min(nb, split * per);
-  const int b1 = min(nb, b0 + per);
+  // Work is handed out in 32-block chunks.  With several splits the CTAs of a
+  // (sequence, kv head) take chunks from a shared atomic counter, so CTAs on
+  // less loaded SMs (or launched earlier) take more of them and HOT-heavy
+  // chunks (sink, recent window) do not pile up on one CTA; the merge is
+  // order-free.  One split walks the chunks in order.
+  const int n_chunks = (nb + 31) / 32;
+  const bool dynamic = p.splits > 1;
+  const size_t unit = (size_t)seq * p.kv_heads + kvh;
+  uint32_t* chunk_ctr = p.counters + (size_t)p.batch * p.kv_heads + unit;
+  const int32_t* trow = p.table + (size_t)seq * p.table_stride;
+  const int32_t* srow = p.states + (size_t)seq * p.table_stride;
+  const int32_t* lrow = p.lengths + (size_t)seq * p.table_stride;
+  // the producer's first chunk (and its table entries) is requested before
+  // the prologue
+  int chunk = 0;
+  int nslot = -1, nstate = 2, nlen = 0;
+  if (warp == 0) {
+    if (dynamic) {
+      int c = 0;
+      if (lane == 0) c = (int)atomicAdd(chunk_ctr, 1u);
+      chunk = __shfl_sync(0xffffffffu, c, 0);
+    }
+    if (chunk < n_chunks && 32 * chunk + lane < nb) {
+      nslot = __ldg(trow + 32 * chunk + lane);
+      nstate = __ldg(srow + 32 * chunk + lane);
+      nlen = __ldg(lrow + 32 * chunk + lane);
+    }
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) {
@@ -214,31 +242,30 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       prefetch_tensormap(&tm_wk);
       prefetch_tensormap(&tm_wv);
     }
-    const int32_t* trow = p.table + (size_t)seq * p.table_stride;
-    const int32_t* srow = p.states + (size_t)seq * p.table_stride;
-    const int32_t* lrow = p.lengths + (size_t)seq * p.table_stride;
     int tile = 0;
     int cold = 0;
     bool fail = false;
-    // software-pipelined table reads: entries of the next 32-block chunk are
+    // software-pipelined table reads: the next chunk is claimed and its entries
     // requested before the current chunk's tiles are issued
-    int nslot = -1, nstate = 2, nlen = 0;
-    if (b0 + lane < b1) {
-      nslot = __ldg(trow + b0 + lane);
-      nstate = __ldg(srow + b0 + lane);
-      nlen = __ldg(lrow + b0 + lane);
-    }
-    for (int base = b0; base < b1 && !fail; base += 32) {
+    while (chunk < n_chunks && !fail) {
+      const int base = 32 * chunk;
       const int i = base + lane;
       const int slot = nslot;
       const int st = nstate;
       const int len = max(0, min(nlen, BS));
-      if (base + 32 + lane < b1) {
-        nslot = __ldg(trow + base + 32 + lane);
-        nstate = __ldg(srow + base + 32 + lane);
-        nlen = __ldg(lrow + base + 32 + lane);
+      if (dynamic) {
+        int c = 0;
+        if (lane == 0) c = (int)atomicAdd(chunk_ctr, 1u);
+        chunk = __shfl_sync(0xffffffffu, c, 0);
+      } else {
+        ++chunk;
       }
-      bool issue = (i < b1) && (st == 0 || st == 1) && len > 0;
+      if (chunk < n_chunks && 32 * chunk + lane < nb) {
+        nslot = __ldg(trow + 32 * chunk + lane);
+        nstate = __ldg(srow + 32 * chunk + lane);
+        nlen = __ldg(lrow + 32 * chunk + lane);
+      }
+      bool issue = (i < nb) && (st == 0 || st == 1) && len > 0;
       if (issue) {
         const int64_t cap = (st == 0) ? p.hot_slots : p.warm_slots;
         if (slot < 0 || (int64_t)slot >= cap) {
@@ -246,7 +273,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           atomicOr(p.err, 0x1u);
         }
       }
-      if (i < b1 && !issue) {
+      if (i < nb && !issue) {
         cold += len;
         if (p.lse_blk != nullptr) {
           const float v = len > 0 ? logf((float)len) : -INFINITY;
@@ -706,7 +733,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   }
   __syncthreads();
   if (misc[1] == 0) return;
-  if (threadIdx.x == 0) atomicExch(&p.counters[(size_t)seq * p.kv_heads + kvh], 0u);
+  if (threadIdx.x == 0) {  // every CTA of this unit is done claiming chunks
+    atomicExch(&p.counters[unit], 0u);
+    atomicExch(chunk_ctr, 0u);
+  }
   __threadfence();
   float* wsl = reinterpret_cast<float*>(stages);          // [G][nsplit] weights
   float* hm = wsl + kMaxGroups * kMaxSplits;              // [G] max, [G] sum
@@ -736,17 +766,49 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     wsl[e] = (M != -INFINITY && S > 0.f) ? ex2((wsl[e] - M) * kLog2e) / S : 0.f;
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < G * D; e += Cfg::kThreads) {
-    const int h = e / D;
-    const int d = e - h * D;
+  // One warp per head: lane owns 4 dims (a float4 of every split's row) and,
+  // for head_dim 64, every other split; the split loop keeps 8 independent
+  // 16-byte loads in flight.
+  constexpr int kVecs = D / 4;                 // float4 per partial row
+  constexpr int kLanesPerRow = kVecs < 32 ? kVecs : 32;
+  constexpr int kSplitLanes = 32 / kLanesPerRow;
+  for (int h = warp; h < G; h += Cfg::kThreads / 32) {
     const size_t row = row0 + h;
-    float o = 0.f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float w = wsl[h * nsplit + sp];
-      if (w != 0.f) o += w * __ldcg(p.part_o + (row * nsplit + sp) * D + d);
+    const int v = lane % kLanesPerRow;
+    const int sp0 = lane / kLanesPerRow;
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + row * nsplit * D) + v;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    int sp = sp0;
+    for (; sp + 7 * kSplitLanes < nsplit; sp += 8 * kSplitLanes) {
+      float4 x[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = __ldcg(src + (size_t)(sp + k * kSplitLanes) * kVecs);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float w = wsl[h * nsplit + sp + k * kSplitLanes];
+        o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
+      }
     }
-    store_out(p.out, p.out_dtype, row * D + d, o);
-    if (d == 0) {
+    for (; sp < nsplit; sp += kSplitLanes) {
+      const float4 x = __ldcg(src + (size_t)sp * kVecs);
+      const float w = wsl[h * nsplit + sp];
+      o.x += w * x.x; o.y += w * x.y; o.z += w * x.z; o.w += w * x.w;
+    }
+#pragma unroll
+    for (int off = kLanesPerRow; off < 32; off <<= 1) {
+      o.x += __shfl_xor_sync(0xffffffffu, o.x, off);
+      o.y += __shfl_xor_sync(0xffffffffu, o.y, off);
+      o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
+      o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
+    }
+    if (sp0 == 0) {
+      const size_t base = row * D + 4 * v;
+      store_out(p.out, p.out_dtype, base + 0, o.x);
+      store_out(p.out, p.out_dtype, base + 1, o.y);
+      store_out(p.out, p.out_dtype, base + 2, o.z);
+      store_out(p.out, p.out_dtype, base + 3, o.w);
+    }
+    if (lane == 0) {
       const float M = hm[h], S = hm[kMaxGroups + h];
       const float lse = (M != -INFINITY && S > 0.f) ? M + logf(S) : -INFINITY;
       if (p.out_lse) p.out_lse[row] = lse;
@@ -761,12 +823,16 @@ static cudaError_t launch_one(const DecodeParams& p, const CUtensorMap maps[4],
                               cudaStream_t stream) {
   using Cfg = DecodeCfg<D, BS, FMT, QT>;
   auto kern = decode_kernel<D, BS, FMT, QT>;
-  static bool attr_set = false;  // per-process; the attribute is per function
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  // the shared-memory opt-in is per function and device; set it once per device
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t(1) << dev) : 0;
+  if (!bit || !(attr_set.load(std::memory_order_relaxed) & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set.fetch_or(bit, std::memory_order_relaxed);
   }
   dim3 grid(p.splits, p.kv_heads, p.batch);
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p, maps[0], maps[1], maps[2], maps[3]);

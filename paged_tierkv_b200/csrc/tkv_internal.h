@@ -11,6 +11,11 @@
 #define TKV_HOT_3D 1
 #endif
 
+// Split planner: fixed cost of one decode CTA expressed in blocks of work.
+#ifndef TKV_CTA_OVERHEAD_BLOCKS
+#define TKV_CTA_OVERHEAD_BLOCKS 16
+#endif
+
 namespace tkv {
 
 constexpr int kFmtR = 0;
@@ -38,7 +43,8 @@ struct DecodeParams {
   float* out_lse;             // optional [batch, num_heads]
   float* part_o;              // [batch*num_heads, splits, D] (splits > 1)
   float* part_lse;            // [batch*num_heads, splits]
-  uint32_t* counters;         // [batch*kv_heads] self-resetting split tickets
+  uint32_t* counters;         // [2][batch*kv_heads] split tickets, then chunk counters
+                              // (both reset by the last CTA of each sequence/kv head)
   float* lse_blk;             // optional [batch*num_heads, max_blocks]: per-block LSE
   float* lse_final;           // optional [batch*num_heads]: final LSE for the score pass
   uint32_t* err;              // device error bits

@@ -104,7 +104,19 @@ class TieredPools:
                    torch.ones(meta, dtype=torch.float32, device=device), None,
                    torch.ones(meta, dtype=torch.float32, device=device), None, FORMAT_S)
 
+    def _key(self):
+        return tuple(id(getattr(self, n)) for n in ("hot_k", "hot_v", "warm_k", "warm_v", "k_scale",
+                                                    "k_zero", "v_scale", "v_zero")) + (self.fmt,)
+
     def validate(self) -> None:
+        """Shape/dtype/layout checks; repeated calls on the same tensors are free."""
+        key = self._key()
+        if getattr(self, "_validated", None) == key:
+            return
+        self._validate()
+        object.__setattr__(self, "_validated", key)
+
+    def _validate(self) -> None:
         hk = self.hot_k
         if hk.ndim != 4:
             raise ValueError("hot pools must have shape [slots, kv_heads, block_size, head_dim].")
