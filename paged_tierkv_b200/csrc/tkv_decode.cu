@@ -54,6 +54,11 @@ struct TileInfo {
 #ifndef TKV_MIN_CTAS
 #define TKV_MIN_CTAS 4
 #endif
+// A consumer hands its stage back as soon as the tile's V fragments are in
+// registers (before the softmax and the PV products) instead of at the end.
+#ifndef TKV_EARLY_RELEASE
+#define TKV_EARLY_RELEASE 1
+#endif
 
 template <int D, int BS, int FMT, int QT>
 struct DecodeCfg {
@@ -67,15 +72,21 @@ struct DecodeCfg {
   static constexpr int kKS = D / 16;                      // 16-wide steps over head_dim
   static constexpr int kSub = BS / 16;                    // 16-token sub-tiles per block
   static constexpr int kWarmSwz = (D == 128) ? 7 : 3;     // SWIZZLE_128B / SWIZZLE_64B
-  // layout of dynamic shared memory (after aligning the base to 1024)
+  // layout of dynamic shared memory (after aligning the base to 1024); bulk
+  // copy destinations (the meta area) must start on 16-byte boundaries
+  static constexpr int align_to(int x, int a) { return (x + a - 1) / a * a; }
   static constexpr int kOffBars = kStages * kStageBytes;
-  static constexpr int kOffInfo = kOffBars + 2 * kStages * 8;
-  static constexpr int kOffMeta = kOffInfo + kStages * (int)sizeof(TileInfo);
-  static constexpr int kOffMisc = kOffMeta + kStages * kMetaBytes;
+  static constexpr int kOffInfo = align_to(kOffBars + 2 * kStages * 8, 16);
+  static constexpr int kOffMeta = align_to(kOffInfo + kStages * (int)sizeof(TileInfo), 128);
+  static constexpr int kOffMisc = align_to(kOffMeta + kStages * kMetaBytes, 16);
+  static_assert(kOffMeta % 128 == 0 && kMetaBytes % 16 == 0 && (BS * 2) % 16 == 0,
+                "every meta bulk-copy destination must be 16-byte aligned");
+  static_assert(kStageBytes % 1024 == 0 && kHotBytes % 1024 == 0,
+                "swizzled TMA boxes need 1024-byte aligned destinations");
   // query of the GQA group, fp16, twice: standard d order (HOT K) and the
   // permuted order of the register-expanded WARM K; rows padded by 16 bytes
   static constexpr int kQStride = D + 8;
-  static constexpr int kOffQ = kOffMisc + 64;
+  static constexpr int kOffQ = kOffMisc + 128;  // misc: 32 words
   static constexpr int kQBytes = kMaxGroups * kQStride * 2;
   static constexpr int kSmemBytes = 1024 + kOffQ + 2 * kQBytes;
   // the end-of-kernel merge scratch aliases the stage ring
@@ -105,7 +116,8 @@ __device__ __forceinline__ uint32_t ld_u32(const void* p) {
 //                   t the dims t*D/4 + 4s + {0,1} (b0) and + {2,3} (b1), the
 //                   order of the register-expanded WARM K codes
 // bf16 queries are rescaled per head by 2^-e (exact) so they fit fp16; the
-// factor 2^e is returned through sexp and folded into the logit scale.
+// factor 2^e is returned through sexp[0..8) and folded into the logit scale;
+// sexp[8..16) receives the per-head sums of the staged values as floats.
 template <int D, int QT, int NT>
 __device__ __forceinline__ void stage_query(const DecodeParams& p, int seq, int kvh,
                                             __half* sqh, __half* sqw, int* sexp) {
@@ -150,6 +162,16 @@ __device__ __forceinline__ void stage_query(const DecodeParams& p, int seq, int 
     sqw[n * QS + 16 * s + 2 * tq + (j & 1) + 8 * (j >> 1)] = h;
   }
   __syncthreads();
+  // per-head sum of the staged fp16 values (the WARM K zero-point correction)
+  float* qsum = reinterpret_cast<float*>(sexp + 8);
+  for (int n = warp; n < kMaxGroups; n += NT / 32) {
+    float sum = 0.f;
+    for (int d = lane; d < D; d += 32) sum += __half2float(sqh[n * QS + d]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) qsum[n] = sum;
+  }
+  __syncthreads();
 }
 
 // B fragments (k = head_dim, n = query head) of k-steps 2m and 2m+1 from a
@@ -180,7 +202,9 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   uint64_t* empty_bar = full_bar + Cfg::kStages;
   TileInfo* info = reinterpret_cast<TileInfo*>(smem + Cfg::kOffInfo);
   uint8_t* meta = smem + Cfg::kOffMeta;
-  int* misc = reinterpret_cast<int*>(smem + Cfg::kOffMisc);  // [0] cold, [1] last CTA, [8..16) exp
+  // misc: [0] cold tokens, [1] last-CTA flag, [8..16) query exponents,
+  // [16..24) per-head sums of the staged fp16 query (as float bits)
+  int* misc = reinterpret_cast<int*>(smem + Cfg::kOffMisc);
   __half* sqh = reinterpret_cast<__half*>(smem + Cfg::kOffQ);
   __half* sqw = reinterpret_cast<__half*>(smem + Cfg::kOffQ + Cfg::kQBytes);
 
@@ -374,8 +398,8 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   // ------------------------------------------------------------ consumers
   float m2[2] = {-INFINITY, -INFINITY};  // running max (log2 domain), heads 2t, 2t+1
   float l[2] = {0.f, 0.f};               // this lane's share of the denominator
-  // O^T accumulator; m-tile 4kk+i holds rows d = 64kk + 4g + i (row g) and
-  // 64kk + 32 + 4g + i (row g+8), columns = heads 2t, 2t+1
+  // O^T accumulator; m-tile 4kk+i holds rows d = 64kk + 8g + i (row g) and
+  // 64kk + 8g + 4 + i (row g+8), columns = heads 2t, 2t+1
   float acc[Cfg::kKS][4];
 #pragma unroll
   for (int i = 0; i < Cfg::kKS; ++i)
@@ -388,9 +412,15 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     const int cw = warp - 1;
     const uint32_t sqh_u = smem_u32(sqh);
     const uint32_t sqw_u = smem_u32(sqw);
-    float qmul[2];  // logit scale (log2 domain) of heads 2t, 2t+1
+    float qmul[2], qsum[2];  // logit scale (log2 domain) and query sum of heads 2t, 2t+1
     qmul[0] = ldexpf(p.scale_log2, misc[8 + 2 * t]);
     qmul[1] = ldexpf(p.scale_log2, misc[8 + 2 * t + 1]);
+    qsum[0] = __int_as_float(misc[16 + 2 * t]);
+    qsum[1] = __int_as_float(misc[16 + 2 * t + 1]);
+    // Lazy rescaling: the running max only moves when a logit exceeds it by
+    // more than 2^8 (log2 domain), so P stays <= 256 and most tiles skip the
+    // cross-lane max and the accumulator rescale.
+    constexpr float kLazy = 8.f;
 
     for (int it = cw;; it += Cfg::kConsumers) {
       const int s = it % Cfg::kStages;
@@ -439,23 +469,21 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           x[u][3] = (x[u][3] + xa[3]) * qmul[1];
         }
       } else {
+        // codes enter the tensor cores as exact fp16 (1024 + code); the zero
+        // point comes out as logit = s * (sum((1024 + q) Q) - (1024 + z) sum(Q))
 #pragma unroll
         for (int u = 0; u < Cfg::kSub; ++u) {
           const int r0 = 16 * u + g;
           const int r1 = r0 + 8;
-          float sc0, sc1;
-          uint32_t z0, z1;
+          float sc0, sc1, zc0, zc1;
           if (FMT == kFmtR) {
             sc0 = __half2float(ms[r0]);
             sc1 = __half2float(ms[r1]);
-            const __half o1024 = __float2half_rn(1024.f);
-            const __half h0 = __hadd(ms[BS + r0], o1024);
-            const __half h1 = __hadd(ms[BS + r1], o1024);
-            z0 = (uint32_t)__half_as_ushort(h0) * 0x10001u;
-            z1 = (uint32_t)__half_as_ushort(h1) * 0x10001u;
+            zc0 = 1024.f + __half2float(ms[BS + r0]);
+            zc1 = 1024.f + __half2float(ms[BS + r1]);
           } else {
             sc0 = sc1 = ti.ks;
-            z0 = z1 = 0x64806480u;  // (1152, 1152): 1024 + 128 offset of flipped int8
+            zc0 = zc1 = 1152.f;  // 1024 + 128: int8 codes are flipped to biased bytes
           }
           uint32_t w0[Cfg::kKS], w1[Cfg::kKS];
 #pragma unroll
@@ -479,64 +507,124 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
                 c0 ^= 0x80808080u;
                 c1 ^= 0x80808080u;
               }
-              const uint32_t a0 = hsub2_u32(__byte_perm(c0, kMagic, 0x4140), z0);
-              const uint32_t a2 = hsub2_u32(__byte_perm(c0, kMagic, 0x4342), z0);
-              const uint32_t a1 = hsub2_u32(__byte_perm(c1, kMagic, 0x4140), z1);
-              const uint32_t a3 = hsub2_u32(__byte_perm(c1, kMagic, 0x4342), z1);
+              const uint32_t a0 = __byte_perm(c0, kMagic, 0x4140);
+              const uint32_t a2 = __byte_perm(c0, kMagic, 0x4342);
+              const uint32_t a1 = __byte_perm(c1, kMagic, 0x4140);
+              const uint32_t a3 = __byte_perm(c1, kMagic, 0x4342);
               if (kk)
                 mma_16816(xa, a0, a1, a2, a3, bq[1][0], bq[1][1]);
               else
                 mma_16816(x[u], a0, a1, a2, a3, bq[0][0], bq[0][1]);
             }
           }
-          x[u][0] = (x[u][0] + xa[0]) * (qmul[0] * sc0);
-          x[u][1] = (x[u][1] + xa[1]) * (qmul[1] * sc0);
-          x[u][2] = (x[u][2] + xa[2]) * (qmul[0] * sc1);
-          x[u][3] = (x[u][3] + xa[3]) * (qmul[1] * sc1);
+          x[u][0] = (x[u][0] + xa[0] - zc0 * qsum[0]) * (qmul[0] * sc0);
+          x[u][1] = (x[u][1] + xa[1] - zc0 * qsum[1]) * (qmul[1] * sc0);
+          x[u][2] = (x[u][2] + xa[2] - zc1 * qsum[0]) * (qmul[0] * sc1);
+          x[u][3] = (x[u][3] + xa[3] - zc1 * qsum[1]) * (qmul[1] * sc1);
         }
       }
 
+      // ---- V fragments to registers; then the stage can be handed back.
+      // Lane (g, t) needs dims 64kk + 8g .. +7 of tokens 2t, 2t+1, 2t+8, 2t+9:
+      // one 16-byte load per token (HOT fp16) or one 8-byte load (WARM codes,
+      // plus the per-token V scale and (1024 + zero)).
+      uint32_t vf[Cfg::kSub][D / 64][16];
+      float vsc[Cfg::kSub][2];
+      uint32_t vzp[Cfg::kSub][2];
+      if (hot) {
+#pragma unroll
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          const int r0 = 16 * u + 2 * t;
+#pragma unroll
+          for (int kk = 0; kk < D / 64; ++kk) {
+            const int rr[4] = {r0, r0 + 1, r0 + 8, r0 + 9};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 v = lds128(vb + swz<7>((kk * BS + rr[j]) * 128 + 16 * g));
+              vf[u][kk][4 * j + 0] = v.x;
+              vf[u][kk][4 * j + 1] = v.y;
+              vf[u][kk][4 * j + 2] = v.z;
+              vf[u][kk][4 * j + 3] = v.w;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < Cfg::kSub; ++u) {
+          const int r0 = 16 * u + 2 * t;
+          if (FMT == kFmtR) {
+            vsc[u][0] = __half2float(ms[2 * BS + 16 * u + g]);
+            vsc[u][1] = __half2float(ms[2 * BS + 16 * u + g + 8]);
+            const __half o1024 = __float2half_rn(1024.f);
+            const __half* vz = ms + 3 * BS;
+            vzp[u][0] = (uint32_t)__half_as_ushort(__hadd(vz[r0], o1024)) |
+                        ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 1], o1024)) << 16);
+            vzp[u][1] = (uint32_t)__half_as_ushort(__hadd(vz[r0 + 8], o1024)) |
+                        ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 9], o1024)) << 16);
+          } else {
+            vsc[u][0] = vsc[u][1] = ti.vs;
+            vzp[u][0] = vzp[u][1] = 0x64806480u;
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 64; ++kk) {
+            const int rr[4] = {r0, r0 + 1, r0 + 8, r0 + 9};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint2 v = lds64(vb + swz<Cfg::kWarmSwz>(rr[j] * D + 64 * kk + 8 * g));
+              vf[u][kk][2 * j] = v.x;
+              vf[u][kk][2 * j + 1] = v.y;
+            }
+          }
+        }
+      }
+#if TKV_EARLY_RELEASE
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+#endif
+
       // ---- mask tokens >= len, online softmax (log2 domain)
-      float mt[2] = {-INFINITY, -INFINITY};
+      float lm[2] = {-INFINITY, -INFINITY};
 #pragma unroll
       for (int u = 0; u < Cfg::kSub; ++u) {
         if (16 * u + g >= ti.len) x[u][0] = x[u][1] = -INFINITY;
         if (16 * u + g + 8 >= ti.len) x[u][2] = x[u][3] = -INFINITY;
-        mt[0] = fmaxf(mt[0], fmaxf(x[u][0], x[u][2]));
-        mt[1] = fmaxf(mt[1], fmaxf(x[u][1], x[u][3]));
+        lm[0] = fmaxf(lm[0], fmaxf(x[u][0], x[u][2]));
+        lm[1] = fmaxf(lm[1], fmaxf(x[u][1], x[u][3]));
       }
+      const bool grow = lm[0] > m2[0] + kLazy || lm[1] > m2[1] + kLazy;
+      if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        mt[0] = fmaxf(mt[0], __shfl_xor_sync(0xffffffffu, mt[0], off));
-        mt[1] = fmaxf(mt[1], __shfl_xor_sync(0xffffffffu, mt[1], off));
-      }
-      float mnew[2], alpha[2];
+        for (int off = 4; off < 32; off <<= 1) {
+          lm[0] = fmaxf(lm[0], __shfl_xor_sync(0xffffffffu, lm[0], off));
+          lm[1] = fmaxf(lm[1], __shfl_xor_sync(0xffffffffu, lm[1], off));
+        }
+        float alpha[2];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        mnew[j] = fmaxf(m2[j], mt[j]);
-        alpha[j] = ex2(m2[j] - mnew[j]);
-        m2[j] = mnew[j];
-      }
-      float pr[Cfg::kSub][4];
-      float ps[2] = {0.f, 0.f};
-#pragma unroll
-      for (int u = 0; u < Cfg::kSub; ++u) {
-        pr[u][0] = ex2(x[u][0] - mnew[0]);
-        pr[u][1] = ex2(x[u][1] - mnew[1]);
-        pr[u][2] = ex2(x[u][2] - mnew[0]);
-        pr[u][3] = ex2(x[u][3] - mnew[1]);
-        ps[0] += pr[u][0] + pr[u][2];
-        ps[1] += pr[u][1] + pr[u][3];
-      }
-      l[0] = l[0] * alpha[0] + ps[0];
-      l[1] = l[1] * alpha[1] + ps[1];
-      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+        for (int j = 0; j < 2; ++j) {
+          const float mn = fmaxf(m2[j], lm[j]);
+          alpha[j] = ex2(m2[j] - mn);
+          m2[j] = mn;
+          l[j] *= alpha[j];
+        }
 #pragma unroll
         for (int i = 0; i < Cfg::kKS; ++i) {
           acc[i][0] *= alpha[0]; acc[i][1] *= alpha[1];
           acc[i][2] *= alpha[0]; acc[i][3] *= alpha[1];
         }
       }
+      float pr[Cfg::kSub][4];
+      float ps[2] = {0.f, 0.f};
+#pragma unroll
+      for (int u = 0; u < Cfg::kSub; ++u) {
+        pr[u][0] = ex2(x[u][0] - m2[0]);
+        pr[u][1] = ex2(x[u][1] - m2[1]);
+        pr[u][2] = ex2(x[u][2] - m2[0]);
+        pr[u][3] = ex2(x[u][3] - m2[1]);
+        ps[0] += pr[u][0] + pr[u][2];
+        ps[1] += pr[u][1] + pr[u][3];
+      }
+      l[0] += ps[0];
+      l[1] += ps[1];
       if (p.lse_blk != nullptr) {
         float bsum[2] = {ps[0], ps[1]};
 #pragma unroll
@@ -550,95 +638,55 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
             const int h = 2 * t + j;
             if (h < G)
               p.lse_blk[((size_t)seq * Hq + (size_t)kvh * G + h) * p.max_blocks + ti.block] =
-                  (mnew[j] + lg2(bsum[j])) * kLn2;
+                  (m2[j] + lg2(bsum[j])) * kLn2;
           }
         }
       }
 
-      // ---- O^T += V^T P^T
+      // ---- O^T += V^T P^T (V fragments are already in registers)
+      // m-tile 4kk+i: A rows g / g+8 are dims 64kk + 8g + i / + 4 + i, A columns
+      // are the token pairs (2t, 2t+1) and (2t+8, 2t+9).
       if (hot) {
-        uint32_t pb[Cfg::kSub][2];
 #pragma unroll
         for (int u = 0; u < Cfg::kSub; ++u) {
-          pb[u][0] = movmatrix_t(pack_half2(pr[u][0], pr[u][1]));
-          pb[u][1] = movmatrix_t(pack_half2(pr[u][2], pr[u][3]));
-        }
-        // V tile in shared memory: [D/64][BS][64] fp16, 128-byte swizzled lines.
-        // Lane (g, t) reads 4 dims of tokens 2t, 2t+1, 2t+8, 2t+9 with one
-        // 8-byte load each and pairs the tokens with byte permutes.
-#pragma unroll
-        for (int u = 0; u < Cfg::kSub; ++u) {
-          const int r0 = 16 * u + 2 * t;
+          const uint32_t pb0 = movmatrix_t(pack_half2(pr[u][0], pr[u][1]));
+          const uint32_t pb1 = movmatrix_t(pack_half2(pr[u][2], pr[u][3]));
 #pragma unroll
           for (int kk = 0; kk < D / 64; ++kk) {
-            const uint32_t line = kk * BS;
-            auto ld = [&](int r, int off) -> uint2 {
-              return lds64(vb + swz<7>((line + r) * 128 + off));
-            };
-            const uint2 l0 = ld(r0, 8 * g), l1 = ld(r0 + 1, 8 * g);
-            const uint2 l2 = ld(r0 + 8, 8 * g), l3 = ld(r0 + 9, 8 * g);
-            const uint2 h0 = ld(r0, 64 + 8 * g), h1 = ld(r0 + 1, 64 + 8 * g);
-            const uint2 h2 = ld(r0 + 8, 64 + 8 * g), h3 = ld(r0 + 9, 64 + 8 * g);
+            const uint32_t* f = vf[u][kk];  // token j: dims (0,1) (2,3) (4,5) (6,7) at 4j..4j+3
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
-              const uint32_t a0 = __byte_perm(i < 2 ? l0.x : l0.y, i < 2 ? l1.x : l1.y, sel);
-              const uint32_t a1 = __byte_perm(i < 2 ? h0.x : h0.y, i < 2 ? h1.x : h1.y, sel);
-              const uint32_t a2 = __byte_perm(i < 2 ? l2.x : l2.y, i < 2 ? l3.x : l3.y, sel);
-              const uint32_t a3 = __byte_perm(i < 2 ? h2.x : h2.y, i < 2 ? h3.x : h3.y, sel);
-              mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+              const int w = i >> 1;
+              const uint32_t a0 = __byte_perm(f[0 + w], f[4 + w], sel);
+              const uint32_t a1 = __byte_perm(f[2 + w], f[6 + w], sel);
+              const uint32_t a2 = __byte_perm(f[8 + w], f[12 + w], sel);
+              const uint32_t a3 = __byte_perm(f[10 + w], f[14 + w], sel);
+              mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb0, pb1);
             }
           }
         }
       } else {
-        uint32_t pb[Cfg::kSub][2];
 #pragma unroll
         for (int u = 0; u < Cfg::kSub; ++u) {
-          float vs0, vs1;
-          if (FMT == kFmtR) {
-            vs0 = __half2float(ms[2 * BS + 16 * u + g]);
-            vs1 = __half2float(ms[2 * BS + 16 * u + g + 8]);
-          } else {
-            vs0 = vs1 = ti.vs;
-          }
-          pb[u][0] = movmatrix_t(pack_half2(pr[u][0] * vs0, pr[u][1] * vs0));
-          pb[u][1] = movmatrix_t(pack_half2(pr[u][2] * vs1, pr[u][3] * vs1));
-        }
-#pragma unroll
-        for (int u = 0; u < Cfg::kSub; ++u) {
-          const int r0 = 16 * u + 2 * t;
-          uint32_t z01, z23;
-          if (FMT == kFmtR) {
-            const __half o1024 = __float2half_rn(1024.f);
-            const __half* vz = ms + 3 * BS;
-            z01 = (uint32_t)__half_as_ushort(__hadd(vz[r0], o1024)) |
-                  ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 1], o1024)) << 16);
-            z23 = (uint32_t)__half_as_ushort(__hadd(vz[r0 + 8], o1024)) |
-                  ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 9], o1024)) << 16);
-          } else {
-            z01 = z23 = 0x64806480u;
-          }
+          const uint32_t pb0 = movmatrix_t(pack_half2(pr[u][0] * vsc[u][0], pr[u][1] * vsc[u][0]));
+          const uint32_t pb1 = movmatrix_t(pack_half2(pr[u][2] * vsc[u][1], pr[u][3] * vsc[u][1]));
+          const uint32_t z01 = vzp[u][0], z23 = vzp[u][1];
 #pragma unroll
           for (int kk = 0; kk < D / 64; ++kk) {
-            const int lo = 64 * kk + 4 * g;
-            const int hi = lo + 32;
-            uint32_t wl0 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 0) * D + lo));
-            uint32_t wl1 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 1) * D + lo));
-            uint32_t wl2 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 8) * D + lo));
-            uint32_t wl3 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 9) * D + lo));
-            uint32_t wh0 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 0) * D + hi));
-            uint32_t wh1 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 1) * D + hi));
-            uint32_t wh2 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 8) * D + hi));
-            uint32_t wh3 = lds32(vb + swz<Cfg::kWarmSwz>((r0 + 9) * D + hi));
+            // token j: codes of dims 0..3 in word 2j, dims 4..7 in word 2j+1
+            uint32_t f[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) f[k] = vf[u][kk][k];
             if (FMT == kFmtS) {
-              wl0 ^= 0x80808080u; wl1 ^= 0x80808080u; wl2 ^= 0x80808080u; wl3 ^= 0x80808080u;
-              wh0 ^= 0x80808080u; wh1 ^= 0x80808080u; wh2 ^= 0x80808080u; wh3 ^= 0x80808080u;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) f[k] ^= 0x80808080u;
             }
             // interleave the two tokens of each k pair byte by byte
-            const uint32_t xl[2] = {__byte_perm(wl0, wl1, 0x5140), __byte_perm(wl0, wl1, 0x7362)};
-            const uint32_t xh[2] = {__byte_perm(wh0, wh1, 0x5140), __byte_perm(wh0, wh1, 0x7362)};
-            const uint32_t yl[2] = {__byte_perm(wl2, wl3, 0x5140), __byte_perm(wl2, wl3, 0x7362)};
-            const uint32_t yh[2] = {__byte_perm(wh2, wh3, 0x5140), __byte_perm(wh2, wh3, 0x7362)};
+            const uint32_t xl[2] = {__byte_perm(f[0], f[2], 0x5140), __byte_perm(f[0], f[2], 0x7362)};
+            const uint32_t xh[2] = {__byte_perm(f[1], f[3], 0x5140), __byte_perm(f[1], f[3], 0x7362)};
+            const uint32_t yl[2] = {__byte_perm(f[4], f[6], 0x5140), __byte_perm(f[4], f[6], 0x7362)};
+            const uint32_t yh[2] = {__byte_perm(f[5], f[7], 0x5140), __byte_perm(f[5], f[7], 0x7362)};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint32_t sel = (i & 1) ? 0x4342u : 0x4140u;
@@ -646,13 +694,15 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
               const uint32_t a1 = hsub2_u32(__byte_perm(xh[i >> 1], kMagic, sel), z01);
               const uint32_t a2 = hsub2_u32(__byte_perm(yl[i >> 1], kMagic, sel), z23);
               const uint32_t a3 = hsub2_u32(__byte_perm(yh[i >> 1], kMagic, sel), z23);
-              mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+              mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb0, pb1);
             }
           }
         }
       }
+#if !TKV_EARLY_RELEASE
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[s]);
+#endif
     }
   }
 
@@ -679,8 +729,8 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     for (int kk = 0; kk < D / 64; ++kk) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int dlo = 64 * kk + 4 * g + i;
-        const int dhi = dlo + 32;
+        const int dlo = 64 * kk + 8 * g + i;
+        const int dhi = dlo + 4;
         a[(2 * t) * D + dlo] = acc[4 * kk + i][0];
         a[(2 * t + 1) * D + dlo] = acc[4 * kk + i][1];
         a[(2 * t) * D + dhi] = acc[4 * kk + i][2];
