@@ -61,6 +61,10 @@ extern "C" {
 #define TKV_ERR_WORKSPACE      3  /* workspace missing or too small -> ValueError */
 #define TKV_ERR_CUDA           4  /* CUDA driver / launch failure -> RuntimeError */
 #define TKV_ERR_NO_DEVICE      5  /* no usable sm_100 device       -> RuntimeError */
+#define TKV_ERR_SCRATCH_LIMIT  6  /* call needs more than the fixed no-alloc scratch -> ValueError */
+
+/* Size of the library-owned device array used by tkv_decode_attention_noalloc. */
+#define TKV_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
 /* ---- enums --------------------------------------------------------------- */
 #define TKV_STATE_HOT   0
@@ -193,6 +197,26 @@ int32_t tkv_promote_to_hot(const tkv_pools* pools, const int32_t* src_warm_slots
 /* Reads and clears the device error bits (TKV_DEVERR_*) that decode calls
  * using this workspace have recorded.  Synchronizes the stream. */
 int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream);
+
+/* Decode attention for callers that cannot allocate device memory -- a serving
+ * runtime that has handed (nearly) all of HBM to its own pools and forbids side
+ * allocations, or a host that reaches this library only through this C ABI
+ * with no device-allocation binding of its own.  Same arguments and results as
+ * tkv_decode_attention, except that args->workspace / workspace_bytes are
+ * ignored: the scratch (split partials, split tickets, chunk counters, score
+ * scratch) lives in a library-owned device array of TKV_NOALLOC_SCRATCH_BYTES
+ * that every GPU loading the library holds until the process exits.  The call
+ * itself allocates nothing (no cudaMalloc/cudaFree, no allocating library
+ * routine); it clears the counters it needs on `stream` before the launch.
+ * Calls whose tkv_decode_plan() workspace exceeds the array return
+ * TKV_ERR_SCRATCH_LIMIT.  The first call on each device looks up the array's
+ * device address with cudaGetSymbolAddress while that device is current; make
+ * that first call before any stream capture.  All calls on a device share the
+ * one array, so calls that overlap on the GPU (different streams, or different
+ * host threads) race and must be serialised by the caller.
+ * No counterpart in the reference (its wrapper allocates with torch). */
+int32_t tkv_decode_attention_noalloc(const tkv_pools* pools, const tkv_decode_args* args,
+                                     void* stream);
 
 #ifdef __cplusplus
 }

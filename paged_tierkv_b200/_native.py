@@ -18,6 +18,8 @@ TKV_ERR_UNSUPPORTED = 2
 TKV_ERR_WORKSPACE = 3
 TKV_ERR_CUDA = 4
 TKV_ERR_NO_DEVICE = 5
+TKV_ERR_SCRATCH_LIMIT = 6
+TKV_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 TKV_FORMAT_R = 0
 TKV_FORMAT_S = 1
@@ -39,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "tkv_demote_to_warm",
     "tkv_promote_to_hot",
     "tkv_read_device_errors",
+    "tkv_decode_attention_noalloc",
 )
 
 
@@ -122,6 +125,8 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
         "tkv_demote_to_warm": ([ctypes.POINTER(TkvPools), vp, vp, vp, i32, i32, vp], i32),
         "tkv_promote_to_hot": ([ctypes.POINTER(TkvPools), vp, vp, vp, i32, vp], i32),
         "tkv_read_device_errors": ([vp, ctypes.POINTER(ctypes.c_uint32), vp], i32),
+        "tkv_decode_attention_noalloc": ([ctypes.POINTER(TkvPools), ctypes.POINTER(TkvDecodeArgs),
+                                          vp], i32),
     }
     for name, (argtypes, restype) in sigs.items():
         fn = getattr(lib, name)
@@ -140,6 +145,6 @@ def check(status: int, what: str) -> None:
     if status == TKV_OK:
         return
     msg = load().tkv_status_string(status).decode()
-    if status in (TKV_ERR_INVALID, TKV_ERR_UNSUPPORTED, TKV_ERR_WORKSPACE):
+    if status in (TKV_ERR_INVALID, TKV_ERR_UNSUPPORTED, TKV_ERR_WORKSPACE, TKV_ERR_SCRATCH_LIMIT):
         raise ValueError(f"{what}: {msg}")
     raise TierKVError(f"{what}: {msg} (status {status})")

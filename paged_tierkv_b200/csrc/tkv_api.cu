@@ -233,6 +233,9 @@ const char* tkv_status_string(int32_t status) {
     case TKV_ERR_WORKSPACE: return "workspace missing or smaller than tkv_decode_plan() requires";
     case TKV_ERR_CUDA: return "CUDA error while encoding or launching";
     case TKV_ERR_NO_DEVICE: return "no usable sm_100 (B200) device is current";
+    case TKV_ERR_SCRATCH_LIMIT:
+      return "call needs more scratch than the library's fixed array (TKV_NOALLOC_SCRATCH_BYTES); "
+             "use tkv_decode_attention with a caller workspace";
     default: return "unknown status";
   }
 }
@@ -448,3 +451,66 @@ int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode without a caller workspace.
+//
+// Some callers cannot allocate device memory: a serving runtime that has
+// already handed (nearly) all of HBM to its own KV-cache pools and forbids side
+// allocations, or a host that reaches this library only through the C ABI with
+// no device-allocation binding.  For them the split partials, split tickets,
+// chunk counters and score scratch live in this fixed array instead.  Every
+// GPU that loads the library holds TKV_NOALLOC_SCRATCH_BYTES of it until the
+// process exits.  Host code must not use `g_tkv_noalloc_scratch` as a device
+// address (on the host the name is only a stand-in); its device address is
+// looked up per device with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------
+namespace {
+
+__device__ __align__(256) uint8_t g_tkv_noalloc_scratch[TKV_NOALLOC_SCRATCH_BYTES];
+
+// Device address of the scratch array on the current device, resolved on the
+// first call made while that device is current.
+int32_t noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TKV_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tkv_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return TKV_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return TKV_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t tkv_decode_attention_noalloc(const tkv_pools* pools,
+                                                const tkv_decode_args* args, void* stream) {
+  if (!args) return TKV_ERR_INVALID;
+  Plan plan;
+  int32_t st = make_plan(pools, args, &plan);
+  if (st != TKV_OK) return st;
+  if (plan.total > (size_t)TKV_NOALLOC_SCRATCH_BYTES) return TKV_ERR_SCRATCH_LIMIT;
+  int sms = 0;
+  st = current_device_sms(&sms);  // rejects devices that are not sm_100
+  if (st != TKV_OK) return st;
+  void* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st != TKV_OK) return st;
+  // The array keeps whatever the previous call left; the error word, split
+  // tickets and chunk counters must start at zero, so clear them first.
+  const size_t counters_end =
+      plan.off_counters + 2 * sizeof(uint32_t) * (size_t)args->batch * pools->kv_heads;
+  if (cudaMemsetAsync(scratch, 0, counters_end, reinterpret_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return TKV_ERR_CUDA;
+  tkv_decode_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = (size_t)TKV_NOALLOC_SCRATCH_BYTES;
+  return tkv_decode_attention(pools, &a, stream);
+}
