@@ -50,9 +50,10 @@ def parse():
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--sweep", action="store_true",
                     help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
-    ap.add_argument("--config", choices=["c5", "c4"], default="c5",
+    ap.add_argument("--config", choices=["c5", "c4", "demote"], default="c5",
                     help="c5: data-parallel batches (default); c4: one 131k-token context "
-                         "over 32 layers, sharded by block range across the GPUs")
+                         "over 32 layers, sharded by block range across the GPUs; demote: "
+                         "HOT->WARM demotion of 2^20 fp16 [16 x 128] tiles per GPU")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-graph", action="store_true",
                     help="c4: launch every layer from Python instead of replaying a CUDA graph")
@@ -467,6 +468,57 @@ def run_c4(a, rank, world, dist_on, device):
     print(json.dumps(line), flush=True)
 
 
+def run_demote(a, rank, world, dist_on, device):
+    """Configuration 5's demotion benchmark: 2^20 tiles of [16 x 128] fp16 N(0,1)
+    (one tile = one (block, kv head) K or V), i.e. 65536 blocks x 8 kv heads x
+    {K, V}, quantized bit-exactly (Format R) into the WARM pool in one launch.
+    Bytes per launch: 4 GiB read, 2 GiB codes + 64 MiB scale/zero written."""
+    from paged_tierkv_b200 import _native, ops
+    _native.load(build_if_missing=True)
+    blocks, hkv, bs, d = 65536, 8, 16, 128
+    pools = ops.TieredPools.allocate(blocks, blocks, hkv, bs, d, device)
+    gen = torch.Generator(device=device).manual_seed(11 + rank)
+    pools.hot_k.normal_(generator=gen)
+    pools.hot_v.normal_(generator=gen)
+    src = torch.arange(blocks, dtype=torch.int32, device=device)
+    dst = torch.flip(src, dims=[0]).contiguous()
+    lens = torch.full((blocks,), bs, dtype=torch.int32, device=device)
+    tiles = blocks * hkv * 2
+    bytes_per = tiles * bs * d * 2 + tiles * bs * d + tiles * bs * 2 * 2
+    for _ in range(a.warmup):
+        ops.demote_blocks_to_warm(pools, src, dst, lens)
+    steps = max(1, min(a.steps, 50))
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        starts[i].record()
+        ops.demote_blocks_to_warm(pools, src, dst, lens)
+        ends[i].record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t[0])
+    if rank != 0:
+        return
+    peak, kind = hbm_peak()
+    gbs = bytes_per / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "HOT->WARM demotion GB/s (2^20 fp16 [16 x 128] tiles, Format R)",
+        "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "dtype": "fp16->u8", "data": "synthetic N(0,1)",
+        "config": {"workload": "demote_2p20_tiles", "tiles": tiles, "bytes_per_launch": bytes_per},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_kind": kind},
+        "gpu_launches": steps,
+    }), flush=True)
+
+
 def main():
     a = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -487,6 +539,8 @@ def main():
             run_reference(a, rank)
         elif a.config == "c4":
             run_c4(a, rank, world, dist_on, device)
+        elif a.config == "demote":
+            run_demote(a, rank, world, dist_on, device)
         else:
             run_ours(a, rank, world, dist_on, device)
     finally:
