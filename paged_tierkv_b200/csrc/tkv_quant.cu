@@ -29,16 +29,25 @@ __device__ __forceinline__ void row_params(float mn, float mx, float& scale, flo
   zp = to_h(-rintf(to_h(__fdiv_rn(mn, s))));
 }
 
-// Code of one value (tierkv_policy.py:34).
-__device__ __forceinline__ uint32_t row_code(float x, float scale, float zp) {
-  const float r = rintf(to_h(__fdiv_rn(x, scale)));
-  const float s = to_h(r + zp);
-  if (s != s) return 0u;  // NaN casts to 0, as the reference's CUDA cast does
-  return (uint32_t)fminf(fmaxf(s, 0.f), 255.f);
+// fp16(fp32 x / s), the reference's `tensor / scale` (x, s fp16 values, s > 0
+// finite or 1).  q = x * RN(1/s) is within 2.5 fp32 ulps of RN(x / s), so
+// both round to the same fp16 value unless q lies within 3 ulps of an fp16
+// rounding midpoint (fp32 mantissa bits [12:0] near 0x1000) or outside the
+// range where fp16 is normal; only those take the IEEE division.
+__device__ __forceinline__ __half div_to_half(float x, float s, float r) {
+  const float q = __fmul_rn(x, r);
+  const uint32_t b = __float_as_uint(q);
+  const uint32_t e = (b >> 23) & 0xffu;
+  const bool fast = e >= 113u && e <= 141u && ((b - 0x0ffdu) & 0x1fffu) > 6u;
+  return __float2half_rn(fast ? q : __fdiv_rn(x, s));
 }
 
 // Quantizes one row held as 8 fp16 values per lane over LPR lanes; returns
-// the 8 codes packed in a uint2 and the row's scale / zero point.
+// the 8 codes packed in a uint2 and the row's scale / zero point
+// (tierkv_policy.py:34: uint8(clamp(h(rint(h(x / scale)) + zp), 0, 255))).
+// After the division every step is exact in fp16: rint, the sum of two
+// integers, the clamp (a NaN row gives code 0, as the reference's CUDA cast
+// does), and +1024 leaves the code in the low byte.
 template <int LPR>
 __device__ __forceinline__ uint2 quant_row(const uint4 raw, __half& hs, __half& hz) {
   const __half* h = reinterpret_cast<const __half*>(&raw);
@@ -62,11 +71,22 @@ __device__ __forceinline__ uint2 quant_row(const uint4 raw, __half& hs, __half& 
   row_params(mn, mx, scale, zp);
   hs = __float2half_rn(scale);
   hz = __float2half_rn(zp);
+  const float rcp = __frcp_rn(scale);
+  const __half2 zp2 = __half2half2(hz);
+  const __half2 lo2 = __float2half2_rn(0.f);
+  const __half2 hi2 = __float2half2_rn(255.f);
+  const __half2 bias2 = __float2half2_rn(1024.f);
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 t = __halves2half2(div_to_half(v[2 * i], scale, rcp),
+                                     div_to_half(v[2 * i + 1], scale, rcp));
+    const __half2 c = __hadd2(__hmin2(__hmax2(__hadd2(h2rint(t), zp2), lo2), hi2), bias2);
+    w[i] = *reinterpret_cast<const uint32_t*>(&c);
+  }
   uint2 out;
-  out.x = row_code(v[0], scale, zp) | (row_code(v[1], scale, zp) << 8) |
-          (row_code(v[2], scale, zp) << 16) | (row_code(v[3], scale, zp) << 24);
-  out.y = row_code(v[4], scale, zp) | (row_code(v[5], scale, zp) << 8) |
-          (row_code(v[6], scale, zp) << 16) | (row_code(v[7], scale, zp) << 24);
+  out.x = __byte_perm(w[0], w[1], 0x6420);
+  out.y = __byte_perm(w[2], w[3], 0x6420);
   return out;
 }
 
