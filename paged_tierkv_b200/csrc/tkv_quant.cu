@@ -6,9 +6,11 @@
 // Every step is one PyTorch fp16 op: evaluated in fp32, rounded to nearest-even
 // fp16; torch.round is round-half-even (rintf).
 //
-// These kernels move bytes: one row of head_dim fp16 values is split over
-// head_dim/8 lanes that each load 16 bytes, so a warp reads 512 contiguous
-// bytes per step.  Rows are independent; the grid strides over rows.
+// These kernels move bytes: one row of head_dim fp16 values is split over a
+// few lanes that each load several 16-byte chunks before computing (memory
+// parallelism), and the per-element work is one multiply by the scale's
+// reciprocal plus exact fp16 steps.  Rows are independent; the grid strides
+// over rows.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -16,62 +18,71 @@
 
 namespace tkv {
 
-__device__ __forceinline__ float hmin_nan(float a, float b) { return (a != a || a < b) ? a : b; }
-__device__ __forceinline__ float hmax_nan(float a, float b) { return (a != a || a > b) ? a : b; }
 __device__ __forceinline__ float to_h(float x) { return __half2float(__float2half_rn(x)); }
 
-// Scale and zero point of one row (tierkv_policy.py:25-33).
-__device__ __forceinline__ void row_params(float mn, float mx, float& scale, float& zp) {
+// fp16(x / s) of the reference (PyTorch divides two fp16 tensors in fp32 and
+// rounds to fp16: RN16(RN32(x / s))) computed as RN16(x * RN32(1/s)).  The two
+// agree for all fp16 x and s > 0 whenever |x / s| >= 2^-14:
+//  * x / s is never an fp16 rounding midpoint there: a midpoint is K * 2^c with
+//    K odd in [2^11, 2^12), so x = K * 2^c * s would need an odd significand
+//    factor >= 2049 in x, whose significand has 11 bits;
+//  * it is more than 2 fp32 ulps from every midpoint: |x - M s| is a nonzero
+//    multiple of 2^(c + exponent of s's last bit), i.e. |x / s - M| > 2^c / 2^11
+//    = 2 ulp32(M);
+//  * q = RN32(x * RN32(1/s)) is within 1.5 ulp32 of x / s (the reciprocal adds
+//    at most 2^-24 relative error, the product rounding half an ulp), and so is
+//    RN32(x / s) (half an ulp): no midpoint separates them from x / s.
+// Below 2^-14 (fp16 subnormal results) only the sign matters to the callers:
+// they round the quotient to an integer, and |q| < 0.25 rounds to a zero of
+// q's sign either way.  Infinities and NaNs propagate as in the division
+// (s = +inf gives r = 0 and x * 0 = x / inf for finite x).
+__device__ __forceinline__ float div_by(float x, float r) { return __fmul_rn(x, r); }
+
+constexpr float kInv255 = 1.0f / 255.0f;  // RN32(1/255)
+
+// Scale, zero point and the scale's reciprocal of one row (tierkv_policy.py:25-33):
+// scale = h(h(max - min) / 255), 1 where that is 0; zp = h(-rint(h(min / scale))).
+__device__ __forceinline__ void row_params(float mn, float mx, float& scale, float& zp,
+                                           float& rcp) {
   const float diff = to_h(mx - mn);
-  float s = to_h(__fdiv_rn(diff, 255.0f));
+  float s = to_h(div_by(diff, kInv255));
   if (s == 0.f) s = 1.f;
   scale = s;
-  zp = to_h(-rintf(to_h(__fdiv_rn(mn, s))));
+  rcp = __frcp_rn(s);
+  zp = to_h(-rintf(to_h(div_by(mn, rcp))));
 }
 
-// fp16(fp32 x / s), the reference's `tensor / scale` (x, s fp16 values, s > 0
-// finite or 1).  q = x * RN(1/s) is within 2.5 fp32 ulps of RN(x / s), so
-// both round to the same fp16 value unless q lies within 3 ulps of an fp16
-// rounding midpoint (fp32 mantissa bits [12:0] near 0x1000) or outside the
-// range where fp16 is normal; only those take the IEEE division.
-__device__ __forceinline__ __half div_to_half(float x, float s, float r) {
-  const float q = __fmul_rn(x, r);
-  const uint32_t b = __float_as_uint(q);
-  const uint32_t e = (b >> 23) & 0xffu;
-  const bool fast = e >= 113u && e <= 141u && ((b - 0x0ffdu) & 0x1fffu) > 6u;
-  return __float2half_rn(fast ? q : __fdiv_rn(x, s));
+// Row minimum and maximum over V 16-byte chunks of fp16 per lane and LPR lanes
+// per row, NaN-propagating like torch.min / torch.max.  The pair travels as one
+// half2 (min, -max) so one shuffle and one min serve both per level.
+template <int LPR, int V>
+__device__ __forceinline__ void row_min_max(const uint4 (&raw)[V], float& mn, float& mx) {
+  const __half2* h = reinterpret_cast<const __half2*>(raw);
+  __half2 lo = h[0], hi = h[0];
+#pragma unroll
+  for (int j = 1; j < 4 * V; ++j) {
+    lo = __hmin2_nan(lo, h[j]);
+    hi = __hmax2_nan(hi, h[j]);
+  }
+  const __half2 nhi = __hneg2(hi);
+  __half2 m = __hmin2_nan(__lows2half2(lo, nhi), __highs2half2(lo, nhi));
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) {
+    uint32_t w = *reinterpret_cast<const uint32_t*>(&m);
+    w = __shfl_xor_sync(0xffffffffu, w, off);
+    m = __hmin2_nan(m, *reinterpret_cast<const __half2*>(&w));
+  }
+  mn = __low2float(m);
+  mx = -__high2float(m);
 }
 
-// Quantizes one row held as 8 fp16 values per lane over LPR lanes; returns
-// the 8 codes packed in a uint2 and the row's scale / zero point
+// Codes of one 16-byte chunk (8 fp16 values) packed in a uint2
 // (tierkv_policy.py:34: uint8(clamp(h(rint(h(x / scale)) + zp), 0, 255))).
 // After the division every step is exact in fp16: rint, the sum of two
 // integers, the clamp (a NaN row gives code 0, as the reference's CUDA cast
 // does), and +1024 leaves the code in the low byte.
-template <int LPR>
-__device__ __forceinline__ uint2 quant_row(const uint4 raw, __half& hs, __half& hz) {
-  const __half* h = reinterpret_cast<const __half*>(&raw);
-  float v[8];
-  float mn, mx;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __half2float(h[i]);
-  mn = v[0];
-  mx = v[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) {
-    mn = hmin_nan(mn, v[i]);
-    mx = hmax_nan(mx, v[i]);
-  }
-#pragma unroll
-  for (int off = LPR / 2; off > 0; off >>= 1) {
-    mn = hmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-    mx = hmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  }
-  float scale, zp;
-  row_params(mn, mx, scale, zp);
-  hs = __float2half_rn(scale);
-  hz = __float2half_rn(zp);
-  const float rcp = __frcp_rn(scale);
+__device__ __forceinline__ uint2 quant_chunk(const uint4 raw, float rcp, __half hz) {
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
   const __half2 zp2 = __half2half2(hz);
   const __half2 lo2 = __float2half2_rn(0.f);
   const __half2 hi2 = __float2half2_rn(255.f);
@@ -79,8 +90,8 @@ __device__ __forceinline__ uint2 quant_row(const uint4 raw, __half& hs, __half& 
   uint32_t w[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const __half2 t = __halves2half2(div_to_half(v[2 * i], scale, rcp),
-                                     div_to_half(v[2 * i + 1], scale, rcp));
+    const float2 f = __half22float2(h[i]);
+    const __half2 t = __floats2half2_rn(div_by(f.x, rcp), div_by(f.y, rcp));
     const __half2 c = __hadd2(__hmin2(__hmax2(__hadd2(h2rint(t), zp2), lo2), hi2), bias2);
     w[i] = *reinterpret_cast<const uint32_t*>(&c);
   }
@@ -90,31 +101,70 @@ __device__ __forceinline__ uint2 quant_row(const uint4 raw, __half& hs, __half& 
   return out;
 }
 
+// Lane layout shared by the row kernels: a row of D fp16 values is 2D bytes,
+// LPR lanes per row, lane `sub` holding the 16-byte chunks sub + LPR * v,
+// v < V = D / (8 LPR); load v of a warp then covers LPR * 16 contiguous bytes
+// of each of its 32 / LPR rows.
+template <int D, int LPR>
+struct RowLayout {
+  static constexpr int V = D / (8 * LPR);
+  static constexpr int RPW = 32 / LPR;
+  static_assert(V >= 1 && V * 8 * LPR == D, "head_dim must be a multiple of 8 * LPR");
+};
+
+// Lanes per row for head_dim D: TKV_QUANT_CHUNKS 16-byte chunks per lane, so
+// the per-row work (reduction, scale, zero point) is shared by few lanes.
+#ifndef TKV_QUANT_CHUNKS
+#define TKV_QUANT_CHUNKS 4
+#endif
+template <int D>
+__host__ __device__ constexpr int lanes_per_row() {
+  return (D / 8) / TKV_QUANT_CHUNKS < 1 ? 1 : (D / 8) / TKV_QUANT_CHUNKS;
+}
+
+// Quantizes the row this lane group holds and stores its codes (and, from the
+// group's first lane, the row's scale and zero point).
+template <int D, int LPR>
+__device__ __forceinline__ void quantize_store(const uint4 (&raw)[RowLayout<D, LPR>::V],
+                                               uint8_t* codes, __half* scale, __half* zero,
+                                               bool store, int sub) {
+  using L = RowLayout<D, LPR>;
+  float mn, mx, s, zp, rcp;
+  row_min_max<LPR, L::V>(raw, mn, mx);
+  row_params(mn, mx, s, zp, rcp);
+  const __half hz = __float2half_rn(zp);
+  if (!store) return;
+#pragma unroll
+  for (int v = 0; v < L::V; ++v)
+    *reinterpret_cast<uint2*>(codes + (sub + LPR * v) * 8) = quant_chunk(raw[v], rcp, hz);
+  if (sub == 0) {
+    *scale = __float2half_rn(s);
+    *zero = hz;
+  }
+}
+
 // ---------------------------------------------------------------- plain rows
-template <int LPR>
-__global__ void quantize_rows_kernel(const __half* __restrict__ x, int64_t rows,
-                                     uint8_t* __restrict__ codes, __half* __restrict__ scale,
-                                     __half* __restrict__ zero) {
-  constexpr int D = LPR * 8;
-  constexpr int RPW = 32 / LPR;  // rows per warp step
+template <int D>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const __half* __restrict__ x,
+                                                            int64_t rows,
+                                                            uint8_t* __restrict__ codes,
+                                                            __half* __restrict__ scale,
+                                                            __half* __restrict__ zero) {
+  constexpr int LPR = lanes_per_row<D>();
+  using L = RowLayout<D, LPR>;
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r0 = warp * RPW; r0 < rows; r0 += nwarps * RPW) {
+  for (int64_t r0 = warp * L::RPW; r0 < rows; r0 += nwarps * L::RPW) {
     const int64_t r = r0 + lane / LPR;
     const bool ok = r < rows;
-    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-    if (ok) raw = *reinterpret_cast<const uint4*>(x + r * D + sub * 8);
-    __half hs, hz;
-    const uint2 c = quant_row<LPR>(raw, hs, hz);
-    if (ok) {
-      *reinterpret_cast<uint2*>(codes + r * D + sub * 8) = c;
-      if (sub == 0) {
-        scale[r] = hs;
-        zero[r] = hz;
-      }
-    }
+    uint4 raw[L::V];
+    const __half* xp = x + r * D + sub * 8;
+#pragma unroll
+    for (int v = 0; v < L::V; ++v)
+      raw[v] = ok ? *reinterpret_cast<const uint4*>(xp + v * LPR * 8) : make_uint4(0u, 0u, 0u, 0u);
+    quantize_store<D, LPR>(raw, codes + r * D, scale + r, zero + r, ok, sub);
   }
 }
 
@@ -125,80 +175,85 @@ cudaError_t launch_quantize_rows(const void* x, int64_t rows, int dim, void* cod
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int threads = 256;
-  const int64_t rows_per_block = (threads / 32) * (32 / (dim / 8));
-  int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
-  blocks = blocks < (int64_t)sms * 16 ? blocks : (int64_t)sms * 16;
   auto* xs = reinterpret_cast<const __half*>(x);
   auto* cs = reinterpret_cast<uint8_t*>(codes);
   auto* ss = reinterpret_cast<__half*>(scale);
   auto* zs = reinterpret_cast<__half*>(zero);
+  auto grid = [&](int lpr) {
+    const int64_t per_block = (int64_t)threads / lpr;
+    const int64_t b = (rows + per_block - 1) / per_block;
+    return (unsigned)(b < (int64_t)sms * 16 ? b : (int64_t)sms * 16);
+  };
+#define TKV_QROWS(DIM)                                                                         \
+  case DIM:                                                                                    \
+    quantize_rows_kernel<DIM><<<grid(lanes_per_row<DIM>()), threads, 0, stream>>>(xs, rows, cs, \
+                                                                                  ss, zs);     \
+    break;
   switch (dim) {
-    case 16: quantize_rows_kernel<2><<<blocks, threads, 0, stream>>>(xs, rows, cs, ss, zs); break;
-    case 32: quantize_rows_kernel<4><<<blocks, threads, 0, stream>>>(xs, rows, cs, ss, zs); break;
-    case 64: quantize_rows_kernel<8><<<blocks, threads, 0, stream>>>(xs, rows, cs, ss, zs); break;
-    case 128: quantize_rows_kernel<16><<<blocks, threads, 0, stream>>>(xs, rows, cs, ss, zs); break;
-    case 256: quantize_rows_kernel<32><<<blocks, threads, 0, stream>>>(xs, rows, cs, ss, zs); break;
+    TKV_QROWS(16)
+    TKV_QROWS(32)
+    TKV_QROWS(64)
+    TKV_QROWS(128)
+    TKV_QROWS(256)
     default: return cudaErrorInvalidValue;
   }
+#undef TKV_QROWS
   return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------- demotion, Format R
-// Row r of the launch = (block i, tensor K/V, kv head, token t).  Rows with
-// t < length are quantized from the HOT slot into the WARM slot; tail rows are
-// cleared (code 0, scale 1, zero 0) only when clear_tail is set.
-template <int LPR>
-__global__ void demote_r_kernel(const DemoteParams p) {
-  constexpr int D = LPR * 8;
-  constexpr int RPW = 32 / LPR;
+// The launch's rows are r = (2 i + kind) * R + rr for demoted block i, tensor
+// kind (K = 0, V = 1) and rr = kv_head * block_size + t < R = kv_heads *
+// block_size: the R rows of one (block, tensor) are contiguous in both the HOT
+// slot and the WARM slot.  rows < 2^31 per launch (the host splits larger
+// calls), so the row arithmetic is 32-bit.  Rows with t < length are
+// quantized; tail rows are cleared (code 0, scale 1, zero 0) only when
+// clear_tail is set.
+template <int D>
+__global__ void __launch_bounds__(256) demote_r_kernel(const DemoteParams p, uint32_t rows) {
+  constexpr int LPR = lanes_per_row<D>();
+  using L = RowLayout<D, LPR>;
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;
-  const int bs = p.block_size;
-  const int64_t rows_per_block = 2LL * p.kv_heads * bs;
-  const int64_t rows = (int64_t)p.count * rows_per_block;
-  const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r0 = warp * RPW; r0 < rows; r0 += nwarps * RPW) {
-    const int64_t r = r0 + lane / LPR;
+  const uint32_t bs = (uint32_t)p.block_size;
+  const uint32_t R = (uint32_t)p.kv_heads * bs;
+  const uint32_t warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const uint32_t wstride = gridDim.x * (blockDim.x >> 5) * L::RPW;
+  for (uint32_t r0 = warp * L::RPW; r0 < rows; r0 += wstride) {
+    const uint32_t r = r0 + lane / LPR;
     bool ok = r < rows;
-    int i = 0, kind = 0, kvh = 0, t = 0, len = 0;
-    int64_t src = -1, dst = -1;
+    uint32_t rr = 0;
+    int kind = 0, len = 0;
+    int64_t src = 0, dst = 0;
     if (ok) {
-      i = (int)(r / rows_per_block);
-      int64_t rem = r - (int64_t)i * rows_per_block;
-      kind = (int)(rem / ((int64_t)p.kv_heads * bs));
-      rem -= (int64_t)kind * p.kv_heads * bs;
-      kvh = (int)(rem / bs);
-      t = (int)(rem - (int64_t)kvh * bs);
+      const uint32_t item = r / R;
+      rr = r - item * R;
+      const uint32_t i = item >> 1;
+      kind = (int)(item & 1u);
       src = p.src[i];
       dst = p.dst[i];
-      len = max(0, min(p.lengths[i], bs));
+      len = max(0, min(p.lengths[i], (int)bs));
       ok = src >= 0 && src < p.hot_slots && dst >= 0 && dst < p.warm_slots;
     }
-    const bool valid = ok && t < len;
-    const int64_t in_row = ((src * p.kv_heads + kvh) * bs + t);
-    const int64_t out_row = ((dst * p.kv_heads + kvh) * bs + t);
-    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-    if (valid) {
-      const __half* hp = reinterpret_cast<const __half*>(kind ? p.hot_v : p.hot_k);
-      raw = *reinterpret_cast<const uint4*>(hp + in_row * D + sub * 8);
-    }
-    __half hs, hz;
-    const uint2 c = quant_row<LPR>(raw, hs, hz);
-    uint8_t* wp = reinterpret_cast<uint8_t*>(kind ? p.warm_v : p.warm_k);
-    __half* sp = reinterpret_cast<__half*>(kind ? p.v_scale : p.k_scale);
-    __half* zp = reinterpret_cast<__half*>(kind ? p.v_zero : p.k_zero);
-    if (valid) {
-      *reinterpret_cast<uint2*>(wp + out_row * D + sub * 8) = c;
+    const bool valid = ok && (int)(rr % bs) < len;
+    const int64_t in_row = src * R + rr;
+    const int64_t out_row = dst * R + rr;
+    uint4 raw[L::V];
+    const __half* hp = reinterpret_cast<const __half*>(kind ? p.hot_v : p.hot_k) + in_row * D + sub * 8;
+#pragma unroll
+    for (int v = 0; v < L::V; ++v)
+      raw[v] = valid ? *reinterpret_cast<const uint4*>(hp + v * LPR * 8) : make_uint4(0u, 0u, 0u, 0u);
+    uint8_t* wp = reinterpret_cast<uint8_t*>(kind ? p.warm_v : p.warm_k) + out_row * D;
+    __half* sp = reinterpret_cast<__half*>(kind ? p.v_scale : p.k_scale) + out_row;
+    __half* zp = reinterpret_cast<__half*>(kind ? p.v_zero : p.k_zero) + out_row;
+    quantize_store<D, LPR>(raw, wp, sp, zp, valid, sub);
+    if (ok && !valid && p.clear_tail) {
+#pragma unroll
+      for (int v = 0; v < L::V; ++v)
+        *reinterpret_cast<uint2*>(wp + (sub + LPR * v) * 8) = make_uint2(0u, 0u);
       if (sub == 0) {
-        sp[out_row] = hs;
-        zp[out_row] = hz;
-      }
-    } else if (ok && p.clear_tail) {
-      *reinterpret_cast<uint2*>(wp + out_row * D + sub * 8) = make_uint2(0u, 0u);
-      if (sub == 0) {
-        sp[out_row] = __float2half_rn(1.f);
-        zp[out_row] = __float2half_rn(0.f);
+        *sp = __float2half_rn(1.f);
+        *zp = __float2half_rn(0.f);
       }
     }
   }
@@ -265,15 +320,24 @@ cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int threads = 256;
   if (format == kFmtR) {
-    const int lpr = p.head_dim / 8;
-    const int64_t rows = (int64_t)p.count * 2 * p.kv_heads * p.block_size;
-    const int64_t per_block = (threads / 32) * (32 / lpr);
-    int64_t blocks = (rows + per_block - 1) / per_block;
-    blocks = blocks < (int64_t)sms * 16 ? blocks : (int64_t)sms * 16;
-    switch (p.head_dim) {
-      case 64: demote_r_kernel<8><<<blocks, threads, 0, stream>>>(p); break;
-      case 128: demote_r_kernel<16><<<blocks, threads, 0, stream>>>(p); break;
-      default: return cudaErrorInvalidValue;
+    if (p.head_dim != 64 && p.head_dim != 128) return cudaErrorInvalidValue;
+    const int lpr = p.head_dim == 64 ? lanes_per_row<64>() : lanes_per_row<128>();
+    const int64_t rows_per_item = 2LL * p.kv_heads * p.block_size;  // rows of one demoted block
+    const int64_t max_items = ((1LL << 31) - 1) / rows_per_item;
+    for (int64_t first = 0; first < p.count; first += max_items) {
+      DemoteParams q = p;
+      q.count = (int32_t)(p.count - first < max_items ? p.count - first : max_items);
+      q.src = p.src + first;
+      q.dst = p.dst + first;
+      q.lengths = p.lengths + first;
+      const int64_t rows = (int64_t)q.count * rows_per_item;
+      const int64_t per_block = threads / lpr;
+      int64_t blocks = (rows + per_block - 1) / per_block;
+      blocks = blocks < (int64_t)sms * 16 ? blocks : (int64_t)sms * 16;
+      if (p.head_dim == 64)
+        demote_r_kernel<64><<<(unsigned)blocks, threads, 0, stream>>>(q, (uint32_t)rows);
+      else
+        demote_r_kernel<128><<<(unsigned)blocks, threads, 0, stream>>>(q, (uint32_t)rows);
     }
   } else {
     const int64_t tiles = (int64_t)p.count * 2 * p.kv_heads;
