@@ -55,6 +55,8 @@ def parse():
                          "over 32 layers, sharded by block range across the GPUs; demote: "
                          "HOT->WARM demotion of 2^20 fp16 [16 x 128] tiles per GPU")
     ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--demote-blocks", type=int, default=65536,
+                    help="demote: demoted blocks per launch (x 8 kv heads x K/V tiles)")
     ap.add_argument("--no-graph", action="store_true",
                     help="c4: launch every layer from Python instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -475,7 +477,7 @@ def run_demote(a, rank, world, dist_on, device):
     Bytes per launch: 4 GiB read, 2 GiB codes + 64 MiB scale/zero written."""
     from paged_tierkv_b200 import _native, ops
     _native.load(build_if_missing=True)
-    blocks, hkv, bs, d = 65536, 8, 16, 128
+    blocks, hkv, bs, d = a.demote_blocks, 8, 16, 128
     pools = ops.TieredPools.allocate(blocks, blocks, hkv, bs, d, device)
     gen = torch.Generator(device=device).manual_seed(11 + rank)
     pools.hot_k.normal_(generator=gen)
@@ -484,38 +486,54 @@ def run_demote(a, rank, world, dist_on, device):
     dst = torch.flip(src, dims=[0]).contiguous()
     lens = torch.full((blocks,), bs, dtype=torch.int32, device=device)
     tiles = blocks * hkv * 2
+    # read fp16, write codes + scale + zero (promotion moves the same bytes back)
     bytes_per = tiles * bs * d * 2 + tiles * bs * d + tiles * bs * 2 * 2
-    for _ in range(a.warmup):
-        ops.demote_blocks_to_warm(pools, src, dst, lens)
     steps = max(1, min(a.steps, 50))
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    if dist_on:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    for i in range(steps):
-        starts[i].record()
-        ops.demote_blocks_to_warm(pools, src, dst, lens)
-        ends[i].record()
-    torch.cuda.synchronize()
-    ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
-    t = torch.tensor([ms], dtype=torch.float64, device=device)
+
+    def timed(fn):
+        for _ in range(a.warmup):
+            fn()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        if dist_on:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        for i in range(steps):
+            starts[i].record()
+            fn()
+            ends[i].record()
+        torch.cuda.synchronize()
+        return statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = timed(lambda: ops.demote_blocks_to_warm(pools, src, dst, lens))
+    clocks = sampler.stop() if sampler else None
+    # promotion of the WARM slots just written back into HOT slots 0..blocks-1
+    ms_p = timed(lambda: ops.promote_blocks_to_hot(pools, dst, src, lens))
+    t = torch.tensor([ms, ms_p], dtype=torch.float64, device=device)
     if dist_on:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t[0])
+    ms, ms_p = float(t[0]), float(t[1])
     if rank != 0:
         return
     peak, kind = hbm_peak()
     gbs = bytes_per / (ms * 1e-3) / 1e9
+    gbs_p = bytes_per / (ms_p * 1e-3) / 1e9
     print(json.dumps({
-        "metric": "HOT->WARM demotion GB/s (2^20 fp16 [16 x 128] tiles, Format R)",
+        "metric": f"HOT->WARM demotion GB/s ({tiles} fp16 [16 x 128] tiles, Format R)",
         "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
         "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "dtype": "fp16->u8", "data": "synthetic N(0,1)",
-        "config": {"workload": "demote_2p20_tiles", "tiles": tiles, "bytes_per_launch": bytes_per},
+        "config": {"workload": f"demote_{tiles}_tiles", "tiles": tiles,
+                   "bytes_per_launch": bytes_per, "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "peak_kind": kind},
-        "gpu_launches": steps,
+        "promote": {"value": round(gbs_p * world, 1), "unit": "GB/s", "ms_per_step": round(ms_p, 4),
+                    "frac": round(gbs_p / peak, 4)},
+        "clocks": clocks,
+        "gpu_launches": 2 * steps,
     }), flush=True)
 
 

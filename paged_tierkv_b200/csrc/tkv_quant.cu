@@ -354,64 +354,86 @@ cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream
 
 // ---------------------------------------------------------------- promotion, Format R
 // HOT[dst] rows [0, length) = h(h(h(code) - zero) * scale)  (tierkv_policy.py:39-44).
-template <int LPR>
-__global__ void promote_r_kernel(const DemoteParams p) {
-  constexpr int D = LPR * 8;
-  constexpr int RPW = 32 / LPR;
+// h(code) - zero is evaluated in fp32 and rounded, as the reference does; the
+// product of two fp16 values is exact in fp32, so the fp16 multiply (one
+// rounding of the exact product) equals the reference's fp32 multiply + cast.
+__device__ __forceinline__ uint4 dequant_chunk(const uint2 c, float z, __half2 s2) {
+  const __half2 bias2 = __float2half2_rn(1024.f);
+  const uint32_t w[2] = {c.x, c.y};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // (1024 + code) as fp16: the code in the low byte of the significand
+    const uint32_t x = __byte_perm(w[i >> 1], 0x64646464u, (i & 1) ? 0x4342u : 0x4140u);
+    const float2 q = __half22float2(__hsub2(*reinterpret_cast<const __half2*>(&x), bias2));
+    const __half2 h = __hmul2(__floats2half2_rn(q.x - z, q.y - z), s2);
+    o[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Rows as in demote_r_kernel, with src a WARM slot and dst a HOT slot.
+template <int D>
+__global__ void __launch_bounds__(256) promote_r_kernel(const DemoteParams p, uint32_t rows) {
+  constexpr int LPR = lanes_per_row<D>();
+  using L = RowLayout<D, LPR>;
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;
-  const int bs = p.block_size;
-  const int64_t rows_per_block = 2LL * p.kv_heads * bs;
-  const int64_t rows = (int64_t)p.count * rows_per_block;
-  const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r0 = warp * RPW; r0 < rows; r0 += nwarps * RPW) {
-    const int64_t r = r0 + lane / LPR;
+  const uint32_t bs = (uint32_t)p.block_size;
+  const uint32_t R = (uint32_t)p.kv_heads * bs;
+  const uint32_t warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const uint32_t wstride = gridDim.x * (blockDim.x >> 5) * L::RPW;
+  for (uint32_t r0 = warp * L::RPW; r0 < rows; r0 += wstride) {
+    const uint32_t r = r0 + lane / LPR;
     if (r >= rows) continue;
-    const int i = (int)(r / rows_per_block);
-    int64_t rem = r - (int64_t)i * rows_per_block;
-    const int kind = (int)(rem / ((int64_t)p.kv_heads * bs));
-    rem -= (int64_t)kind * p.kv_heads * bs;
-    const int kvh = (int)(rem / bs);
-    const int t = (int)(rem - (int64_t)kvh * bs);
-    const int64_t src = p.src[i], dst = p.dst[i];  // src: WARM slot, dst: HOT slot
-    const int len = max(0, min(p.lengths[i], bs));
-    if (src < 0 || src >= p.warm_slots || dst < 0 || dst >= p.hot_slots || t >= len) continue;
-    const int64_t in_row = (src * p.kv_heads + kvh) * bs + t;
-    const int64_t out_row = (dst * p.kv_heads + kvh) * bs + t;
-    const uint8_t* wp = reinterpret_cast<const uint8_t*>(kind ? p.warm_v : p.warm_k);
-    const __half* sp = reinterpret_cast<const __half*>(kind ? p.v_scale : p.k_scale);
-    const __half* zp = reinterpret_cast<const __half*>(kind ? p.v_zero : p.k_zero);
-    const uint2 c = *reinterpret_cast<const uint2*>(wp + in_row * D + sub * 8);
-    const float s = __half2float(sp[in_row]);
-    const float z = __half2float(zp[in_row]);
-    const uint32_t w[2] = {c.x, c.y};
-    __half o[8];
+    const uint32_t item = r / R;
+    const uint32_t rr = r - item * R;
+    const uint32_t i = item >> 1;
+    const int kind = (int)(item & 1u);
+    const int64_t src = p.src[i], dst = p.dst[i];
+    const int len = max(0, min(p.lengths[i], (int)bs));
+    if (src < 0 || src >= p.warm_slots || dst < 0 || dst >= p.hot_slots || (int)(rr % bs) >= len)
+      continue;
+    const int64_t in_row = src * R + rr;
+    const int64_t out_row = dst * R + rr;
+    const uint8_t* wp = reinterpret_cast<const uint8_t*>(kind ? p.warm_v : p.warm_k) + in_row * D;
+    uint2 c[L::V];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float q = (float)((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
-      o[k] = __float2half_rn(to_h(q - z) * s);
-    }
-    __half* hp = reinterpret_cast<__half*>(kind ? const_cast<void*>(p.hot_v) : const_cast<void*>(p.hot_k));
-    *reinterpret_cast<uint4*>(hp + out_row * D + sub * 8) = *reinterpret_cast<const uint4*>(o);
+    for (int v = 0; v < L::V; ++v) c[v] = *reinterpret_cast<const uint2*>(wp + (sub + LPR * v) * 8);
+    const __half hs = reinterpret_cast<const __half*>(kind ? p.v_scale : p.k_scale)[in_row];
+    const float z = __half2float(reinterpret_cast<const __half*>(kind ? p.v_zero : p.k_zero)[in_row]);
+    const __half2 s2 = __half2half2(hs);
+    __half* hp = reinterpret_cast<__half*>(const_cast<void*>(kind ? p.hot_v : p.hot_k)) + out_row * D;
+#pragma unroll
+    for (int v = 0; v < L::V; ++v)
+      *reinterpret_cast<uint4*>(hp + (sub + LPR * v) * 8) = dequant_chunk(c[v], z, s2);
   }
 }
 
 cudaError_t launch_promote(const DemoteParams& p, cudaStream_t stream) {
   if (p.count <= 0) return cudaSuccess;
+  if (p.head_dim != 64 && p.head_dim != 128) return cudaErrorInvalidValue;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int threads = 256;
-  const int lpr = p.head_dim / 8;
-  const int64_t rows = (int64_t)p.count * 2 * p.kv_heads * p.block_size;
-  const int64_t per_block = (threads / 32) * (32 / lpr);
-  int64_t blocks = (rows + per_block - 1) / per_block;
-  blocks = blocks < (int64_t)sms * 16 ? blocks : (int64_t)sms * 16;
-  switch (p.head_dim) {
-    case 64: promote_r_kernel<8><<<blocks, threads, 0, stream>>>(p); break;
-    case 128: promote_r_kernel<16><<<blocks, threads, 0, stream>>>(p); break;
-    default: return cudaErrorInvalidValue;
+  const int lpr = p.head_dim == 64 ? lanes_per_row<64>() : lanes_per_row<128>();
+  const int64_t rows_per_item = 2LL * p.kv_heads * p.block_size;
+  const int64_t max_items = ((1LL << 31) - 1) / rows_per_item;
+  for (int64_t first = 0; first < p.count; first += max_items) {
+    DemoteParams q = p;
+    q.count = (int32_t)(p.count - first < max_items ? p.count - first : max_items);
+    q.src = p.src + first;
+    q.dst = p.dst + first;
+    q.lengths = p.lengths + first;
+    const int64_t rows = (int64_t)q.count * rows_per_item;
+    const int64_t per_block = threads / lpr;
+    int64_t blocks = (rows + per_block - 1) / per_block;
+    blocks = blocks < (int64_t)sms * 16 ? blocks : (int64_t)sms * 16;
+    if (p.head_dim == 64)
+      promote_r_kernel<64><<<(unsigned)blocks, threads, 0, stream>>>(q, (uint32_t)rows);
+    else
+      promote_r_kernel<128><<<(unsigned)blocks, threads, 0, stream>>>(q, (uint32_t)rows);
   }
   return cudaGetLastError();
 }
