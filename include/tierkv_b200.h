@@ -82,6 +82,9 @@ extern "C" {
 #define TKV_DEVERR_BAD_SLOT  0x1u  /* HOT/WARM block whose slot is outside its pool */
 #define TKV_DEVERR_TIMEOUT   0x2u  /* a bounded pipeline wait gave up            */
 
+/* tkv_decode_args.flags: blocks per work chunk (0 = chosen by the planner) */
+#define TKV_FLAG_CHUNK_MASK  0xff
+
 typedef struct tkv_pools {
     void*   hot_k;
     void*   hot_v;
@@ -100,7 +103,8 @@ typedef struct tkv_pools {
 } tkv_pools;
 
 typedef struct tkv_decode_args {
-    const void*    query;          /* [batch, num_heads, head_dim] (query_len 1) */
+    const void*    query;          /* [batch, num_heads, head_dim] (query_len 1),
+                                      16-byte aligned */
     int32_t        query_dtype;    /* TKV_DTYPE_F16 / TKV_DTYPE_BF16 */
     int32_t        out_dtype;      /* TKV_DTYPE_F16 / BF16 / F32 */
     int32_t        batch;
@@ -120,7 +124,8 @@ typedef struct tkv_decode_args {
     float*         out_lse;        /* optional [batch, num_heads] natural-log LSE */
     float*         score_sums;     /* optional [batch, num_heads, max_blocks] */
     int32_t        num_splits;     /* 0 = automatic */
-    int32_t        flags;          /* reserved, 0 */
+    int32_t        flags;          /* bits 0-7: blocks per work chunk (0 = planned,
+                                      else 8, 16 or 32); other bits 0 */
     void*          workspace;      /* zero-filled once by the owner, see below */
     size_t         workspace_bytes;
 } tkv_decode_args;

@@ -149,6 +149,7 @@ bool encode_hot_map_3d(CUtensorMap* map, void* base, int64_t rows, int head_dim,
 
 struct Plan {
   int splits = 1;
+  int chunk = 32;
   size_t off_err = 0, off_counters = 0, off_part_o = 0, off_part_lse = 0, off_lse_final = 0,
          off_lse_blk = 0, total = 0;
 };
@@ -166,35 +167,54 @@ int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
   if (a->num_blocks < 0 || a->max_blocks < 0 || a->num_blocks > a->max_blocks) return TKV_ERR_INVALID;
   if (a->table_stride < a->max_blocks) return TKV_ERR_INVALID;
   if (a->num_splits < 0 || a->num_splits > kMaxSplits) return TKV_ERR_INVALID;
+  if ((a->flags & ~TKV_FLAG_CHUNK_MASK) != 0) return TKV_ERR_INVALID;
+  const int forced_chunk = a->flags & TKV_FLAG_CHUNK_MASK;
+  if (forced_chunk != 0 && forced_chunk != 8 && forced_chunk != 16 && forced_chunk != 32)
+    return TKV_ERR_INVALID;
   int splits = a->num_splits;
-  if (splits == 0) {
-    int sms = 0;
-    st = current_device_sms(&sms);
-    if (st != TKV_OK) return st;
-    int ctas = 0;
-    if (!cached_occupancy(pl->head_dim, pl->block_size, pl->format, a->query_dtype, &ctas) ||
-        ctas <= 0)
-      return TKV_ERR_CUDA;
-    const int64_t slots = (int64_t)sms * ctas;
+  int chunk = forced_chunk != 0 ? forced_chunk : 32;
+  if (splits == 0 || forced_chunk == 0) {
+    // with the split count given, the waves do not depend on the chunk size:
+    // the choice needs no device
+    int64_t slots = 1;
+    if (splits == 0) {
+      int sms = 0;
+      st = current_device_sms(&sms);
+      if (st != TKV_OK) return st;
+      int ctas = 0;
+      if (!cached_occupancy(pl->head_dim, pl->block_size, pl->format, a->query_dtype, &ctas) ||
+          ctas <= 0)
+        return TKV_ERR_CUDA;
+      slots = (int64_t)sms * ctas;
+    }
     const int64_t units = (int64_t)a->batch * pl->kv_heads;
-    // splits own interleaved 32-block chunks; cost ~ waves * (blocks per CTA
-    // + a fixed per-CTA overhead: prologue, pipeline fill and drain, merge)
-    const int chunks = std::max(1, (a->num_blocks + 31) / 32);
+    // The CTAs of a (sequence, kv head) claim `chunk`-block pieces of its
+    // table; cost ~ waves * (blocks of the busiest CTA + its chunk claims + a
+    // fixed per-CTA overhead: prologue, pipeline fill and drain, merge).
+    // Smaller chunks even out the CTAs' shares when there are few chunks per
+    // CTA (one long context, small batches).
     double best = 1e300;
-    splits = 1;
-    const int max_s = std::min(kMaxSplits, chunks);
-    for (int s = 1; s <= max_s; ++s) {
-      const int64_t ctas_total = units * s;
-      const double waves = (double)((ctas_total + slots - 1) / slots);
-      const double per = 32.0 * ((chunks + s - 1) / s);
-      const double cost = waves * (per + (double)TKV_CTA_OVERHEAD_BLOCKS);
-      if (cost < best - 1e-9) {
-        best = cost;
-        splits = s;
+    for (int c = 32; c >= 8; c >>= 1) {
+      if (forced_chunk != 0 && c != forced_chunk) continue;
+      const int chunks = std::max(1, (a->num_blocks + c - 1) / c);
+      const int lo = a->num_splits > 0 ? a->num_splits : 1;
+      const int hi = a->num_splits > 0 ? a->num_splits : std::min(kMaxSplits, chunks);
+      for (int s = lo; s <= hi; ++s) {
+        const int64_t ctas_total = units * s;
+        const double waves = (double)((ctas_total + slots - 1) / slots);
+        const double per_chunks = (double)((chunks + s - 1) / s);
+        const double cost = waves * (per_chunks * (c + (double)TKV_CHUNK_OVERHEAD_BLOCKS) +
+                                     (double)TKV_CTA_OVERHEAD_BLOCKS);
+        if (cost < best - 1e-9) {
+          best = cost;
+          splits = s;
+          chunk = c;
+        }
       }
     }
   }
   plan->splits = std::max(1, splits);
+  plan->chunk = chunk;
   const size_t rows = (size_t)a->batch * a->num_heads;
   size_t off = 0;
   plan->off_err = off;
@@ -254,7 +274,7 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   Plan plan;
   int32_t st = make_plan(pools, a, &plan);
   if (st != TKV_OK) return st;
-  if (!a->query || !a->out || !aligned(a->query, 4)) return TKV_ERR_INVALID;
+  if (!a->query || !a->out || !aligned(a->query, 16)) return TKV_ERR_INVALID;
   if (a->max_blocks > 0 && (!a->block_table || !a->block_states || !a->block_lengths))
     return TKV_ERR_INVALID;
   if (!a->workspace || a->workspace_bytes < plan.total || !aligned(a->workspace, 256))
@@ -315,6 +335,7 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   p.groups = a->num_kv_groups;
   p.max_blocks = a->max_blocks;
   p.splits = plan.splits;
+  p.chunk = plan.chunk;
   p.out_dtype = a->out_dtype;
   p.scale_log2 = a->scaling * kLog2e;
 

@@ -3,9 +3,10 @@
 // Replaces the Triton kernels of xiaoMartintin/Paged_TierKV
 // (tierkv_triton.py:45-145 single pass + score pass, 147-264 split + reduce).
 //
-// One CTA per (split, kv head, sequence); split s owns the 32-block chunks
-// s, s + splits, ...  Warp 0 is the producer: it reads the block table one
-// chunk (32 entries) at a time, skips COLD blocks (their valid tokens
+// One CTA per (split, kv head, sequence); the splits of a (sequence, kv head)
+// claim chunks of 8, 16 or 32 blocks (chosen per launch by the planner) from a
+// shared counter.  Warp 0 is the producer: it reads the block table one chunk
+// (a lane per entry) at a time, skips COLD blocks (their valid tokens
 // only add the analytic term n * exp(0 - m) to the softmax denominator), and
 // streams each HOT / WARM block tile of this kv head through a ring of shared
 // memory stages with TMA (128-byte swizzled boxes; no multicast), completing
@@ -109,8 +110,8 @@ __device__ __forceinline__ uint32_t ld_u32(const void* p) {
   return *reinterpret_cast<const uint32_t*>(p);
 }
 
-// Stages the query heads of this kv head in shared memory (all threads of the
-// CTA take part; ends with __syncthreads).  Rows n >= G are zero.
+// Stages the query heads of this kv head in shared memory.  Rows n >= G are
+// zero.
 //  sqh[n][d]        standard d order, for ldmatrix-fed HOT K fragments
 //  sqw[n][pw(d)]    permuted so that a standard ldmatrix of k-step s hands lane
 //                   t the dims t*D/4 + 4s + {0,1} (b0) and + {2,3} (b1), the
@@ -118,16 +119,23 @@ __device__ __forceinline__ uint32_t ld_u32(const void* p) {
 // bf16 queries are rescaled per head by 2^-e (exact) so they fit fp16; the
 // factor 2^e is returned through sexp[0..8) and folded into the logit scale;
 // sexp[8..16) receives the per-head sums of the staged values as floats.
-template <int D, int QT, int NT>
+// Only the NC consumer warps take part (the producer is already streaming
+// tiles meanwhile); each thread moves one 16-byte vector of the query per
+// step, and the call ends with named barrier 1 over the consumer warps.
+template <int D, int QT, int NC>
 __device__ __forceinline__ void stage_query(const DecodeParams& p, int seq, int kvh,
                                             __half* sqh, __half* sqw, int* sexp) {
   constexpr int QS = D + 8;
+  constexpr int NT = NC * 32;
+  constexpr int VPR = D / 8;                  // 16-byte vectors per head row
+  constexpr int kVecs = kMaxGroups * VPR;
   const int G = p.groups;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x - 32;           // consumer thread
+  const int cw = tid >> 5, lane = tid & 31;
   const size_t row0 = (size_t)seq * p.num_heads + (size_t)kvh * G;
   if (QT == kDtBF16) {
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.query);
-    for (int n = warp; n < kMaxGroups; n += NT / 32) {
+    for (int n = cw; n < kMaxGroups; n += NC) {
       float amax = 0.f;
       if (n < G)
         for (int d = lane; d < D; d += 32)
@@ -139,39 +147,47 @@ __device__ __forceinline__ void stage_query(const DecodeParams& p, int seq, int 
       frexpf(amax, &k);  // amax < 2^k
       if (lane == 0) sexp[n] = max(0, k - 15);
     }
-  } else if (threadIdx.x < kMaxGroups) {
-    sexp[threadIdx.x] = 0;
+    named_barrier(1, NT);
+  } else if (tid < kMaxGroups) {
+    sexp[tid] = 0;
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < kMaxGroups * D; e += NT) {
-    const int n = e / D;
-    const int d = e - n * D;
-    float v = 0.f;
-    if (n < G) {
-      if (QT == kDtF16)
-        v = __half2float(reinterpret_cast<const __half*>(p.query)[(row0 + n) * D + d]);
-      else
-        v = ldexpf(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.query)[(row0 + n) * D + d]),
-                   -sexp[n]);
-    }
-    const __half h = __float2half_rn(v);
-    sqh[n * QS + d] = h;
-    const int tq = d / (D / 4);
-    const int s = (d % (D / 4)) / 4;
-    const int j = d & 3;
-    sqw[n * QS + 16 * s + 2 * tq + (j & 1) + 8 * (j >> 1)] = h;
-  }
-  __syncthreads();
-  // per-head sum of the staged fp16 values (the WARM K zero-point correction)
   float* qsum = reinterpret_cast<float*>(sexp + 8);
-  for (int n = warp; n < kMaxGroups; n += NT / 32) {
-    float sum = 0.f;
-    for (int d = lane; d < D; d += 32) sum += __half2float(sqh[n * QS + d]);
+  // the loop is warp-uniform: a row's VPR vectors lie in one aligned lane group
+  for (int base = cw * 32; base < kVecs; base += NT) {
+    const int e = base + lane;
+    const int n = e / VPR;
+    const int c = e % VPR;
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    if (e < kVecs && n < G)
+      raw = __ldg(reinterpret_cast<const uint4*>(p.query) + ((row0 + n) * D) / 8 + c);
+    __align__(16) __half h[8];
+    if (QT == kDtF16) {
+      *reinterpret_cast<uint4*>(h) = raw;
+    } else {
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      const int ex = n < kMaxGroups ? sexp[n] : 0;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (lane == 0) qsum[n] = sum;
+      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(ldexpf(__bfloat162float(b[j]), -ex));
+    }
+    float sum = 0.f;
+    if (e < kVecs) {
+      *reinterpret_cast<uint4*>(sqh + n * QS + 8 * c) = *reinterpret_cast<const uint4*>(h);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = 8 * c + j;
+        const int tq = d / (D / 4);
+        const int s = (d % (D / 4)) / 4;
+        const int jj = d & 3;
+        sqw[n * QS + 16 * s + 2 * tq + (jj & 1) + 8 * (jj >> 1)] = h[j];
+        sum += __half2float(h[j]);
+      }
+    }
+    // per-head sum of the staged fp16 values (the WARM K zero-point correction)
+#pragma unroll
+    for (int off = VPR / 2; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (e < kVecs && c == 0) qsum[n] = sum;
   }
-  __syncthreads();
+  named_barrier(1, NT);
 }
 
 // B fragments (k = head_dim, n = query head) of k-steps 2m and 2m+1 from a
@@ -218,12 +234,14 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
 
   int nb = p.nb_dev ? p.nb_dev[seq] : p.nb_uniform;
   nb = max(0, min(nb, p.max_blocks));
-  // Work is handed out in 32-block chunks.  With several splits the CTAs of a
-  // (sequence, kv head) take chunks from a shared atomic counter, so CTAs on
-  // less loaded SMs (or launched earlier) take more of them and HOT-heavy
-  // chunks (sink, recent window) do not pile up on one CTA; the merge is
-  // order-free.  One split walks the chunks in order.
-  const int n_chunks = (nb + 31) / 32;
+  // Work is handed out in chunks of p.chunk (8, 16 or 32) blocks, one block
+  // per producer lane.  With several splits the CTAs of a (sequence, kv head)
+  // take chunks from a shared atomic counter, so CTAs on less loaded SMs (or
+  // launched earlier) take more of them and HOT-heavy chunks (sink, recent
+  // window) do not pile up on one CTA; the merge is order-free.  One split
+  // walks the chunks in order.
+  const int C = p.chunk;
+  const int n_chunks = (nb + C - 1) / C;
   const bool dynamic = p.splits > 1;
   const size_t unit = (size_t)seq * p.kv_heads + kvh;
   uint32_t* chunk_ctr = p.counters + (size_t)p.batch * p.kv_heads + unit;
@@ -240,10 +258,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       if (lane == 0) c = (int)atomicAdd(chunk_ctr, 1u);
       chunk = __shfl_sync(0xffffffffu, c, 0);
     }
-    if (chunk < n_chunks && 32 * chunk + lane < nb) {
-      nslot = __ldg(trow + 32 * chunk + lane);
-      nstate = __ldg(srow + 32 * chunk + lane);
-      nlen = __ldg(lrow + 32 * chunk + lane);
+    if (chunk < n_chunks && lane < C && C * chunk + lane < nb) {
+      nslot = __ldg(trow + C * chunk + lane);
+      nstate = __ldg(srow + C * chunk + lane);
+      nlen = __ldg(lrow + C * chunk + lane);
     }
   }
 
@@ -256,7 +274,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     misc[1] = 0;
     fence_mbar_init();
   }
-  stage_query<D, QT, Cfg::kThreads>(p, seq, kvh, sqh, sqw, misc + 8);  // ends with __syncthreads
+  __syncthreads();  // barriers initialised; the consumers stage the query below
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -272,8 +290,9 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     // software-pipelined table reads: the next chunk is claimed and its entries
     // requested before the current chunk's tiles are issued
     while (chunk < n_chunks && !fail) {
-      const int base = 32 * chunk;
+      const int base = C * chunk;
       const int i = base + lane;
+      const bool mine = lane < C && i < nb;  // this lane's block of the chunk
       const int slot = nslot;
       const int st = nstate;
       const int len = max(0, min(nlen, BS));
@@ -284,12 +303,12 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       } else {
         ++chunk;
       }
-      if (chunk < n_chunks && 32 * chunk + lane < nb) {
-        nslot = __ldg(trow + 32 * chunk + lane);
-        nstate = __ldg(srow + 32 * chunk + lane);
-        nlen = __ldg(lrow + 32 * chunk + lane);
+      if (chunk < n_chunks && lane < C && C * chunk + lane < nb) {
+        nslot = __ldg(trow + C * chunk + lane);
+        nstate = __ldg(srow + C * chunk + lane);
+        nlen = __ldg(lrow + C * chunk + lane);
       }
-      bool issue = (i < nb) && (st == 0 || st == 1) && len > 0;
+      bool issue = mine && (st == 0 || st == 1) && len > 0;
       if (issue) {
         const int64_t cap = (st == 0) ? p.hot_slots : p.warm_slots;
         if (slot < 0 || (int64_t)slot >= cap) {
@@ -297,7 +316,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           atomicOr(p.err, 0x1u);
         }
       }
-      if (i < nb && !issue) {
+      if (mine && !issue) {
         cold += len;
         if (p.lse_blk != nullptr) {
           const float v = len > 0 ? logf((float)len) : -INFINITY;
@@ -410,6 +429,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   const int t = lane & 3;
   if (warp > 0) {
     const int cw = warp - 1;
+    stage_query<D, QT, Cfg::kConsumers>(p, seq, kvh, sqh, sqw, misc + 8);
     const uint32_t sqh_u = smem_u32(sqh);
     const uint32_t sqw_u = smem_u32(sqw);
     float qmul[2], qsum[2];  // logit scale (log2 domain) and query sum of heads 2t, 2t+1

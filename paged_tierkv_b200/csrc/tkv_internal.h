@@ -15,6 +15,10 @@
 #ifndef TKV_CTA_OVERHEAD_BLOCKS
 #define TKV_CTA_OVERHEAD_BLOCKS 16
 #endif
+// ... and of claiming one work chunk (atomic ticket + table entries).
+#ifndef TKV_CHUNK_OVERHEAD_BLOCKS
+#define TKV_CHUNK_OVERHEAD_BLOCKS 1
+#endif
 
 namespace tkv {
 
@@ -58,6 +62,7 @@ struct DecodeParams {
   int32_t groups;
   int32_t max_blocks;
   int32_t splits;
+  int32_t chunk;              // blocks per claimed work chunk: 8, 16 or 32
   int32_t out_dtype;
   float scale_log2;           // scaling * log2(e)
 };

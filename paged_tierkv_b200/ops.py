@@ -185,11 +185,14 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
                      block_lengths: torch.Tensor, pools: TieredPools, num_blocks,
                      num_key_value_groups: int, scaling: float, *, return_scores: bool = False,
                      return_lse: bool = False, out: torch.Tensor | None = None,
-                     out_dtype: torch.dtype | None = None, num_splits: int = 0, stream=None):
+                     out_dtype: torch.dtype | None = None, num_splits: int = 0,
+                     chunk_blocks: int = 0, stream=None):
     """Tiered paged decode attention over a batch of sequences.
 
     query [B, Hq, D] or [B, Hq, 1, D]; tables [B, T] (or [T] for B = 1) int32;
     num_blocks: int (all sequences) or an int32 CUDA tensor [B].
+    num_splits / chunk_blocks (8, 16 or 32): CTAs per (sequence, kv head) and
+    blocks per claimed work chunk; 0 lets the planner choose.
     Returns (out [B, Hq, D], score_sums [B, Hq, T] or None, lse [B, Hq] or None).
     """
     if query.ndim == 4:
@@ -203,6 +206,8 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
     if query.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError("TierKV decode supports fp16/bf16 query tensors only.")
     query = query.contiguous()
+    if query.data_ptr() % 16:  # the kernel reads the query in 16-byte vectors
+        query = query.clone()
     pools.validate()
     batch, num_heads, head_dim = query.shape
     if head_dim != pools.head_dim:
@@ -239,7 +244,8 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
     args = N.TkvDecodeArgs(
         _ptr(query), _DTYPE[query.dtype], _DTYPE[odt], batch, num_heads, int(num_key_value_groups),
         max_blocks, _ptr(table), _ptr(states), _ptr(lengths), _row_stride(table), _ptr(nb_dev),
-        nb_uniform, float(scaling), _ptr(out), _ptr(lse), _ptr(scores), int(num_splits), 0, None, 0)
+        nb_uniform, float(scaling), _ptr(out), _ptr(lse), _ptr(scores), int(num_splits),
+        int(chunk_blocks), None, 0)
     splits = ctypes.c_int32()
     nbytes = ctypes.c_size_t()
     N.check(lib.tkv_decode_plan(ctypes.byref(pstruct), ctypes.byref(args), ctypes.byref(splits),

@@ -65,7 +65,7 @@ def test_mixed_tiers_match_oracle(head_dim, block_size, fmt, groups):
 @pytest.mark.parametrize("num_blocks", [1, 2, 4, 5, 127, 128, 129])
 @pytest.mark.parametrize("splits", [0, 1, 3, 7])
 def test_block_counts_and_splits(num_blocks, splits):
-    """Splits claim 32-block chunks dynamically; more splits than chunks leaves
+    """Splits claim work chunks dynamically; more splits than chunks leaves
     some CTAs without work (empty partials).  Repeated calls reuse the
     self-resetting counters of the workspace."""
     case = make_case(seed=num_blocks * 7 + splits, batch=1, q_heads=32, kv_heads=8, head_dim=128,
@@ -75,6 +75,30 @@ def test_block_counts_and_splits(num_blocks, splits):
         out, scores, _ = _run(case, num_splits=splits, return_scores=True)
         _close(out, ref)
         np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-4, rtol=1e-3)
+
+
+@pytest.mark.parametrize("chunk", [8, 16, 32])
+@pytest.mark.parametrize("num_blocks", [1, 9, 40, 129])
+@pytest.mark.parametrize("splits", [0, 1, 5])
+def test_chunk_sizes(chunk, num_blocks, splits):
+    """Every work-chunk size the planner can choose, with the last chunk
+    partial and with more splits than chunks."""
+    case = make_case(seed=1000 + chunk * 31 + num_blocks * 7 + splits, batch=2, q_heads=32,
+                     kv_heads=8, head_dim=128, block_size=16, num_blocks=num_blocks)
+    ref, ref_lse, ref_scores = oracle_decode(case)
+    for _ in range(2):
+        out, scores, lse = _run(case, num_splits=splits, chunk_blocks=chunk, return_scores=True,
+                                return_lse=True)
+        _close(out, ref)
+        np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=1e-3, rtol=1e-4)
+        np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-4, rtol=1e-3)
+
+
+@pytest.mark.parametrize("chunk", [4, 12, 64, 0x100])
+def test_bad_chunk_size_is_rejected(chunk):
+    case = make_case(seed=3, batch=1, q_heads=8, kv_heads=2, head_dim=64, num_blocks=4)
+    with pytest.raises(ValueError):
+        _run(case, chunk_blocks=chunk)
 
 
 def test_all_cold_and_empty():
