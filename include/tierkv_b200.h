@@ -135,9 +135,11 @@ int32_t     tkv_get_version(void);
 const char* tkv_status_string(int32_t status);
 
 /* Number of splits the launch will use and the workspace it needs.
- * The workspace must be zero-filled once when it is allocated; the kernels
- * leave it in that state (its split counters reset themselves).  Concurrent
- * calls on different streams need different workspaces.
+ * The workspace must be zero-filled once when it is allocated.  Its first
+ * eighth holds the work counters, which every launch returns to zero; the
+ * partial results live above them, so one workspace serves calls of any
+ * shape in any order.  Concurrent calls on different streams need different
+ * workspaces.
  * Replaces the partial-buffer allocations of tierkv_triton.py:316-325. */
 int32_t tkv_decode_plan(const tkv_pools* pools, const tkv_decode_args* args,
                         int32_t* num_splits_out, size_t* workspace_bytes_out);

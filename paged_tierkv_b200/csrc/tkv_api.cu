@@ -147,12 +147,43 @@ bool encode_hot_map_3d(CUtensorMap* map, void* base, int64_t rows, int head_dim,
   return r == CUDA_SUCCESS;
 }
 
+// Workspace layout, a function of the workspace's size W alone: [0, 256) the
+// device error word, [256, 256 + R) the counters with R = W / 8 rounded down
+// to 256 bytes, then the data regions (partials, per-block LSE).  Every launch
+// returns its counters to zero and no data region reaches below 256 + R, so
+// one workspace, zero-filled once, serves calls of any shape in any order.
+inline size_t counter_reserve(size_t w) { return (w / 8) / kAlign * kAlign; }
+inline size_t data_base(size_t w) { return kAlign + counter_reserve(w); }
+inline bool layout_fits(size_t w, size_t counters, size_t data) {
+  return counter_reserve(w) >= counters && data_base(w) + data <= w;
+}
+size_t required_workspace(size_t counters, size_t data) {
+  constexpr size_t kStep = 8 * kAlign;
+  size_t w = std::max(8 * align_up(counters), (data + kAlign) * 8 / 7 + kAlign);
+  w = (w + kStep - 1) / kStep * kStep;
+  while (!layout_fits(w, counters, data)) w += kStep;
+  return w;
+}
+
 struct Plan {
   int splits = 1;
   int chunk = 32;
-  size_t off_err = 0, off_counters = 0, off_part_o = 0, off_part_lse = 0, off_lse_final = 0,
-         off_lse_blk = 0, total = 0;
+  int group_size = 1;  // splits per merge group; = splits when the merge has one level
+  size_t counters_bytes = 0, data_bytes = 0;
+  // offsets of the data regions from the data base
+  size_t off_part_o = 0, off_part_lse = 0, off_gpart_o = 0, off_gpart_lse = 0,
+         off_lse_final = 0, off_lse_blk = 0;
+  size_t total = 0;  // smallest workspace that holds this layout
 };
+
+// Splits beyond this count are merged in two levels: groups of about
+// sqrt(splits) partials, then the group results.  Each level costs a ticket,
+// a round of LSE loads and three CTA barriers (measured: at 74 splits one
+// level is 1.3 us faster per launch), so only very wide merges use two.
+#ifndef TKV_TREE_MERGE_SPLITS
+#define TKV_TREE_MERGE_SPLITS 128
+#endif
+constexpr int kTreeMergeSplits = TKV_TREE_MERGE_SPLITS;
 
 int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
   int32_t st = check_pools(pl, true);
@@ -202,7 +233,8 @@ int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
       for (int s = lo; s <= hi; ++s) {
         const int64_t ctas_total = units * s;
         const double waves = (double)((ctas_total + slots - 1) / slots);
-        const double per_chunks = (double)((chunks + s - 1) / s);
+        // dynamic claiming evens the CTAs' shares to within about one chunk
+        const double per_chunks = (double)chunks / s + 0.5;
         const double cost = waves * (per_chunks * (c + (double)TKV_CHUNK_OVERHEAD_BLOCKS) +
                                      (double)TKV_CTA_OVERHEAD_BLOCKS);
         if (cost < best - 1e-9) {
@@ -215,17 +247,30 @@ int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
   }
   plan->splits = std::max(1, splits);
   plan->chunk = chunk;
+  plan->group_size = plan->splits;
+  if (plan->splits > kTreeMergeSplits) {
+    int g = (int)std::ceil(std::sqrt((double)plan->splits));
+    while (g * g < plan->splits) ++g;
+    plan->group_size = g;
+  }
+  const int ngroups = (plan->splits + plan->group_size - 1) / plan->group_size;
   const size_t rows = (size_t)a->batch * a->num_heads;
+  const size_t units = (size_t)a->batch * pl->kv_heads;
+  // counters: split (or group) tickets and chunk counters, one each per
+  // (sequence, kv head), then the group tickets
+  plan->counters_bytes = sizeof(uint32_t) * units * (2 + (ngroups > 1 ? ngroups : 0));
   size_t off = 0;
-  plan->off_err = off;
-  off = align_up(off + 16);
-  plan->off_counters = off;  // split tickets, then chunk counters, one per (sequence, kv head)
-  off = align_up(off + 2 * sizeof(uint32_t) * (size_t)a->batch * pl->kv_heads);
   if (plan->splits > 1) {
     plan->off_part_o = off;
     off = align_up(off + sizeof(float) * rows * plan->splits * pl->head_dim);
     plan->off_part_lse = off;
     off = align_up(off + sizeof(float) * rows * plan->splits);
+  }
+  if (ngroups > 1) {
+    plan->off_gpart_o = off;
+    off = align_up(off + sizeof(float) * rows * ngroups * pl->head_dim);
+    plan->off_gpart_lse = off;
+    off = align_up(off + sizeof(float) * rows * ngroups);
   }
   if (a->score_sums) {
     plan->off_lse_final = off;
@@ -233,7 +278,8 @@ int32_t make_plan(const tkv_pools* pl, const tkv_decode_args* a, Plan* plan) {
     plan->off_lse_blk = off;
     off = align_up(off + sizeof(float) * rows * std::max(1, a->max_blocks));
   }
-  plan->total = off;
+  plan->data_bytes = off;
+  plan->total = required_workspace(plan->counters_bytes, plan->data_bytes);
   return TKV_OK;
 }
 
@@ -277,7 +323,8 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   if (!a->query || !a->out || !aligned(a->query, 16)) return TKV_ERR_INVALID;
   if (a->max_blocks > 0 && (!a->block_table || !a->block_states || !a->block_lengths))
     return TKV_ERR_INVALID;
-  if (!a->workspace || a->workspace_bytes < plan.total || !aligned(a->workspace, 256))
+  if (!a->workspace || !layout_fits(a->workspace_bytes, plan.counters_bytes, plan.data_bytes) ||
+      !aligned(a->workspace, 256))
     return TKV_ERR_WORKSPACE;
   if (pools->hot_slots * pools->kv_heads * pools->block_size >= (int64_t(1) << 31))
     return TKV_ERR_INVALID;
@@ -315,15 +362,20 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   p.v_zero = pools->v_zero;
   p.out = a->out;
   p.out_lse = a->out_lse;
-  p.err = reinterpret_cast<uint32_t*>(ws + plan.off_err);
-  p.counters = reinterpret_cast<uint32_t*>(ws + plan.off_counters);
+  p.err = reinterpret_cast<uint32_t*>(ws);
+  p.counters = reinterpret_cast<uint32_t*>(ws + kAlign);
+  uint8_t* data = ws + data_base(a->workspace_bytes);
   if (plan.splits > 1) {
-    p.part_o = reinterpret_cast<float*>(ws + plan.off_part_o);
-    p.part_lse = reinterpret_cast<float*>(ws + plan.off_part_lse);
+    p.part_o = reinterpret_cast<float*>(data + plan.off_part_o);
+    p.part_lse = reinterpret_cast<float*>(data + plan.off_part_lse);
+  }
+  if (plan.group_size < plan.splits) {
+    p.gpart_o = reinterpret_cast<float*>(data + plan.off_gpart_o);
+    p.gpart_lse = reinterpret_cast<float*>(data + plan.off_gpart_lse);
   }
   if (a->score_sums) {
-    p.lse_final = reinterpret_cast<float*>(ws + plan.off_lse_final);
-    p.lse_blk = reinterpret_cast<float*>(ws + plan.off_lse_blk);
+    p.lse_final = reinterpret_cast<float*>(data + plan.off_lse_final);
+    p.lse_blk = reinterpret_cast<float*>(data + plan.off_lse_blk);
   }
   p.table_stride = a->table_stride;
   p.hot_slots = pools->hot_slots;
@@ -336,6 +388,7 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   p.max_blocks = a->max_blocks;
   p.splits = plan.splits;
   p.chunk = plan.chunk;
+  p.group_size = plan.group_size;
   p.out_dtype = a->out_dtype;
   p.scale_log2 = a->scaling * kLog2e;
 
@@ -525,8 +578,7 @@ extern "C" int32_t tkv_decode_attention_noalloc(const tkv_pools* pools,
   if (st != TKV_OK) return st;
   // The array keeps whatever the previous call left; the error word, split
   // tickets and chunk counters must start at zero, so clear them first.
-  const size_t counters_end =
-      plan.off_counters + 2 * sizeof(uint32_t) * (size_t)args->batch * pools->kv_heads;
+  const size_t counters_end = kAlign + plan.counters_bytes;
   if (cudaMemsetAsync(scratch, 0, counters_end, reinterpret_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
     return TKV_ERR_CUDA;

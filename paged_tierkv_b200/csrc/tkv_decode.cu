@@ -4,9 +4,10 @@
 // (tierkv_triton.py:45-145 single pass + score pass, 147-264 split + reduce).
 //
 // One CTA per (split, kv head, sequence); the splits of a (sequence, kv head)
-// claim chunks of 8, 16 or 32 blocks (chosen per launch by the planner) from a
-// shared counter.  Warp 0 is the producer: it reads the block table one chunk
-// (a lane per entry) at a time, skips COLD blocks (their valid tokens
+// claim block ranges of up to 8, 16 or 32 blocks (the maximum chosen per
+// launch by the planner) from a shared counter.  Warp 0 is the producer: it
+// reads the block table one range (a lane per entry) at a time, skips COLD
+// blocks (their valid tokens
 // only add the analytic term n * exp(0 - m) to the softmax denominator), and
 // streams each HOT / WARM block tile of this kv head through a ring of shared
 // memory stages with TMA (128-byte swizzled boxes; no multicast), completing
@@ -61,6 +62,7 @@ struct TileInfo {
 #define TKV_EARLY_RELEASE 1
 #endif
 
+
 template <int D, int BS, int FMT, int QT>
 struct DecodeCfg {
   static constexpr int kConsumers = TKV_CONSUMERS;
@@ -93,7 +95,8 @@ struct DecodeCfg {
   // the end-of-kernel merge scratch aliases the stage ring
   static constexpr int kMergeFloats = kConsumers * (2 * kMaxGroups + kMaxGroups * D);
   static_assert(kMergeFloats * 4 <= kStages * kStageBytes, "merge scratch must fit the ring");
-  static_assert(kMaxGroups * kMaxSplits * 4 <= kStages * kStageBytes, "split scratch must fit");
+  static_assert(kMaxGroups * (kMaxSplits + 2) * 4 <= kStages * kStageBytes,
+                "split-merge scratch must fit the ring");
 };
 
 __device__ __forceinline__ void store_out(void* out, int dtype, size_t idx, float v) {
@@ -200,6 +203,102 @@ __device__ __forceinline__ void load_qfrag(uint32_t sq, int lane, int m, uint32_
   ldsm_x4(addr, b00, b01, b10, b11);
 }
 
+// Merges `cnt` normalised partials (o, LSE) of the G rows row0.. of a
+// (sequence, kv head): part j of row r at po + ((r * rstride) + j0 + j) * D
+// and plse[r * rstride + j0 + j].  The result goes to the final output
+// (p.out / p.out_lse / p.lse_final) when dst_o is null, else to the fp32
+// partial slot dj of rows with stride dstride.  All NT threads take part;
+// wsl is shared scratch of kMaxGroups * (cnt + 2) floats.  One warp per
+// head: a lane owns 4 dims (a float4 of every part's row) and, for head_dim
+// 64, every other part; the loop keeps 8 independent 16-byte loads in flight.
+template <int D, int NT>
+__device__ __forceinline__ void merge_parts(const float* po, const float* plse, int rstride,
+                                            int j0, int cnt, size_t row0, int G, float* wsl,
+                                            const DecodeParams& p, float* dst_o, float* dst_lse,
+                                            int dstride, int dj) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* hm = wsl + kMaxGroups * cnt;  // [G] max, [G] sum
+  for (int e = threadIdx.x; e < G * cnt; e += NT) {
+    const int h = e / cnt;
+    wsl[e] = __ldcg(plse + (row0 + h) * rstride + j0 + (e - h * cnt));
+  }
+  __syncthreads();
+  for (int h = warp; h < G; h += NT / 32) {
+    float M = -INFINITY;
+    for (int sp = lane; sp < cnt; sp += 32) M = fmaxf(M, wsl[h * cnt + sp]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float S = 0.f;
+    if (M != -INFINITY)
+      for (int sp = lane; sp < cnt; sp += 32) S += ex2((wsl[h * cnt + sp] - M) * kLog2e);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
+    if (lane == 0) {
+      hm[h] = M;
+      hm[kMaxGroups + h] = S;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * cnt; e += NT) {
+    const int h = e / cnt;
+    const float M = hm[h], S = hm[kMaxGroups + h];
+    wsl[e] = (M != -INFINITY && S > 0.f) ? ex2((wsl[e] - M) * kLog2e) / S : 0.f;
+  }
+  __syncthreads();
+  constexpr int kVecs = D / 4;                 // float4 per partial row
+  constexpr int kLanesPerRow = kVecs < 32 ? kVecs : 32;
+  constexpr int kSplitLanes = 32 / kLanesPerRow;
+  for (int h = warp; h < G; h += NT / 32) {
+    const size_t row = row0 + h;
+    const int v = lane % kLanesPerRow;
+    const int sp0 = lane / kLanesPerRow;
+    const float4* src = reinterpret_cast<const float4*>(po + (row * rstride + j0) * D) + v;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    int sp = sp0;
+    for (; sp + 7 * kSplitLanes < cnt; sp += 8 * kSplitLanes) {
+      float4 x[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = __ldcg(src + (size_t)(sp + k * kSplitLanes) * kVecs);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float w = wsl[h * cnt + sp + k * kSplitLanes];
+        o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
+      }
+    }
+    for (; sp < cnt; sp += kSplitLanes) {
+      const float4 x = __ldcg(src + (size_t)sp * kVecs);
+      const float w = wsl[h * cnt + sp];
+      o.x += w * x.x; o.y += w * x.y; o.z += w * x.z; o.w += w * x.w;
+    }
+#pragma unroll
+    for (int off = kLanesPerRow; off < 32; off <<= 1) {
+      o.x += __shfl_xor_sync(0xffffffffu, o.x, off);
+      o.y += __shfl_xor_sync(0xffffffffu, o.y, off);
+      o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
+      o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
+    }
+    const float M = hm[h], S = hm[kMaxGroups + h];
+    const float lse = (M != -INFINITY && S > 0.f) ? M + logf(S) : -INFINITY;
+    if (dst_o != nullptr) {
+      if (sp0 == 0)
+        reinterpret_cast<float4*>(dst_o + (row * dstride + dj) * D)[v] = o;
+      if (lane == 0) dst_lse[row * dstride + dj] = lse;
+    } else {
+      if (sp0 == 0) {
+        const size_t base = row * D + 4 * v;
+        store_out(p.out, p.out_dtype, base + 0, o.x);
+        store_out(p.out, p.out_dtype, base + 1, o.y);
+        store_out(p.out, p.out_dtype, base + 2, o.z);
+        store_out(p.out, p.out_dtype, base + 3, o.w);
+      }
+      if (lane == 0) {
+        if (p.out_lse) p.out_lse[row] = lse;
+        if (p.lse_final) p.lse_final[row] = lse;
+      }
+    }
+  }
+}
+
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0
 
 template <int D, int BS, int FMT, int QT>
@@ -235,33 +334,31 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   int nb = p.nb_dev ? p.nb_dev[seq] : p.nb_uniform;
   nb = max(0, min(nb, p.max_blocks));
   // Work is handed out in chunks of p.chunk (8, 16 or 32) blocks, one block
-  // per producer lane.  With several splits the CTAs of a (sequence, kv head)
-  // take chunks from a shared atomic counter, so CTAs on less loaded SMs (or
-  // launched earlier) take more of them and HOT-heavy chunks (sink, recent
-  // window) do not pile up on one CTA; the merge is order-free.  One split
+  // per producer lane.  With several splits, split s starts on chunk s and
+  // then the CTAs of a (sequence, kv head) claim further chunks from a shared
+  // atomic counter, so CTAs on less loaded SMs (or launched earlier) take more
+  // of them and HOT-heavy chunks (sink, recent window) do not pile up on one
+  // CTA; the merge is order-free.  (Measured: shrinking the claims towards the
+  // end costs more in claim latency than it gains in balance.)  One split
   // walks the chunks in order.
-  const int C = p.chunk;
-  const int n_chunks = (nb + C - 1) / C;
+  const int cmax = p.chunk;
   const bool dynamic = p.splits > 1;
   const size_t unit = (size_t)seq * p.kv_heads + kvh;
   uint32_t* chunk_ctr = p.counters + (size_t)p.batch * p.kv_heads + unit;
   const int32_t* trow = p.table + (size_t)seq * p.table_stride;
   const int32_t* srow = p.states + (size_t)seq * p.table_stride;
   const int32_t* lrow = p.lengths + (size_t)seq * p.table_stride;
-  // the producer's first chunk (and its table entries) is requested before
-  // the prologue
-  int chunk = 0;
+  // the table entries of the producer's first chunk are requested before the
+  // prologue; (nbase, ncnt) is the chunk whose entries are loading
+  int nbase = dynamic ? split * cmax : 0;
+  int ncnt = 0;
   int nslot = -1, nstate = 2, nlen = 0;
   if (warp == 0) {
-    if (dynamic) {
-      int c = 0;
-      if (lane == 0) c = (int)atomicAdd(chunk_ctr, 1u);
-      chunk = __shfl_sync(0xffffffffu, c, 0);
-    }
-    if (chunk < n_chunks && lane < C && C * chunk + lane < nb) {
-      nslot = __ldg(trow + C * chunk + lane);
-      nstate = __ldg(srow + C * chunk + lane);
-      nlen = __ldg(lrow + C * chunk + lane);
+    ncnt = max(0, min(cmax, nb - nbase));
+    if (lane < ncnt) {
+      nslot = __ldg(trow + nbase + lane);
+      nstate = __ldg(srow + nbase + lane);
+      nlen = __ldg(lrow + nbase + lane);
     }
   }
 
@@ -289,24 +386,30 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     bool fail = false;
     // software-pipelined table reads: the next chunk is claimed and its entries
     // requested before the current chunk's tiles are issued
-    while (chunk < n_chunks && !fail) {
-      const int base = C * chunk;
+    while (ncnt > 0 && !fail) {
+      const int base = nbase;
       const int i = base + lane;
-      const bool mine = lane < C && i < nb;  // this lane's block of the chunk
+      const bool mine = lane < ncnt;  // this lane's block of the chunk
       const int slot = nslot;
       const int st = nstate;
       const int len = max(0, min(nlen, BS));
       if (dynamic) {
+        // claims beyond the first chunks of all splits
         int c = 0;
         if (lane == 0) c = (int)atomicAdd(chunk_ctr, 1u);
-        chunk = __shfl_sync(0xffffffffu, c, 0);
+        nbase = (__shfl_sync(0xffffffffu, c, 0) + p.splits) * cmax;
+        ncnt = max(0, min(cmax, nb - nbase));
       } else {
-        ++chunk;
+        nbase = base + ncnt;
+        ncnt = max(0, min(cmax, nb - nbase));
       }
-      if (chunk < n_chunks && lane < C && C * chunk + lane < nb) {
-        nslot = __ldg(trow + C * chunk + lane);
-        nstate = __ldg(srow + C * chunk + lane);
-        nlen = __ldg(lrow + C * chunk + lane);
+      nslot = -1;
+      nstate = 2;
+      nlen = 0;
+      if (lane < ncnt) {
+        nslot = __ldg(trow + nbase + lane);
+        nstate = __ldg(srow + nbase + lane);
+        nlen = __ldg(lrow + nbase + lane);
       }
       bool issue = mine && (st == 0 || st == 1) && len > 0;
       if (issue) {
@@ -795,96 +898,57 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   if (nsplit == 1) return;
 
   // ------------------------------------------------------------ split merge
+  // The last CTA of each group of group_size splits merges the group's
+  // partials; with more than one group, the last group's merger then merges
+  // the group partials.  Tickets reset themselves, as does the chunk counter
+  // once every CTA of the unit is done claiming.
+  const int gsz = p.group_size;
+  const int ngroups = (nsplit + gsz - 1) / gsz;
+  const int group = split / gsz;
+  const int gfirst = group * gsz;
+  const int gcount = min(gsz, nsplit - gfirst);
+  const size_t row0 = (size_t)seq * Hq + (size_t)kvh * G;
+  float* wsl = reinterpret_cast<float*>(stages);  // merge scratch aliases the ring
+  uint32_t* ticket = ngroups > 1 ? p.counters + 2 * (size_t)p.batch * p.kv_heads +
+                                       unit * (size_t)ngroups + group
+                                 : p.counters + unit;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const uint32_t prev = atomicAdd(&p.counters[(size_t)seq * p.kv_heads + kvh], 1u);
-    misc[1] = (prev == (uint32_t)(nsplit - 1)) ? 1 : 0;
+    const uint32_t prev = atomicAdd(ticket, 1u);
+    misc[1] = (prev == (uint32_t)(gcount - 1)) ? 1 : 0;
   }
   __syncthreads();
   if (misc[1] == 0) return;
-  if (threadIdx.x == 0) {  // every CTA of this unit is done claiming chunks
-    atomicExch(&p.counters[unit], 0u);
+  if (ngroups == 1) {
+    if (threadIdx.x == 0) {
+      atomicExch(ticket, 0u);
+      atomicExch(chunk_ctr, 0u);
+    }
+    __threadfence();
+    merge_parts<D, Cfg::kThreads>(p.part_o, p.part_lse, nsplit, 0, nsplit, row0, G, wsl, p,
+                                  nullptr, nullptr, 0, 0);
+    return;
+  }
+  if (threadIdx.x == 0) atomicExch(ticket, 0u);
+  __threadfence();
+  merge_parts<D, Cfg::kThreads>(p.part_o, p.part_lse, nsplit, gfirst, gcount, row0, G, wsl, p,
+                                p.gpart_o, p.gpart_lse, ngroups, group);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(p.counters + unit, 1u);
+    misc[1] = (prev == (uint32_t)(ngroups - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (misc[1] == 0) return;
+  if (threadIdx.x == 0) {
+    atomicExch(p.counters + unit, 0u);
     atomicExch(chunk_ctr, 0u);
   }
   __threadfence();
-  float* wsl = reinterpret_cast<float*>(stages);          // [G][nsplit] weights
-  float* hm = wsl + kMaxGroups * kMaxSplits;              // [G] max, [G] sum
-  const size_t row0 = (size_t)seq * Hq + (size_t)kvh * G;
-  for (int e = threadIdx.x; e < G * nsplit; e += Cfg::kThreads)
-    wsl[e] = __ldcg(p.part_lse + row0 * nsplit + e);
-  __syncthreads();
-  for (int h = warp; h < G; h += Cfg::kThreads / 32) {
-    float M = -INFINITY;
-    for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, wsl[h * nsplit + sp]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float S = 0.f;
-    if (M != -INFINITY)
-      for (int sp = lane; sp < nsplit; sp += 32) S += ex2((wsl[h * nsplit + sp] - M) * kLog2e);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
-    if (lane == 0) {
-      hm[h] = M;
-      hm[kMaxGroups + h] = S;
-    }
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * nsplit; e += Cfg::kThreads) {
-    const int h = e / nsplit;
-    const float M = hm[h], S = hm[kMaxGroups + h];
-    wsl[e] = (M != -INFINITY && S > 0.f) ? ex2((wsl[e] - M) * kLog2e) / S : 0.f;
-  }
-  __syncthreads();
-  // One warp per head: lane owns 4 dims (a float4 of every split's row) and,
-  // for head_dim 64, every other split; the split loop keeps 8 independent
-  // 16-byte loads in flight.
-  constexpr int kVecs = D / 4;                 // float4 per partial row
-  constexpr int kLanesPerRow = kVecs < 32 ? kVecs : 32;
-  constexpr int kSplitLanes = 32 / kLanesPerRow;
-  for (int h = warp; h < G; h += Cfg::kThreads / 32) {
-    const size_t row = row0 + h;
-    const int v = lane % kLanesPerRow;
-    const int sp0 = lane / kLanesPerRow;
-    const float4* src = reinterpret_cast<const float4*>(p.part_o + row * nsplit * D) + v;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    int sp = sp0;
-    for (; sp + 7 * kSplitLanes < nsplit; sp += 8 * kSplitLanes) {
-      float4 x[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = __ldcg(src + (size_t)(sp + k * kSplitLanes) * kVecs);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float w = wsl[h * nsplit + sp + k * kSplitLanes];
-        o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
-      }
-    }
-    for (; sp < nsplit; sp += kSplitLanes) {
-      const float4 x = __ldcg(src + (size_t)sp * kVecs);
-      const float w = wsl[h * nsplit + sp];
-      o.x += w * x.x; o.y += w * x.y; o.z += w * x.z; o.w += w * x.w;
-    }
-#pragma unroll
-    for (int off = kLanesPerRow; off < 32; off <<= 1) {
-      o.x += __shfl_xor_sync(0xffffffffu, o.x, off);
-      o.y += __shfl_xor_sync(0xffffffffu, o.y, off);
-      o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
-      o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
-    }
-    if (sp0 == 0) {
-      const size_t base = row * D + 4 * v;
-      store_out(p.out, p.out_dtype, base + 0, o.x);
-      store_out(p.out, p.out_dtype, base + 1, o.y);
-      store_out(p.out, p.out_dtype, base + 2, o.z);
-      store_out(p.out, p.out_dtype, base + 3, o.w);
-    }
-    if (lane == 0) {
-      const float M = hm[h], S = hm[kMaxGroups + h];
-      const float lse = (M != -INFINITY && S > 0.f) ? M + logf(S) : -INFINITY;
-      if (p.out_lse) p.out_lse[row] = lse;
-      if (p.lse_final) p.lse_final[row] = lse;
-    }
-  }
+  merge_parts<D, Cfg::kThreads>(p.gpart_o, p.gpart_lse, ngroups, 0, ngroups, row0, G, wsl, p,
+                                nullptr, nullptr, 0, 0);
 }
 
 // ---------------------------------------------------------------- dispatch

@@ -15,9 +15,10 @@
 #ifndef TKV_CTA_OVERHEAD_BLOCKS
 #define TKV_CTA_OVERHEAD_BLOCKS 16
 #endif
-// ... and of claiming one work chunk (atomic ticket + table entries).
+// ... and of claiming one work chunk (atomic ticket + table entries), as
+// measured on a 131072-token context: 32-block chunks beat 16 and 8.
 #ifndef TKV_CHUNK_OVERHEAD_BLOCKS
-#define TKV_CHUNK_OVERHEAD_BLOCKS 1
+#define TKV_CHUNK_OVERHEAD_BLOCKS 6
 #endif
 
 namespace tkv {
@@ -47,7 +48,10 @@ struct DecodeParams {
   float* out_lse;             // optional [batch, num_heads]
   float* part_o;              // [batch*num_heads, splits, D] (splits > 1)
   float* part_lse;            // [batch*num_heads, splits]
-  uint32_t* counters;         // [2][batch*kv_heads] split tickets, then chunk counters
+  float* gpart_o;             // [batch*num_heads, groups, D] (more than one split group)
+  float* gpart_lse;           // [batch*num_heads, groups]
+  uint32_t* counters;         // [batch*kv_heads] split (or group) tickets, [batch*kv_heads]
+                              // chunk counters, then [batch*kv_heads][groups] group tickets
                               // (both reset by the last CTA of each sequence/kv head)
   float* lse_blk;             // optional [batch*num_heads, max_blocks]: per-block LSE
   float* lse_final;           // optional [batch*num_heads]: final LSE for the score pass
@@ -63,6 +67,7 @@ struct DecodeParams {
   int32_t max_blocks;
   int32_t splits;
   int32_t chunk;              // blocks per claimed work chunk: 8, 16 or 32
+  int32_t group_size;         // splits merged per group (= splits: one level)
   int32_t out_dtype;
   float scale_log2;           // scaling * log2(e)
 };

@@ -260,3 +260,34 @@ def test_c1_config_against_reference_golden():
                                          num_splits=splits)
         torch.cuda.synchronize()
         _close(out, g["out"].astype(np.float32))
+
+
+@pytest.mark.parametrize("splits", [17, 74, 129, 200, 512])
+def test_split_merge_one_and_two_levels(splits):
+    """One merge level up to 128 splits, two above (groups of about
+    sqrt(splits), then across groups); many CTAs find no chunk to claim."""
+    case = make_case(seed=2000 + splits, batch=2, q_heads=32, kv_heads=8, head_dim=128,
+                     block_size=16, num_blocks=129)
+    ref, ref_lse, ref_scores = oracle_decode(case)
+    for _ in range(2):
+        out, scores, lse = _run(case, num_splits=splits, chunk_blocks=8, return_scores=True,
+                                return_lse=True)
+        _close(out, ref)
+        np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=1e-3, rtol=1e-4)
+        np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-4, rtol=1e-3)
+
+
+def test_one_workspace_serves_calls_of_any_shape():
+    """Calls of different batch sizes, split counts and score settings share
+    the stream's workspace in an order where a later call's work counters sit
+    where an earlier call would have put partial results."""
+    shapes = [(1, 130, True), (16, 40, False), (3, 5, True), (24, 74, True), (1, 2, False),
+              (16, 0, True)]
+    for i, (batch, splits, scores_on) in enumerate(shapes):
+        case = make_case(seed=3000 + i, batch=batch, q_heads=32, kv_heads=8, head_dim=128,
+                         block_size=16, num_blocks=97)
+        ref, _, ref_scores = oracle_decode(case)
+        out, scores, _ = _run(case, num_splits=splits, return_scores=scores_on)
+        _close(out, ref)
+        if scores_on:
+            np.testing.assert_allclose(scores.cpu().numpy(), ref_scores, atol=1e-4, rtol=1e-3)
