@@ -1,0 +1,291 @@
+"""One policy tick of the compact tiered pool, batched.
+
+Drop-in for ``TieredKVRuntime.sync_storage_states`` (tierkv_policy.py:1849-1867)
+over a ``CompactTieredKVTensorPool`` (tierkv_policy.py:701-1365).  The
+reference walks the layer's blocks one by one; every HOT->WARM demotion
+(``demote_to_warm``, 1042-1068) and WARM->HOT promotion (``promote_to_hot``,
+1087-1115) runs its own handful of torch kernels, and every metadata update
+(``_set_metadata``, 917-926; ``set_block_state``, 1037-1040) writes single
+elements of the GPU block tables.  Here the tick is split in two:
+
+* ``plan_sync`` replays the reference loop's bookkeeping exactly -- the same
+  checks and errors, the same LIFO slot pops and pushes (growing the pool by
+  the pool's own ``_alloc_*_slot`` when a free list runs dry), the same
+  physical-block dictionaries and storage sets -- but only records the data
+  moves and the table cells, in the reference's order;
+* ``apply_sync`` performs all demotions in one launch of the demotion kernel,
+  all promotions in one launch of the promotion kernel, and writes the table
+  cells with one host->device copy.
+
+Slot reuse inside one tick makes the reference's order matter: a demotion can
+free a HOT slot that a later promotion fills (and a promotion a WARM slot that
+a later demotion fills).  Such a move writes to a staging buffer first and is
+copied into its slot after every move has read its source, so each slot ends
+with exactly the bytes the sequential reference leaves there -- rows at or
+beyond a block's length included, which the reference never touches.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import ops
+
+HOT_STATE = 0
+WARM_STATE = 1
+COLD_STATE = 2
+
+
+@dataclass
+class SyncPlan:
+    """The data moves and table cells of one tick, in the reference's order."""
+
+    layer: int
+    demotions: list = field(default_factory=list)   # (hot slot, warm slot, length)
+    promotions: list = field(default_factory=list)  # (warm slot, hot slot, length)
+    states: dict = field(default_factory=dict)      # (layer, logical) -> state
+    slots: dict = field(default_factory=dict)       # (layer, logical) -> slot
+    lengths: dict = field(default_factory=dict)     # (layer, logical) -> length
+
+    def staged(self):
+        """(demotions, promotions) whose destination another move of the tick
+        reads: they go through staging."""
+        read_hot = {h for h, _, _ in self.demotions}
+        read_warm = {w for w, _, _ in self.promotions}
+        dem = [i for i, (_, w, _) in enumerate(self.demotions) if w in read_warm]
+        pro = [i for i, (_, h, _) in enumerate(self.promotions) if h in read_hot]
+        return dem, pro
+
+
+# ---------------------------------------------------------------------------
+# bookkeeping (the reference's pool methods without their data movement)
+# ---------------------------------------------------------------------------
+
+def _metadata(pool, plan: SyncPlan, physical_idx: int, state: int, slot: int, length: int) -> None:
+    """_set_metadata (tierkv_policy.py:917-926) with the table writes recorded."""
+    pool.physical_states[physical_idx] = int(state)
+    pool.physical_slots[physical_idx] = int(slot)
+    pool.physical_lengths[physical_idx] = int(length)
+    location = pool.physical_locations.get(physical_idx)
+    if location is not None and pool.is_allocated():
+        cell = (int(location[0]), int(location[1]))
+        plan.states[cell] = int(state)
+        plan.slots[cell] = int(slot)
+        plan.lengths[cell] = int(length)
+
+
+def _demote_to_warm(pool, plan: SyncPlan, physical_idx: int) -> None:
+    """demote_to_warm (tierkv_policy.py:1042-1068)."""
+    physical_idx = pool._check_physical_idx(physical_idx)
+    state = pool.get_physical_state(physical_idx)
+    if state == WARM_STATE:
+        return
+    if state == COLD_STATE:
+        raise KeyError(f"Physical block {physical_idx} is not eligible for WARM demotion from COLD storage.")
+    if state != HOT_STATE:
+        raise KeyError(f"Physical block {physical_idx} is not present in HOT storage.")
+    length = pool.get_block_length(physical_idx)
+    hot_slot = int(pool.physical_slots[physical_idx])
+    warm_slot = int(pool._alloc_warm_slot())
+    plan.demotions.append((hot_slot, warm_slot, int(length)))
+    pool._free_hot_slot(hot_slot)
+    pool.hot_storage.discard(physical_idx)
+    pool.warm_storage.add(physical_idx)
+    pool.cold_storage.discard(physical_idx)
+    _metadata(pool, plan, physical_idx, WARM_STATE, warm_slot, length)
+
+
+def _demote_to_cold(pool, plan: SyncPlan, physical_idx: int) -> None:
+    """demote_to_cold (tierkv_policy.py:1070-1085): frees the slot, moves nothing."""
+    physical_idx = pool._check_physical_idx(physical_idx)
+    state = pool.get_physical_state(physical_idx)
+    if state == COLD_STATE:
+        return
+    if state == HOT_STATE:
+        pool._free_hot_slot(pool.physical_slots.get(physical_idx, -1))
+    elif state == WARM_STATE:
+        pool._free_warm_slot(pool.physical_slots.get(physical_idx, -1))
+    elif state is None:
+        raise KeyError(f"Physical block {physical_idx} is not present in HOT or WARM storage.")
+    length = pool.get_block_length(physical_idx)
+    pool.hot_storage.discard(physical_idx)
+    pool.warm_storage.discard(physical_idx)
+    pool.cold_storage.add(physical_idx)
+    _metadata(pool, plan, physical_idx, COLD_STATE, -1, length)
+
+
+def _promote_to_hot(pool, plan: SyncPlan, physical_idx: int) -> None:
+    """promote_to_hot (tierkv_policy.py:1087-1115)."""
+    physical_idx = pool._check_physical_idx(physical_idx)
+    state = pool.get_physical_state(physical_idx)
+    if state == HOT_STATE:
+        return
+    if state == COLD_STATE:
+        raise KeyError(f"Physical block {physical_idx} is not eligible for HOT promotion from COLD storage.")
+    if state != WARM_STATE:
+        raise KeyError(f"Physical block {physical_idx} is not present in WARM storage.")
+    length = pool.get_block_length(physical_idx)
+    warm_slot = int(pool.physical_slots[physical_idx])
+    hot_slot = int(pool._alloc_hot_slot())
+    plan.promotions.append((warm_slot, hot_slot, int(length)))
+    pool._free_warm_slot(warm_slot)
+    pool.hot_storage.add(physical_idx)
+    pool.warm_storage.discard(physical_idx)
+    pool.cold_storage.discard(physical_idx)
+    _metadata(pool, plan, physical_idx, HOT_STATE, hot_slot, length)
+
+
+def plan_sync(pool, layer_idx: int, physical_indices, states) -> SyncPlan:
+    """The loop of sync_storage_states (tierkv_policy.py:1849-1867), recording
+    moves and table cells instead of performing them.  Updates the pool's
+    bookkeeping (free lists, dictionaries, storage sets) in place, exactly as
+    the reference does, and may grow its tensors through the pool's own slot
+    allocators."""
+    plan = SyncPlan(int(layer_idx))
+    for logical_idx, (physical_idx, state) in enumerate(zip(physical_indices, states)):
+        physical_idx = int(physical_idx)
+        state = int(state)
+        current_state = pool.get_physical_state(physical_idx)
+        if state == HOT_STATE:
+            if current_state == WARM_STATE:
+                _promote_to_hot(pool, plan, physical_idx)
+            elif current_state == COLD_STATE:
+                raise KeyError(f"Physical block {physical_idx} cannot be promoted from COLD to HOT.")
+        elif state == COLD_STATE and current_state != COLD_STATE:
+            _demote_to_cold(pool, plan, physical_idx)
+        elif state == WARM_STATE:
+            if current_state == HOT_STATE:
+                _demote_to_warm(pool, plan, physical_idx)
+            elif current_state == COLD_STATE:
+                raise KeyError(f"Physical block {physical_idx} cannot be promoted from COLD to WARM.")
+        # set_block_state (tierkv_policy.py:1037-1040)
+        if not pool.is_allocated():
+            raise RuntimeError("CompactTieredKVTensorPool has not been allocated yet.")
+        plan.states[(int(layer_idx), logical_idx)] = state
+    return plan
+
+
+# ---------------------------------------------------------------------------
+# data movement and table writes
+# ---------------------------------------------------------------------------
+
+def _pools(pool) -> ops.TieredPools:
+    return ops.TieredPools(pool.hot_k_pool, pool.hot_v_pool, pool.warm_k_pool, pool.warm_v_pool,
+                           pool.k_scale, pool.k_zero, pool.v_scale, pool.v_zero)
+
+
+def _rows(slots, lengths, kv_heads: int, block_size: int) -> torch.Tensor:
+    """Flat row indices (slot, head, t < length) of [slots, heads, bs, *] tensors."""
+    out = []
+    for slot, length in zip(slots, lengths):
+        for h in range(kv_heads):
+            base = (slot * kv_heads + h) * block_size
+            out.extend(range(base, base + length))
+    return torch.tensor(out, dtype=torch.int64)
+
+
+def apply_sync(pool, plan: SyncPlan, stream=None) -> dict:
+    """Performs the plan's moves (one demotion and one promotion launch, plus
+    staging copies for reused slots) and writes its table cells.  Returns
+    counts of the moves, for tests and logs."""
+    n_dem, n_pro = len(plan.demotions), len(plan.promotions)
+    staged_dem, staged_pro = plan.staged()
+    if n_dem or n_pro:
+        if not pool.hot_k_pool.is_cuda:
+            raise ValueError("TierKV storage sync requires CUDA pool tensors.")
+        pools = _pools(pool)
+        dev = pools.device
+        kvh, bs, d = pools.kv_heads, pools.block_size, pools.head_dim
+        sd, sp = set(staged_dem), set(staged_pro)
+        direct_dem = [m for i, m in enumerate(plan.demotions) if i not in sd]
+        direct_pro = [m for i, m in enumerate(plan.promotions) if i not in sp]
+        # phase 1: every move reads its source; direct moves write their slot
+        # (no move of this tick reads it), staged moves write staging
+        stage_w = stage_h = None
+        if direct_dem:
+            h, w, n = zip(*direct_dem)
+            ops.demote_blocks_to_warm(pools, list(h), list(w), list(n), stream=stream)
+        if staged_dem:
+            moves = [plan.demotions[i] for i in staged_dem]
+            stage_w = ops.TieredPools.allocate(1, len(moves), kvh, bs, d, dev)
+            view = ops.TieredPools(pool.hot_k_pool, pool.hot_v_pool, stage_w.warm_k, stage_w.warm_v,
+                                   stage_w.k_scale, stage_w.k_zero, stage_w.v_scale, stage_w.v_zero)
+            ops.demote_blocks_to_warm(view, [m[0] for m in moves], list(range(len(moves))),
+                                      [m[2] for m in moves], stream=stream)
+        if direct_pro:
+            w, h, n = zip(*direct_pro)
+            ops.promote_blocks_to_hot(pools, list(w), list(h), list(n), stream=stream)
+        if staged_pro:
+            moves = [plan.promotions[i] for i in staged_pro]
+            stage_h = ops.TieredPools.allocate(len(moves), 1, kvh, bs, d, dev)
+            view = ops.TieredPools(stage_h.hot_k, stage_h.hot_v, pool.warm_k_pool, pool.warm_v_pool,
+                                   pool.k_scale, pool.k_zero, pool.v_scale, pool.v_zero)
+            ops.promote_blocks_to_hot(view, [m[0] for m in moves], list(range(len(moves))),
+                                      [m[2] for m in moves], stream=stream)
+        # phase 2: staged results into their slots, rows below the length only
+        with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+            if staged_dem:
+                moves = [plan.demotions[i] for i in staged_dem]
+                dst = _rows([m[1] for m in moves], [m[2] for m in moves], kvh, bs).to(dev)
+                src = _rows(range(len(moves)), [m[2] for m in moves], kvh, bs).to(dev)
+                for real, st, width in ((pool.warm_k_pool, stage_w.warm_k, d),
+                                        (pool.warm_v_pool, stage_w.warm_v, d),
+                                        (pool.k_scale, stage_w.k_scale, 1), (pool.k_zero, stage_w.k_zero, 1),
+                                        (pool.v_scale, stage_w.v_scale, 1), (pool.v_zero, stage_w.v_zero, 1)):
+                    real.view(-1, width).index_copy_(0, dst, st.view(-1, width).index_select(0, src))
+            if staged_pro:
+                moves = [plan.promotions[i] for i in staged_pro]
+                dst = _rows([m[1] for m in moves], [m[2] for m in moves], kvh, bs).to(dev)
+                src = _rows(range(len(moves)), [m[2] for m in moves], kvh, bs).to(dev)
+                for real, st in ((pool.hot_k_pool, stage_h.hot_k), (pool.hot_v_pool, stage_h.hot_v)):
+                    real.view(-1, d).index_copy_(0, dst, st.view(-1, d).index_select(0, src))
+    _write_tables(pool, plan, stream)
+    return {"demotions": n_dem, "promotions": n_pro, "staged_demotions": len(staged_dem),
+            "staged_promotions": len(staged_pro)}
+
+
+class _nullcontext:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+def _write_tables(pool, plan: SyncPlan, stream=None) -> None:
+    """The recorded cells of block_states / block_slot_indices / block_lengths,
+    last write winning as in the reference, in one host->device copy."""
+    groups = [(pool.block_states, plan.states), (pool.block_slot_indices, plan.slots),
+              (pool.block_lengths, plan.lengths)]
+    groups = [(t, cells) for t, cells in groups if cells]
+    if not groups:
+        return
+    width = int(pool.block_states.shape[1])
+    flat = []
+    for _, cells in groups:
+        flat.extend(l * width + i for (l, i) in cells)
+        flat.extend(cells.values())
+    dev = pool.block_states.device
+    host = torch.tensor(flat, dtype=torch.int64)
+    if dev.type == "cuda":
+        host = host.pin_memory()
+    with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+        buf = host.to(dev, non_blocking=True)
+        off = 0
+        for table, cells in groups:
+            n = len(cells)
+            idx, val = buf[off:off + n], buf[off + n:off + 2 * n]
+            off += 2 * n
+            table.view(-1).index_copy_(0, idx, val.to(table.dtype))
+
+
+def sync_storage_states(self, seq_id: int) -> None:
+    """Method-compatible replacement of TieredKVRuntime.sync_storage_states
+    (tierkv_policy.py:1849-1867): ``TieredKVRuntime.sync_storage_states =
+    paged_tierkv_b200.tiering.sync_storage_states``."""
+    physical_indices = self.block_manager.get_physical_indices(seq_id)
+    states = self.block_manager.get_states(seq_id)
+    plan = plan_sync(self.kv_pool, seq_id, physical_indices, states)
+    apply_sync(self.kv_pool, plan)

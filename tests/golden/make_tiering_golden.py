@@ -1,0 +1,168 @@
+"""Golden fixtures for the batched storage sync, made by the reference itself.
+
+Usage (only where a checkout of xiaoMartintin/Paged_TierKV is available):
+
+    python tests/golden/make_tiering_golden.py --reference <path-to-Paged_TierKV>
+
+For each scenario it builds a ``CompactTieredKVTensorPool``
+(tierkv_policy.py:701-1365) on the CPU through the reference's own
+``write_hot_tokens`` / ``set_block_entry`` / ``demote_to_warm`` /
+``demote_to_cold``, records the pool's complete state, then runs the
+reference's ``TieredKVRuntime.sync_storage_states`` (tierkv_policy.py:1849-1867,
+called unbound with a stand-in block manager that returns the scenario's
+physical indices and desired states) and records the complete state again.
+A state is the slot bookkeeping (free lists, per-physical state / slot /
+length / location, storage sets, allocated capacities), the layer tables and
+every pool tensor, so the fixture pins slot numbering (LIFO reuse, growth by
+chunks) and every stored byte, stale rows of reused slots included.
+
+Scenarios (seeded): LIFO reuse in both directions within one sync (a
+demotion frees a HOT slot a later promotion takes, and the reverse), pool
+growth during the sync, partial blocks, HOT->COLD and WARM->COLD, no-ops.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import types
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+HOT, WARM, COLD = 0, 1, 2
+
+
+def _state(pool):
+    book = {
+        "hot_free_slots": [int(x) for x in pool.hot_free_slots],
+        "warm_free_slots": [int(x) for x in pool.warm_free_slots],
+        "physical_states": {str(k): int(v) for k, v in pool.physical_states.items()},
+        "physical_slots": {str(k): int(v) for k, v in pool.physical_slots.items()},
+        "physical_lengths": {str(k): int(v) for k, v in pool.physical_lengths.items()},
+        "physical_locations": {str(k): [int(v[0]), int(v[1])] for k, v in pool.physical_locations.items()},
+        "hot_storage": sorted(int(x) for x in pool.hot_storage),
+        "warm_storage": sorted(int(x) for x in pool.warm_storage),
+        "cold_storage": sorted(int(x) for x in pool.cold_storage),
+        "allocated_hot_slots": int(pool.allocated_hot_slots),
+        "allocated_warm_slots": int(pool.allocated_warm_slots),
+    }
+    arrays = {
+        "hot_k": pool.hot_k_pool, "hot_v": pool.hot_v_pool, "warm_k": pool.warm_k_pool,
+        "warm_v": pool.warm_v_pool, "k_scale": pool.k_scale, "k_zero": pool.k_zero,
+        "v_scale": pool.v_scale, "v_zero": pool.v_zero,
+        "block_states": pool.block_states, "block_slot_indices": pool.block_slot_indices,
+        "block_lengths": pool.block_lengths, "physical_block_tables": pool.physical_block_tables,
+    }
+    return book, {k: v.detach().cpu().numpy().copy() for k, v in arrays.items()}
+
+
+def build(tp, torch, *, seed, n_blocks, kv_heads, head_dim, block_size, chunk, partial_every,
+          initial_warm, initial_cold, desired_fn):
+    rng = np.random.default_rng(seed)
+    gen = torch.Generator().manual_seed(seed)
+    pool = tp.CompactTieredKVTensorPool(num_layers=1, block_size=block_size,
+                                        max_seq_len=block_size * n_blocks, pool_blocks=n_blocks + 8,
+                                        pool_chunk_blocks=chunk)
+    physical = rng.permutation(n_blocks + 8)[:n_blocks].tolist()  # physical ids != logical ids
+    for logical, p in enumerate(physical):
+        length = block_size if (partial_every == 0 or logical % partial_every) else int(rng.integers(1, block_size))
+        k = torch.randn((1, kv_heads, length, head_dim), generator=gen).to(torch.float16)
+        v = torch.randn((1, kv_heads, length, head_dim), generator=gen).to(torch.float16)
+        pool.write_hot_tokens(p, 0, k, v)
+        pool.set_block_entry(0, logical, p, HOT)
+    # initial tiering in a shuffled order, so the free lists are not sorted
+    order = rng.permutation(n_blocks).tolist()
+    states = [HOT] * n_blocks
+    for logical in order:
+        if logical in initial_warm:
+            pool.demote_to_warm(physical[logical])
+            pool.set_block_state(0, logical, WARM)
+            states[logical] = WARM
+        elif logical in initial_cold:
+            pool.demote_to_cold(physical[logical])
+            pool.set_block_state(0, logical, COLD)
+            states[logical] = COLD
+    before_book, before = _state(pool)
+    desired = desired_fn(states, rng)
+    bm = types.SimpleNamespace(get_physical_indices=lambda seq_id: list(physical),
+                               get_states=lambda seq_id: list(desired))
+    runtime = types.SimpleNamespace(block_manager=bm, kv_pool=pool)
+    tp.TieredKVRuntime.sync_storage_states(runtime, 0)
+    after_book, after = _state(pool)
+    meta = {
+        "seed": seed, "kv_heads": kv_heads, "head_dim": head_dim, "block_size": block_size,
+        "num_layers": 1, "max_blocks_per_layer": int(pool.max_blocks_per_layer),
+        "max_hot_slots": int(pool.max_hot_slots), "max_warm_slots": int(pool.max_warm_slots),
+        "hot_chunk_slots": int(pool.hot_chunk_slots), "warm_chunk_slots": int(pool.warm_chunk_slots),
+        "layer": 0, "physical_indices": [int(x) for x in physical], "desired": [int(x) for x in desired],
+        "before": before_book, "after": after_book,
+    }
+    out = {"meta": np.array(json.dumps(meta))}
+    out.update({f"before_{k}": v for k, v in before.items()})
+    out.update({f"after_{k}": v for k, v in after.items()})
+    return out
+
+
+def _swap(states, rng):
+    """Swap tiers: some HOT become WARM (and COLD), some WARM become HOT (and COLD)."""
+    out = list(states)
+    for i, s in enumerate(states):
+        r = rng.random()
+        if s == HOT:
+            out[i] = WARM if r < 0.45 else (COLD if r < 0.55 else HOT)
+        elif s == WARM:
+            out[i] = HOT if r < 0.45 else (COLD if r < 0.6 else WARM)
+    return out
+
+
+def _demote_many(states, rng):
+    """Most HOT blocks go WARM: the WARM pool has to grow during the sync."""
+    return [WARM if (s == HOT and rng.random() < 0.8) else s for s in states]
+
+
+def _alternate(states, rng):
+    """Alternating demotion / promotion in logical order (chains of slot reuse)."""
+    out = list(states)
+    for i, s in enumerate(states):
+        if s == HOT and i % 2 == 0:
+            out[i] = WARM
+        elif s == WARM and i % 2 == 1:
+            out[i] = HOT
+    return out
+
+
+SCENARIOS = {
+    "tiering_swap": dict(seed=101, n_blocks=24, kv_heads=2, head_dim=64, block_size=16, chunk=4,
+                         partial_every=5, initial_warm=set(range(3, 20, 2)),
+                         initial_cold={4, 10, 16}, desired_fn=_swap),
+    "tiering_grow": dict(seed=202, n_blocks=20, kv_heads=1, head_dim=128, block_size=16, chunk=3,
+                         partial_every=4, initial_warm={1, 2}, initial_cold={7},
+                         desired_fn=_demote_many),
+    "tiering_alternate": dict(seed=303, n_blocks=18, kv_heads=1, head_dim=64, block_size=32, chunk=5,
+                              partial_every=6, initial_warm=set(range(1, 18, 2)), initial_cold=set(),
+                              desired_fn=_alternate),
+}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of a Paged_TierKV checkout (read-only)")
+    args = ap.parse_args(argv)
+    sys.path.insert(0, os.path.abspath(args.reference))
+    import torch
+    import tierkv_policy as tp  # noqa: E402  (the reference)
+    for name, kw in SCENARIOS.items():
+        out = build(tp, torch, **kw)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **out)
+        meta = json.loads(str(out["meta"]))
+        print(name, os.path.getsize(path), "bytes; desired", meta["desired"])
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

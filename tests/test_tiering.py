@@ -1,0 +1,114 @@
+"""Batched storage sync (one policy tick) against the reference's own result.
+
+Golden fixtures (tests/golden/make_tiering_golden.py) hold a compact pool's
+complete state before and after the reference's ``sync_storage_states``
+(tierkv_policy.py:1849-1867).  The CPU tests replay the bookkeeping and the
+table cells; the GPU tests also move the data with the batched kernels and
+compare every pool byte, stale rows of reused slots included.
+"""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from compact_pool_stub import CompactPoolStub  # noqa: E402
+from paged_tierkv_b200 import tiering  # noqa: E402
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "tiering_*.npz")))
+TABLES = ("block_states", "block_slot_indices", "block_lengths")
+
+
+def _load(path):
+    return dict(np.load(path))
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=lambda p: os.path.basename(p)[:-4])
+def test_bookkeeping_matches_reference(path):
+    fx = _load(path)
+    pool = CompactPoolStub(fx, "cpu")
+    meta = pool.meta
+    plan = tiering.plan_sync(pool, meta["layer"], meta["physical_indices"], meta["desired"])
+    assert pool.bookkeeping() == meta["after"]
+    # the recorded cells turn the "before" tables into the "after" tables
+    for name, cells in zip(TABLES, (plan.states, plan.slots, plan.lengths)):
+        table = fx[f"before_{name}"].copy()
+        for (layer, logical), v in cells.items():
+            table[layer, logical] = v
+        np.testing.assert_array_equal(table, fx[f"after_{name}"], err_msg=name)
+
+
+def test_fixtures_cover_slot_reuse_and_growth():
+    """The scenarios exercise what the staging and growth paths are for."""
+    staged_dem = staged_pro = grown = 0
+    for path in FIXTURES:
+        fx = _load(path)
+        pool = CompactPoolStub(fx, "cpu")
+        meta = pool.meta
+        before = (pool.allocated_hot_slots, pool.allocated_warm_slots)
+        plan = tiering.plan_sync(pool, meta["layer"], meta["physical_indices"], meta["desired"])
+        d, p = plan.staged()
+        staged_dem += len(d)
+        staged_pro += len(p)
+        grown += (pool.allocated_hot_slots, pool.allocated_warm_slots) != before
+    assert staged_dem > 0 and staged_pro > 0 and grown > 0
+
+
+def test_cold_to_hot_is_rejected_like_the_reference():
+    fx = _load(os.path.join(GOLDEN, "tiering_swap.npz"))
+    pool = CompactPoolStub(fx, "cpu")
+    meta = pool.meta
+    cold = [i for i, p in enumerate(meta["physical_indices"])
+            if meta["before"]["physical_states"][str(p)] == tiering.COLD_STATE]
+    desired = list(meta["desired"])
+    desired[cold[0]] = tiering.HOT_STATE
+    with pytest.raises(KeyError, match="cannot be promoted from COLD to HOT"):
+        tiering.plan_sync(pool, meta["layer"], meta["physical_indices"], desired)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("path", FIXTURES, ids=lambda p: os.path.basename(p)[:-4])
+def test_batched_sync_matches_reference_bytes(path):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    fx = _load(path)
+    pool = CompactPoolStub(fx, "cuda")
+    meta = pool.meta
+    plan = tiering.plan_sync(pool, meta["layer"], meta["physical_indices"], meta["desired"])
+    stats = tiering.apply_sync(pool, plan)
+    torch.cuda.synchronize()
+    assert stats["demotions"] + stats["promotions"] > 0
+    assert pool.bookkeeping() == meta["after"]
+    got = {"hot_k": pool.hot_k_pool, "hot_v": pool.hot_v_pool, "warm_k": pool.warm_k_pool,
+           "warm_v": pool.warm_v_pool, "k_scale": pool.k_scale, "k_zero": pool.k_zero,
+           "v_scale": pool.v_scale, "v_zero": pool.v_zero, "block_states": pool.block_states,
+           "block_slot_indices": pool.block_slot_indices, "block_lengths": pool.block_lengths,
+           "physical_block_tables": pool.physical_block_tables}
+    for name, t in got.items():
+        want = fx[f"after_{name}"]
+        have = t.cpu().numpy()
+        assert have.shape == want.shape, name
+        # compare bit patterns (signed zeros, NaN payloads)
+        np.testing.assert_array_equal(have.view(np.uint8), want.view(np.uint8), err_msg=name)
+
+
+@pytest.mark.gpu
+def test_runtime_method_drop_in():
+    """sync_storage_states bound to a runtime-like object, as the reference calls it."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import types
+    fx = _load(FIXTURES[0])
+    pool = CompactPoolStub(fx, "cuda")
+    meta = pool.meta
+    bm = types.SimpleNamespace(get_physical_indices=lambda s: list(meta["physical_indices"]),
+                               get_states=lambda s: list(meta["desired"]))
+    runtime = types.SimpleNamespace(block_manager=bm, kv_pool=pool)
+    tiering.sync_storage_states(runtime, meta["layer"])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(pool.warm_k_pool.cpu().numpy(), fx["after_warm_k"])
+    np.testing.assert_array_equal(pool.block_states.cpu().numpy(), fx["after_block_states"])
