@@ -25,6 +25,9 @@
  *                          329-361 (dense pool) demote_to_warm(), batched
  *   tkv_promote_to_hot     tierkv_policy.py:1087-1115 (compact) and 375-402
  *                          (dense) promote_to_hot(), batched
+ *   tkv_append_hot_tokens  tierkv_policy.py:934-967 write_hot_tokens() tensor
+ *                          work plus the block-table writes of _set_metadata
+ *                          (917-926) and set_block_entry (1016-1035), fused
  *
  * Pool layout (the reference's, tierkv_policy.py:129-135 and 835-841):
  *   hot_k / hot_v     [hot_slots,  kv_heads, block_size, head_dim] fp16
@@ -200,6 +203,28 @@ int32_t tkv_demote_to_warm(const tkv_pools* pools, const int32_t* src_hot_slots,
 int32_t tkv_promote_to_hot(const tkv_pools* pools, const int32_t* src_warm_slots,
                            const int32_t* dst_hot_slots, const int32_t* lengths,
                            int32_t count, void* stream);
+
+/* One int32 table cell for tkv_append_hot_tokens: table[index] = value. */
+typedef struct tkv_table_cell {
+    int32_t* table;   /* device pointer to an int32 table */
+    int64_t  index;   /* element index */
+    int32_t  value;
+    int32_t  reserved;
+} tkv_table_cell;
+
+#define TKV_APPEND_MAX_CELLS 8
+
+/* Decode-time KV append in one launch: rows [start, start + tokens) of HOT
+ * slot hot_slot get the new key / value rows ([kv_heads, tokens, head_dim]
+ * fp16, contiguous, 16-byte aligned), rows [start + tokens, block_size) are
+ * zeroed (as write_hot_tokens does, tierkv_policy.py:956-958), and up to
+ * TKV_APPEND_MAX_CELLS block-table cells are written (the GPU-table updates of
+ * _set_metadata and set_block_entry, passed by value: no host->device copy).
+ * Replaces the tensor work of tierkv_policy.py:934-967 plus 917-926 and
+ * 1016-1035; the slot bookkeeping stays with the caller. */
+int32_t tkv_append_hot_tokens(const tkv_pools* pools, int32_t hot_slot, int32_t start,
+                              int32_t tokens, const void* key, const void* value,
+                              const tkv_table_cell* cells, int32_t n_cells, void* stream);
 
 /* Reads and clears the device error bits (TKV_DEVERR_*) that decode calls
  * using this workspace have recorded.  Synchronizes the stream. */

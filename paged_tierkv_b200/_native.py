@@ -42,7 +42,10 @@ EXPORTED_SYMBOLS = (
     "tkv_promote_to_hot",
     "tkv_read_device_errors",
     "tkv_decode_attention_noalloc",
+    "tkv_append_hot_tokens",
 )
+
+TKV_APPEND_MAX_CELLS = 8
 
 
 class TkvPools(ctypes.Structure):
@@ -90,6 +93,15 @@ class TkvDecodeArgs(ctypes.Structure):
     ]
 
 
+class TkvTableCell(ctypes.Structure):
+    _fields_ = [
+        ("table", ctypes.c_void_p),
+        ("index", ctypes.c_int64),
+        ("value", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 _LIB = None
 
 
@@ -127,6 +139,8 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
         "tkv_read_device_errors": ([vp, ctypes.POINTER(ctypes.c_uint32), vp], i32),
         "tkv_decode_attention_noalloc": ([ctypes.POINTER(TkvPools), ctypes.POINTER(TkvDecodeArgs),
                                           vp], i32),
+        "tkv_append_hot_tokens": ([ctypes.POINTER(TkvPools), i32, i32, i32, vp, vp,
+                                   ctypes.POINTER(TkvTableCell), i32, vp], i32),
     }
     for name, (argtypes, restype) in sigs.items():
         fn = getattr(lib, name)

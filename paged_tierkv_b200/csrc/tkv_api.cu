@@ -512,6 +512,42 @@ int32_t tkv_promote_to_hot(const tkv_pools* pools, const int32_t* src_warm_slots
   return cuda_status(launch_promote(p, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int32_t tkv_append_hot_tokens(const tkv_pools* pools, int32_t hot_slot, int32_t start,
+                              int32_t tokens, const void* key, const void* value,
+                              const tkv_table_cell* cells, int32_t n_cells, void* stream) {
+  if (!pools || !pools->hot_k || !pools->hot_v || !key || !value) return TKV_ERR_INVALID;
+  if (pools->kv_heads <= 0 || pools->block_size <= 0 || pools->hot_slots <= 0) return TKV_ERR_INVALID;
+  if (pools->head_dim <= 0 || pools->head_dim % 8 != 0) return TKV_ERR_UNSUPPORTED;
+  if (hot_slot < 0 || hot_slot >= pools->hot_slots) return TKV_ERR_INVALID;
+  if (start < 0 || tokens < 1 || start + tokens > pools->block_size) return TKV_ERR_INVALID;
+  if (!aligned(pools->hot_k, 16) || !aligned(pools->hot_v, 16) || !aligned(key, 16) ||
+      !aligned(value, 16))
+    return TKV_ERR_INVALID;
+  if (n_cells < 0 || n_cells > TKV_APPEND_MAX_CELLS || (n_cells > 0 && !cells)) return TKV_ERR_INVALID;
+  AppendParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.hot_k = pools->hot_k;
+  p.hot_v = pools->hot_v;
+  p.key = key;
+  p.value = value;
+  p.slot = hot_slot;
+  p.start = start;
+  p.tokens = tokens;
+  p.kv_heads = pools->kv_heads;
+  p.block_size = pools->block_size;
+  p.head_dim = pools->head_dim;
+  p.n_cells = n_cells;
+  for (int i = 0; i < n_cells; ++i) {
+    if (!cells[i].table || cells[i].index < 0 || !aligned(cells[i].table, 4)) return TKV_ERR_INVALID;
+    p.cell_ptr[i] = cells[i].table + cells[i].index;
+    p.cell_val[i] = cells[i].value;
+  }
+  int sms = 0;
+  const int32_t st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+  return cuda_status(launch_append(p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream) {
   if (!workspace || !bits_out) return TKV_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

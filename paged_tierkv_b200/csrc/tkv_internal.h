@@ -139,7 +139,24 @@ cudaError_t launch_scores(const ScoreParams& p, cudaStream_t stream);
 cudaError_t launch_block_scores(const BlockScoreParams& p, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const void* x, int64_t rows, int dim, void* codes, void* scale,
                                  void* zero, cudaStream_t stream);
+struct AppendParams {
+  void* hot_k;
+  void* hot_v;
+  const void* key;            // [kv_heads, tokens, head_dim] fp16
+  const void* value;
+  int64_t slot;
+  int32_t start;
+  int32_t tokens;
+  int32_t kv_heads;
+  int32_t block_size;
+  int32_t head_dim;
+  int32_t n_cells;
+  int32_t* cell_ptr[8];       // table + index, resolved on the host
+  int32_t cell_val[8];
+};
+
 cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream);
+cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_promote(const DemoteParams& p, cudaStream_t stream);
 
 }  // namespace tkv

@@ -438,4 +438,29 @@ cudaError_t launch_promote(const DemoteParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- decode append
+// One CTA per (kv head, K/V): rows [start, start + tokens) of the HOT slot get
+// the new rows, rows [start + tokens, block_size) are zeroed
+// (tierkv_policy.py:954-958), 16 bytes per thread-step; CTA (0, 0) also writes
+// the block-table cells.
+__global__ void __launch_bounds__(128) append_kernel(const AppendParams p) {
+  const int h = blockIdx.x;
+  const int kind = blockIdx.y;
+  const int vpr = p.head_dim / 8;  // 16-byte vectors per row
+  uint4* dst = reinterpret_cast<uint4*>(kind ? p.hot_v : p.hot_k) +
+               ((p.slot * p.kv_heads + h) * p.block_size + p.start) * vpr;
+  const uint4* src = reinterpret_cast<const uint4*>(kind ? p.value : p.key) +
+                     (size_t)h * p.tokens * vpr;
+  const int n = (p.block_size - p.start) * vpr;
+  const int fill = p.tokens * vpr;
+  for (int e = threadIdx.x; e < n; e += blockDim.x)
+    dst[e] = e < fill ? __ldg(src + e) : make_uint4(0u, 0u, 0u, 0u);
+  if (h == 0 && kind == 0 && threadIdx.x < p.n_cells) *p.cell_ptr[threadIdx.x] = p.cell_val[threadIdx.x];
+}
+
+cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
+  append_kernel<<<dim3((unsigned)p.kv_heads, 2), 128, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace tkv

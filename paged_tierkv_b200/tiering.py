@@ -1,4 +1,4 @@
-"""One policy tick of the compact tiered pool, batched.
+"""One policy tick of the compact tiered pool, batched; fused decode append.
 
 Drop-in for ``TieredKVRuntime.sync_storage_states`` (tierkv_policy.py:1849-1867)
 over a ``CompactTieredKVTensorPool`` (tierkv_policy.py:701-1365).  The
@@ -23,6 +23,13 @@ a later demotion fills).  Such a move writes to a staging buffer first and is
 copied into its slot after every move has read its source, so each slot ends
 with exactly the bytes the sequential reference leaves there -- rows at or
 beyond a block's length included, which the reference never touches.
+
+The decode-time append (``append_to_layer``, tierkv_policy.py:1768-1816, with
+``write_hot_tokens`` 934-967 and ``set_block_entry`` 1016-1035) is split the
+same way: ``plan_append`` replays the bookkeeping (block-manager allocation,
+slot allocation, dictionaries) and ``apply_append`` issues one fused launch
+per block touched -- the new rows, the zeroed tail rows and every block-table
+cell the reference writes one element at a time.
 """
 
 from __future__ import annotations
@@ -48,6 +55,7 @@ class SyncPlan:
     states: dict = field(default_factory=dict)      # (layer, logical) -> state
     slots: dict = field(default_factory=dict)       # (layer, logical) -> slot
     lengths: dict = field(default_factory=dict)     # (layer, logical) -> length
+    physical: dict = field(default_factory=dict)    # (layer, logical) -> physical block
 
     def staged(self):
         """(demotions, promotions) whose destination another move of the tick
@@ -254,12 +262,15 @@ class _nullcontext:
         return False
 
 
+def _table_groups(pool, plan: SyncPlan):
+    return [(pool.block_states, plan.states), (pool.block_slot_indices, plan.slots),
+            (pool.block_lengths, plan.lengths), (pool.physical_block_tables, plan.physical)]
+
+
 def _write_tables(pool, plan: SyncPlan, stream=None) -> None:
     """The recorded cells of block_states / block_slot_indices / block_lengths,
     last write winning as in the reference, in one host->device copy."""
-    groups = [(pool.block_states, plan.states), (pool.block_slot_indices, plan.slots),
-              (pool.block_lengths, plan.lengths)]
-    groups = [(t, cells) for t, cells in groups if cells]
+    groups = [(t, cells) for t, cells in _table_groups(pool, plan) if cells]
     if not groups:
         return
     width = int(pool.block_states.shape[1])
@@ -289,3 +300,154 @@ def sync_storage_states(self, seq_id: int) -> None:
     states = self.block_manager.get_states(seq_id)
     plan = plan_sync(self.kv_pool, seq_id, physical_indices, states)
     apply_sync(self.kv_pool, plan)
+
+
+# ---------------------------------------------------------------------------
+# decode-time append
+# ---------------------------------------------------------------------------
+
+@dataclass
+class AppendStep:
+    """One block's share of an append: rows [start, start + key.shape[-2]) of
+    HOT slot `slot`, the table cells, and a promotion to run first (the open
+    block was WARM)."""
+
+    slot: int
+    start: int
+    key: torch.Tensor    # [1, kv_heads, take, head_dim] fp16, contiguous
+    value: torch.Tensor
+    plan: SyncPlan
+
+
+def _write_hot_tokens(pool, plan: SyncPlan, physical_idx: int, start: int,
+                      key_states: torch.Tensor, value_states: torch.Tensor):
+    """write_hot_tokens (tierkv_policy.py:934-967) without its tensor work:
+    returns (slot, key, value) after the reference's checks and bookkeeping."""
+    physical_idx = pool._check_physical_idx(physical_idx)
+    key_states, value_states = pool._coerce_kv(key_states, value_states)
+    pool._ensure_metadata(key_states)
+    start = int(start)
+    tokens = int(key_states.shape[-2])
+    if start < 0 or start + tokens > pool.block_size:
+        raise ValueError("KV write exceeds the physical block capacity.")
+    current_state = pool.get_physical_state(physical_idx)
+    if current_state == COLD_STATE:
+        raise KeyError(f"Physical block {physical_idx} is COLD and cannot be promoted.")
+    if current_state == WARM_STATE:
+        _promote_to_hot(pool, plan, physical_idx)
+    slot_idx = pool.physical_slots.get(physical_idx)
+    if slot_idx is None or current_state is None:
+        slot_idx = pool._alloc_hot_slot()
+    pool.hot_storage.add(physical_idx)
+    pool.warm_storage.discard(physical_idx)
+    pool.cold_storage.discard(physical_idx)
+    _metadata(pool, plan, physical_idx, HOT_STATE, slot_idx, start + tokens)
+    return int(slot_idx), key_states, value_states
+
+
+def _set_block_entry(pool, plan: SyncPlan, layer_idx: int, logical_idx: int, physical_idx: int,
+                     state: int) -> None:
+    """set_block_entry (tierkv_policy.py:1016-1035) with the table writes recorded."""
+    if not pool.is_allocated():
+        raise RuntimeError("CompactTieredKVTensorPool has not been allocated yet.")
+    layer_idx = int(layer_idx)
+    logical_idx = int(logical_idx)
+    physical_idx = pool._check_physical_idx(physical_idx)
+    if layer_idx < 0 or layer_idx >= pool.num_layers:
+        raise ValueError("layer_idx is out of range.")
+    if logical_idx < 0 or logical_idx >= pool.max_blocks_per_layer:
+        raise RuntimeError(
+            f"Logical block {logical_idx} exceeds max_blocks_per_layer={pool.max_blocks_per_layer}.")
+    pool.physical_locations[physical_idx] = (layer_idx, logical_idx)
+    cell = (layer_idx, logical_idx)
+    plan.physical[cell] = physical_idx
+    plan.states[cell] = int(state)
+    plan.slots[cell] = int(pool.physical_slots.get(physical_idx, -1))
+    plan.lengths[cell] = int(pool.physical_lengths.get(physical_idx, 0))
+
+
+def plan_append(self, seq_id: int, key_states: torch.Tensor, value_states: torch.Tensor):
+    """The bookkeeping of append_to_layer (tierkv_policy.py:1768-1816) on a
+    runtime (``layer_states``, ``block_manager``, ``kv_pool``, ``block_size``,
+    ``max_blocks_per_layer``).  Returns (steps, allocated_new_block)."""
+    if key_states.shape[-2] != value_states.shape[-2]:
+        raise ValueError("Key and value states must have the same sequence length.")
+    pool = self.kv_pool
+    layer_state = self.layer_states[seq_id]
+    offset = 0
+    total_tokens = int(key_states.shape[-2])
+    allocated_new_block = False
+    steps = []
+    while offset < total_tokens:
+        new_logical_idx = None
+        if layer_state.open_physical_idx is None:
+            layer_state.open_physical_idx = self.block_manager.allocate_block(seq_id)
+            layer_state.open_token_count = 0
+            allocated_new_block = True
+            new_logical_idx = layer_state.num_blocks
+            if new_logical_idx >= self.max_blocks_per_layer:
+                raise RuntimeError(
+                    f"Layer {seq_id} exceeded max_blocks_per_layer={self.max_blocks_per_layer}.")
+            pool._check_physical_idx(layer_state.open_physical_idx)
+        physical_idx = layer_state.open_physical_idx
+        plan = SyncPlan(int(seq_id))
+        if pool.get_physical_state(physical_idx) == WARM_STATE:
+            _promote_to_hot(pool, plan, physical_idx)
+        remaining_capacity = self.block_size - layer_state.open_token_count
+        take = min(remaining_capacity, total_tokens - offset)
+        k_chunk = key_states[:, :, offset:offset + take, :].contiguous()
+        v_chunk = value_states[:, :, offset:offset + take, :].contiguous()
+        start = layer_state.open_token_count
+        slot, k_chunk, v_chunk = _write_hot_tokens(pool, plan, physical_idx, start, k_chunk, v_chunk)
+        if new_logical_idx is not None:
+            _set_block_entry(pool, plan, seq_id, new_logical_idx, physical_idx, HOT_STATE)
+            layer_state.num_blocks += 1
+        steps.append(AppendStep(slot, start, k_chunk, v_chunk, plan))
+        layer_state.open_token_count += take
+        offset += take
+        if layer_state.open_token_count == self.block_size:
+            layer_state.open_physical_idx = None
+            layer_state.open_token_count = 0
+    return steps, allocated_new_block
+
+
+def apply_append(pool, steps, stream=None) -> int:
+    """One fused launch per step (after its promotion, if any); returns the
+    number of launches."""
+    from . import _native as N
+    import ctypes
+    launches = 0
+    for step in steps:
+        if step.plan.promotions:
+            w, h, n = zip(*step.plan.promotions)
+            ops.promote_blocks_to_hot(_pools(pool), list(w), list(h), list(n), stream=stream)
+            launches += 1
+        if not (step.key.is_cuda and pool.hot_k_pool.is_cuda):
+            raise ValueError("TierKV decode append requires CUDA tensors.")
+        key = step.key if step.key.data_ptr() % 16 == 0 else step.key.clone()
+        value = step.value if step.value.data_ptr() % 16 == 0 else step.value.clone()
+        cells = []
+        for table, recorded in _table_groups(pool, step.plan):
+            width = int(table.shape[1])
+            for (layer, logical), v in recorded.items():
+                cells.append(N.TkvTableCell(table.data_ptr(), layer * width + logical, int(v), 0))
+        if len(cells) > N.TKV_APPEND_MAX_CELLS:
+            raise RuntimeError("append step records more table cells than one launch carries.")
+        arr = (N.TkvTableCell * max(1, len(cells)))(*cells)
+        pools = _pools(pool)
+        ps = pools.as_struct()
+        N.check(N.load().tkv_append_hot_tokens(ctypes.byref(ps), step.slot, step.start,
+                                                int(key.shape[-2]), key.data_ptr(), value.data_ptr(),
+                                                arr, len(cells), ops._stream(stream)),
+                "tkv_append_hot_tokens")
+        launches += 1
+    return launches
+
+
+def append_to_layer(self, seq_id: int, key_states: torch.Tensor, value_states: torch.Tensor) -> bool:
+    """Method-compatible replacement of TieredKVRuntime.append_to_layer
+    (tierkv_policy.py:1768-1816): ``TieredKVRuntime.append_to_layer =
+    paged_tierkv_b200.tiering.append_to_layer``."""
+    steps, allocated_new_block = plan_append(self, seq_id, key_states, value_states)
+    apply_append(self.kv_pool, steps)
+    return allocated_new_block

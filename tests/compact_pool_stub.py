@@ -57,6 +57,19 @@ class CompactPoolStub:
     def _check_physical_idx(self, physical_idx):
         return int(physical_idx)
 
+    def _coerce_kv(self, key_states, value_states):
+        if key_states.shape != value_states.shape:
+            raise ValueError("Key and value tensors must have identical shape.")
+        if key_states.ndim != 4 or key_states.shape[0] != 1:
+            raise ValueError("KV tensors must have shape [1, kv_heads, tokens, head_dim].")
+        if key_states.shape[-2] > self.block_size:
+            raise ValueError("A single stored block cannot exceed block_size tokens.")
+        return (key_states.to(torch.float16).contiguous(), value_states.to(torch.float16).contiguous())
+
+    def _ensure_metadata(self, key_states):
+        if int(key_states.shape[1]) != self.kv_heads or int(key_states.shape[-1]) != self.head_dim:
+            raise ValueError("KV tensor geometry changed after tensor-pool allocation.")
+
     def get_physical_state(self, physical_idx):
         return self.physical_states.get(int(physical_idx))
 
@@ -134,3 +147,25 @@ class CompactPoolStub:
             "allocated_hot_slots": self.allocated_hot_slots,
             "allocated_warm_slots": self.allocated_warm_slots,
         }
+
+
+class LayerState:
+    """LayerRuntimeState (tierkv_policy.py:1481-1484)."""
+
+    def __init__(self, open_physical_idx=None, open_token_count=0, num_blocks=0):
+        self.open_physical_idx = open_physical_idx
+        self.open_token_count = open_token_count
+        self.num_blocks = num_blocks
+
+    def as_list(self):
+        return [self.open_physical_idx, self.open_token_count, self.num_blocks]
+
+
+class BlockManagerStub:
+    """allocate_block of csrc/block_manager.cpp:36-50 (LIFO free list)."""
+
+    def __init__(self, free):
+        self.free = list(free)
+
+    def allocate_block(self, seq_id):
+        return self.free.pop()

@@ -19,6 +19,15 @@ chunks) and every stored byte, stale rows of reused slots included.
 Scenarios (seeded): LIFO reuse in both directions within one sync (a
 demotion frees a HOT slot a later promotion takes, and the reverse), pool
 growth during the sync, partial blocks, HOT->COLD and WARM->COLD, no-ops.
+
+``append_decode.npz`` records the decode-time append the same way: a
+two-layer pool filled through the reference's ``TieredKVRuntime.append_to_layer``
+(tierkv_policy.py:1768-1816, called unbound on a stand-in runtime whose
+block manager allocates physical blocks like csrc/block_manager.cpp:36-50,
+LIFO from a free list initialised N-1..0), its state, then a recorded
+sequence of multi-token and one-token appends on both layers (block
+boundaries, pool growth, an open block demoted to WARM and appended to again,
+which promotes it) with their inputs, return values and the state after.
 """
 
 from __future__ import annotations
@@ -148,6 +157,78 @@ SCENARIOS = {
 }
 
 
+class _BlockManager:
+    """csrc/block_manager.cpp:36-50: LIFO over [N-1, ..., 0]."""
+
+    def __init__(self, n):
+        self.free = list(range(n - 1, -1, -1))
+
+    def allocate_block(self, seq_id):
+        return self.free.pop()
+
+
+def _layer_states(rt):
+    return {str(k): [v.open_physical_idx, int(v.open_token_count), int(v.num_blocks)]
+            for k, v in rt.layer_states.items()}
+
+
+def build_append(tp, torch, *, seed=404, kv_heads=2, head_dim=64, block_size=16, layers=2):
+    gen = torch.Generator().manual_seed(seed)
+    max_blocks = 10
+    pool = tp.CompactTieredKVTensorPool(num_layers=layers, block_size=block_size,
+                                        max_seq_len=block_size * max_blocks,
+                                        pool_blocks=layers * max_blocks, pool_chunk_blocks=3)
+    bm = _BlockManager(layers * max_blocks)
+    rt = types.SimpleNamespace(layer_states={i: tp.LayerRuntimeState() for i in range(layers)},
+                               block_manager=bm, kv_pool=pool, block_size=block_size,
+                               max_blocks_per_layer=max_blocks)
+
+    def kv(tokens):
+        k = torch.randn((1, kv_heads, tokens, head_dim), generator=gen).to(torch.float16)
+        v = torch.randn((1, kv_heads, tokens, head_dim), generator=gen).to(torch.float16)
+        return k, v
+
+    # set-up: a 21-token and a 3-token prompt, then a few decode tokens
+    for layer, n in ((0, 21), (1, 3), (0, 1), (1, 1)):
+        tp.TieredKVRuntime.append_to_layer(rt, layer, *kv(n))
+    # layer 0's first (full) block goes WARM, so both pools exist
+    first = next(p for p, loc in pool.physical_locations.items() if tuple(loc) == (0, 0))
+    pool.demote_to_warm(first)
+    pool.set_block_state(0, 0, WARM)
+    before_book, before = _state(pool)
+    before_layers = _layer_states(rt)
+    before_bm = list(bm.free)
+    calls, inputs = [], {}
+    plan = [(0, 1)] * 3 + [(1, 1)] * 4 + [(1, 14), (0, 1), (1, 1)] + [(0, 1), (1, 1)] * 12
+    for i, (layer, n) in enumerate(plan):
+        if i == 5:
+            # the open block of layer 0 goes WARM; the next append promotes it
+            open_p = rt.layer_states[0].open_physical_idx
+            pool.demote_to_warm(open_p)
+            loc = pool.physical_locations[open_p]
+            pool.set_block_state(loc[0], loc[1], WARM)
+            calls.append({"demote_open": 0})
+        k, v = kv(n)
+        inputs[f"in_{i}_k"], inputs[f"in_{i}_v"] = k.numpy(), v.numpy()
+        new_block = tp.TieredKVRuntime.append_to_layer(rt, layer, k, v)
+        calls.append({"layer": layer, "tokens": n, "index": i, "new_block": bool(new_block)})
+    after_book, after = _state(pool)
+    meta = {
+        "seed": seed, "kv_heads": kv_heads, "head_dim": head_dim, "block_size": block_size,
+        "num_layers": layers, "max_blocks_per_layer": max_blocks,
+        "max_hot_slots": int(pool.max_hot_slots), "max_warm_slots": int(pool.max_warm_slots),
+        "hot_chunk_slots": int(pool.hot_chunk_slots), "warm_chunk_slots": int(pool.warm_chunk_slots),
+        "before": before_book, "after": after_book, "before_layers": before_layers,
+        "after_layers": _layer_states(rt), "before_bm_free": before_bm, "after_bm_free": list(bm.free),
+        "calls": calls,
+    }
+    out = {"meta": np.array(json.dumps(meta))}
+    out.update({f"before_{k}": v for k, v in before.items()})
+    out.update({f"after_{k}": v for k, v in after.items()})
+    out.update(inputs)
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of a Paged_TierKV checkout (read-only)")
@@ -161,6 +242,10 @@ def main(argv=None) -> int:
         np.savez_compressed(path, **out)
         meta = json.loads(str(out["meta"]))
         print(name, os.path.getsize(path), "bytes; desired", meta["desired"])
+    out = build_append(tp, torch)
+    path = os.path.join(HERE, "append_decode.npz")
+    np.savez_compressed(path, **out)
+    print("append_decode", os.path.getsize(path), "bytes")
     return 0
 
 

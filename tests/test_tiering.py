@@ -112,3 +112,113 @@ def test_runtime_method_drop_in():
     torch.cuda.synchronize()
     np.testing.assert_array_equal(pool.warm_k_pool.cpu().numpy(), fx["after_warm_k"])
     np.testing.assert_array_equal(pool.block_states.cpu().numpy(), fx["after_block_states"])
+
+
+# ---------------------------------------------------------------------------
+# decode-time append
+# ---------------------------------------------------------------------------
+
+def _append_runtime(fx, device):
+    import types
+    from compact_pool_stub import BlockManagerStub, LayerState
+    pool = CompactPoolStub(fx, device)
+    meta = pool.meta
+    layers = {int(k): LayerState(*v) for k, v in meta["before_layers"].items()}
+    rt = types.SimpleNamespace(layer_states=layers, block_manager=BlockManagerStub(meta["before_bm_free"]),
+                               kv_pool=pool, block_size=meta["block_size"],
+                               max_blocks_per_layer=meta["max_blocks_per_layer"])
+    return rt, pool, meta
+
+
+def _demote_open(rt, pool, layer):
+    """The fixture's event: the layer's open block goes WARM (demote_to_warm +
+    set_block_state), done with the batched tick's machinery."""
+    p = rt.layer_states[layer].open_physical_idx
+    plan = tiering.SyncPlan(layer)
+    tiering._demote_to_warm(pool, plan, p)
+    loc = pool.physical_locations[p]
+    plan.states[(int(loc[0]), int(loc[1]))] = tiering.WARM_STATE
+    return plan
+
+
+def test_append_bookkeeping_matches_reference():
+    fx = _load(os.path.join(GOLDEN, "append_decode.npz"))
+    rt, pool, meta = _append_runtime(fx, "cpu")
+    tables = {n: fx[f"before_{n}"].copy() for n in TABLES + ("physical_block_tables",)}
+
+    def put(plan):
+        for name, cells in zip(TABLES + ("physical_block_tables",),
+                               (plan.states, plan.slots, plan.lengths, plan.physical)):
+            for (layer, logical), v in cells.items():
+                tables[name][layer, logical] = v
+
+    for call in meta["calls"]:
+        if "demote_open" in call:
+            put(_demote_open(rt, pool, call["demote_open"]))
+            continue
+        i = call["index"]
+        k = torch.from_numpy(fx[f"in_{i}_k"])
+        v = torch.from_numpy(fx[f"in_{i}_v"])
+        steps, new_block = tiering.plan_append(rt, call["layer"], k, v)
+        assert new_block == call["new_block"], i
+        for st in steps:
+            put(st.plan)
+    assert pool.bookkeeping() == meta["after"]
+    assert {str(k): v.as_list() for k, v in rt.layer_states.items()} == meta["after_layers"]
+    assert rt.block_manager.free == meta["after_bm_free"]
+    for name, t in tables.items():
+        np.testing.assert_array_equal(t, fx[f"after_{name}"], err_msg=name)
+
+
+@pytest.mark.gpu
+def test_fused_append_matches_reference_bytes():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    fx = _load(os.path.join(GOLDEN, "append_decode.npz"))
+    rt, pool, meta = _append_runtime(fx, "cuda")
+    launches = 0
+    for call in meta["calls"]:
+        if "demote_open" in call:
+            tiering.apply_sync(pool, _demote_open(rt, pool, call["demote_open"]))
+            continue
+        i = call["index"]
+        k = torch.from_numpy(fx[f"in_{i}_k"]).cuda()
+        v = torch.from_numpy(fx[f"in_{i}_v"]).cuda()
+        steps, new_block = tiering.plan_append(rt, call["layer"], k, v)
+        launches += tiering.apply_append(pool, steps)
+        assert new_block == call["new_block"], i
+    torch.cuda.synchronize()
+    assert launches == sum(1 for c in meta["calls"] if "index" in c) + 2  # + a second block, a promotion
+    assert pool.bookkeeping() == meta["after"]
+    got = {"hot_k": pool.hot_k_pool, "hot_v": pool.hot_v_pool, "warm_k": pool.warm_k_pool,
+           "warm_v": pool.warm_v_pool, "k_scale": pool.k_scale, "k_zero": pool.k_zero,
+           "v_scale": pool.v_scale, "v_zero": pool.v_zero, "block_states": pool.block_states,
+           "block_slot_indices": pool.block_slot_indices, "block_lengths": pool.block_lengths,
+           "physical_block_tables": pool.physical_block_tables}
+    for name, t in got.items():
+        want = fx[f"after_{name}"]
+        have = t.cpu().numpy()
+        assert have.shape == want.shape, name
+        np.testing.assert_array_equal(have.view(np.uint8), want.view(np.uint8), err_msg=name)
+
+
+@pytest.mark.gpu
+def test_fused_append_rejects_bad_arguments():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import ctypes
+    from paged_tierkv_b200 import _native as N
+    from paged_tierkv_b200 import ops
+    pools = ops.TieredPools.allocate(4, 4, 2, 16, 64, "cuda")
+    k = torch.zeros((2, 1, 64), dtype=torch.float16, device="cuda")
+    ps = pools.as_struct()
+    lib = N.load()
+    stream = ops._stream(None)
+    cells = (N.TkvTableCell * 1)()
+    for slot, start, tokens in ((4, 0, 1), (-1, 0, 1), (0, 16, 1), (0, 15, 2), (0, 0, 0)):
+        st = lib.tkv_append_hot_tokens(ctypes.byref(ps), slot, start, tokens, k.data_ptr(),
+                                       k.data_ptr(), cells, 0, stream)
+        assert st == N.TKV_ERR_INVALID, (slot, start, tokens)
+    st = lib.tkv_append_hot_tokens(ctypes.byref(ps), 0, 0, 1, k.data_ptr(), k.data_ptr(), cells,
+                                   N.TKV_APPEND_MAX_CELLS + 1, stream)
+    assert st == N.TKV_ERR_INVALID
