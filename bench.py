@@ -50,10 +50,12 @@ def parse():
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--sweep", action="store_true",
                     help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
-    ap.add_argument("--config", choices=["c5", "c4", "demote"], default="c5",
+    ap.add_argument("--config", choices=["c5", "c4", "demote", "tick", "append"], default="c5",
                     help="c5: data-parallel batches (default); c4: one 131k-token context "
                          "over 32 layers, sharded by block range across the GPUs; demote: "
-                         "HOT->WARM demotion of 2^20 fp16 [16 x 128] tiles per GPU")
+                         "HOT->WARM demotion of 2^20 fp16 [16 x 128] tiles per GPU; tick: one "
+                         "policy tick (storage sync) of a 2048-block layer; append: the "
+                         "decode-time KV append of one token")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--demote-blocks", type=int, default=65536,
                     help="demote: demoted blocks per launch (x 8 kv heads x K/V tiles)")
@@ -518,6 +520,24 @@ def run_demote(a, rank, world, dist_on, device):
     ms, ms_p = float(t[0]), float(t[1])
     if rank != 0:
         return
+    cpu = None
+    if world == 1 and not a.no_cpu_baseline:
+        # the oracle's restatement of quantize_fp16_to_int8 on a 2048-tile slice
+        from oracle import tierkv_oracle as orc
+        sample_blocks = min(blocks, 128)
+        x = pools.hot_k[:sample_blocks].cpu().numpy()
+        tiles_s = sample_blocks * hkv * 2
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            orc.quantize_rows_r(x)
+            orc.quantize_rows_r(x)  # K and V
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= a.cpu_seconds / 2 and reps >= 2:
+                break
+        cpu = {"value": round(tiles_s * reps * (bytes_per / tiles) / el / 1e9, 4), "unit": "GB/s",
+               "cores": 1, "kind": "port",
+               "sample": f"{tiles_s} tiles (128 blocks x 8 kv heads x K/V), numpy, repeated"}
     peak, kind = hbm_peak()
     gbs = bytes_per / (ms * 1e-3) / 1e9
     gbs_p = bytes_per / (ms_p * 1e-3) / 1e9
@@ -533,8 +553,173 @@ def run_demote(a, rank, world, dist_on, device):
         "promote": {"value": round(gbs_p * world, 1), "unit": "GB/s", "ms_per_step": round(ms_p, 4),
                     "frac": round(gbs_p / peak, 4)},
         "clocks": clocks,
+        "cpu_baseline": cpu,
         "gpu_launches": 2 * steps,
     }), flush=True)
+
+
+def _tiering_layer(device, blocks=2048, n_hot=512, n_warm=1024, seed=17):
+    """One layer of configuration 5's sequence shape in a CompactPool: 2048
+    blocks appended through the fused append, then tiered by one tick into
+    512 HOT (sink + recent) / 1024 WARM / 512 COLD."""
+    import types
+    from paged_tierkv_b200 import compact_pool, tiering
+    bs, hkv, d = 16, 8, 128
+    pool = compact_pool.CompactPool(num_layers=1, block_size=bs, kv_heads=hkv, head_dim=d,
+                                    max_blocks_per_layer=blocks + 64, max_hot_slots=blocks + 64,
+                                    max_warm_slots=blocks + 64, device=device)
+    rt = types.SimpleNamespace(layer_states={0: compact_pool.LayerState()},
+                               block_manager=compact_pool.BlockAllocator(blocks + 64),
+                               kv_pool=pool, block_size=bs, max_blocks_per_layer=blocks + 64)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    k = torch.randn((1, hkv, blocks * bs, d), generator=gen, device=device).to(torch.float16)
+    v = torch.randn((1, hkv, blocks * bs, d), generator=gen, device=device).to(torch.float16)
+    tiering.append_to_layer(rt, 0, k, v)
+    rng = np.random.default_rng(seed)
+    states = np.full(blocks, tiering.COLD_STATE, np.int32)
+    states[0] = tiering.HOT_STATE
+    states[blocks - (n_hot - 1):] = tiering.HOT_STATE
+    mid = rng.permutation(np.arange(1, blocks - (n_hot - 1)))
+    states[mid[:n_warm]] = tiering.WARM_STATE
+    physical = list(range(blocks))
+    tiering.apply_sync(pool, tiering.plan_sync(pool, 0, physical, states.tolist()))
+    torch.cuda.synchronize()
+    return rt, pool, physical, states
+
+
+def run_tiering(a, rank, world, dist_on, device):
+    """The survey's "next" rows measured on one layer of configuration 5's
+    shape (2048 blocks x 8 kv heads x [16 x 128]):
+      tick   -- sync_storage_states after the policy swaps 64 HOT and 64 WARM
+                blocks (128 data moves), batched (one demotion + one promotion
+                launch + staging + one table write) against the same moves done
+                the reference's way, one launch per move and one element write
+                per table cell;
+      append -- one decode token appended to the open block, fused (one launch)
+                against the reference's per-op sequence (two row copies, two
+                tail fills, three table-element writes)."""
+    from paged_tierkv_b200 import _native, ops, tiering
+    _native.load(build_if_missing=True)
+    rt, pool, physical, states = _tiering_layer(device)
+    steps = max(3, min(a.steps, 200))
+    warm = max(1, a.warmup)
+    if a.config == "tick":
+        rng = np.random.default_rng(5)
+        warm_ids = rng.choice(np.nonzero(states == tiering.WARM_STATE)[0], 64, replace=False)
+        recent = np.arange(len(states) - 511, len(states))
+        hot_pick = rng.choice(recent[:-1], 64, replace=False)
+        a_states = states.copy()
+        b_states = states.copy()
+        b_states[warm_ids] = tiering.HOT_STATE
+        b_states[hot_pick] = tiering.WARM_STATE
+        flip = [b_states, a_states]
+
+        def batched(target):
+            plan = tiering.plan_sync(pool, 0, physical, target.tolist())
+            return tiering.apply_sync(pool, plan)
+
+        def per_block(target):
+            plan = tiering.plan_sync(pool, 0, physical, target.tolist())
+            pools = tiering._pools(pool)
+            for h, w, n in plan.demotions:
+                ops.demote_blocks_to_warm(pools, [h], [w], [n])
+            for w, h, n in plan.promotions:
+                ops.promote_blocks_to_hot(pools, [w], [h], [n])
+            for table, cells in tiering._table_groups(pool, plan):
+                for (layer, logical), val in cells.items():
+                    table[layer, logical] = val
+            return plan
+
+        def timed(fn):
+            for i in range(warm * 2):
+                fn(flip[i % 2])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record()
+            for i in range(steps * 2):
+                fn(flip[i % 2])
+            e1.record()
+            torch.cuda.synchronize()
+            return (time.perf_counter() - t0) * 1e3 / (steps * 2), e0.elapsed_time(e1) / (steps * 2)
+
+        stats = batched(flip[0])
+        batched(flip[1])
+        wall, dev = timed(batched)
+        wall_pb, dev_pb = timed(per_block)
+        moves = stats["demotions"] + stats["promotions"]
+        tile_bytes = 8 * 16 * 128 * 2 * 2 + 8 * 16 * 128 * 2 + 8 * 16 * 8
+        line = {
+            "metric": "policy tick ms (storage sync of one 2048-block layer, 64 HOT<->64 WARM swaps)",
+            "value": round(wall, 3), "unit": "ms", "n_gpus": 1, "steps": steps * 2, "warmup": warm * 2,
+            "ms_per_step": round(wall, 3), "higher_is_better": False, "scaling": "none",
+            "dtype": "fp16<->u8", "data": "synthetic N(0,1)",
+            "config": {"workload": "tick_2048_blocks_128_moves", "moves": moves,
+                       "staged_moves": stats["staged_demotions"] + stats["staged_promotions"],
+                       "bytes_moved": moves * tile_bytes},
+            "device_ms": round(dev, 3),
+            "per_block": {"ms": round(wall_pb, 3), "device_ms": round(dev_pb, 3),
+                          "what": "same plan, one kernel launch per move, one element write "
+                                  "per table cell (the reference's launch pattern)"},
+            "gpu_launches": steps * 2 * (2 + int(stats["staged_demotions"] > 0)
+                                         + int(stats["staged_promotions"] > 0)),
+        }
+        print(json.dumps(line), flush=True)
+        return
+    # append: one token per step into the open block of the layer
+    hkv, d = pool.kv_heads, pool.head_dim
+    gen = torch.Generator(device=device).manual_seed(3)
+    toks = torch.randn((steps * 2 + warm * 4, 1, hkv, 1, d), generator=gen, device=device).to(torch.float16)
+    cur = [0]
+
+    def fused():
+        t = toks[cur[0]]
+        cur[0] += 1
+        tiering.append_to_layer(rt, 0, t, t)
+
+    def per_op():
+        t = toks[cur[0]]
+        cur[0] += 1
+        steps_, _ = tiering.plan_append(rt, 0, t, t)
+        for st in steps_:
+            n = int(st.key.shape[-2])
+            pool.hot_k_pool[st.slot, :, st.start:st.start + n, :].copy_(st.key[0])
+            pool.hot_v_pool[st.slot, :, st.start:st.start + n, :].copy_(st.value[0])
+            if st.start + n < pool.block_size:
+                pool.hot_k_pool[st.slot, :, st.start + n:, :].zero_()
+                pool.hot_v_pool[st.slot, :, st.start + n:, :].zero_()
+            for table, cells in tiering._table_groups(pool, st.plan):
+                for (layer, logical), val in cells.items():
+                    table[layer, logical] = val
+
+    def timed(fn, n):
+        for _ in range(warm * 2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) * 1e6 / n, e0.elapsed_time(e1) * 1e3 / n
+
+    us, dev_us = timed(fused, steps)
+    us_po, dev_po = timed(per_op, steps)
+    line = {
+        "metric": "decode KV append us per token (one layer, 8 kv heads x 128, block 16)",
+        "value": round(us, 2), "unit": "us", "n_gpus": 1, "steps": steps, "warmup": warm * 2,
+        "ms_per_step": round(us / 1e3, 5), "higher_is_better": False, "scaling": "none",
+        "dtype": "fp16", "data": "synthetic N(0,1)",
+        "config": {"workload": "append_1_token", "blocks": len(physical)},
+        "device_us": round(dev_us, 2),
+        "per_op": {"us": round(us_po, 2), "device_us": round(dev_po, 2),
+                   "what": "same bookkeeping, then the reference's per-op sequence: two row copies, "
+                           "two tail fills, one element write per table cell"},
+        "gpu_launches": steps,
+    }
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -559,6 +744,8 @@ def main():
             run_c4(a, rank, world, dist_on, device)
         elif a.config == "demote":
             run_demote(a, rank, world, dist_on, device)
+        elif a.config in ("tick", "append"):
+            run_tiering(a, rank, world, dist_on, device)
         else:
             run_ours(a, rank, world, dist_on, device)
     finally:

@@ -434,8 +434,10 @@ def apply_append(pool, steps, stream=None) -> int:
         if len(cells) > N.TKV_APPEND_MAX_CELLS:
             raise RuntimeError("append step records more table cells than one launch carries.")
         arr = (N.TkvTableCell * max(1, len(cells)))(*cells)
-        pools = _pools(pool)
-        ps = pools.as_struct()
+        hk, hv = pool.hot_k_pool, pool.hot_v_pool  # the append touches the HOT pool only
+        ps = N.TkvPools(hk.data_ptr(), hv.data_ptr(), None, None, None, None, None, None,
+                        int(hk.shape[0]), 0, int(hk.shape[1]), int(hk.shape[2]), int(hk.shape[3]),
+                        ops.FORMAT_R)
         N.check(N.load().tkv_append_hot_tokens(ctypes.byref(ps), step.slot, step.start,
                                                 int(key.shape[-2]), key.data_ptr(), value.data_ptr(),
                                                 arr, len(cells), ops._stream(stream)),

@@ -105,6 +105,7 @@ def build(tp, torch, *, seed, n_blocks, kv_heads, head_dim, block_size, chunk, p
     meta = {
         "seed": seed, "kv_heads": kv_heads, "head_dim": head_dim, "block_size": block_size,
         "num_layers": 1, "max_blocks_per_layer": int(pool.max_blocks_per_layer),
+        "pool_blocks": int(pool.pool_blocks),
         "max_hot_slots": int(pool.max_hot_slots), "max_warm_slots": int(pool.max_warm_slots),
         "hot_chunk_slots": int(pool.hot_chunk_slots), "warm_chunk_slots": int(pool.warm_chunk_slots),
         "layer": 0, "physical_indices": [int(x) for x in physical], "desired": [int(x) for x in desired],
@@ -215,7 +216,7 @@ def build_append(tp, torch, *, seed=404, kv_heads=2, head_dim=64, block_size=16,
     after_book, after = _state(pool)
     meta = {
         "seed": seed, "kv_heads": kv_heads, "head_dim": head_dim, "block_size": block_size,
-        "num_layers": layers, "max_blocks_per_layer": max_blocks,
+        "num_layers": layers, "max_blocks_per_layer": max_blocks, "pool_blocks": int(pool.pool_blocks),
         "max_hot_slots": int(pool.max_hot_slots), "max_warm_slots": int(pool.max_warm_slots),
         "hot_chunk_slots": int(pool.hot_chunk_slots), "warm_chunk_slots": int(pool.warm_chunk_slots),
         "before": before_book, "after": after_book, "before_layers": before_layers,
