@@ -25,6 +25,8 @@ class CompactPool:
                  hot_chunk_slots: int = 128, warm_chunk_slots: int = 128,
                  pool_blocks: int | None = None, device="cuda"):
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.num_layers = int(num_layers)
         self.block_size = int(block_size)
         self.kv_heads = int(kv_heads)

@@ -36,6 +36,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from . import ops
@@ -56,6 +57,7 @@ class SyncPlan:
     slots: dict = field(default_factory=dict)       # (layer, logical) -> slot
     lengths: dict = field(default_factory=dict)     # (layer, logical) -> length
     physical: dict = field(default_factory=dict)    # (layer, logical) -> physical block
+    state_row: object = None  # block_states[layer, :len] written whole, before the cells
 
     def staged(self):
         """(demotions, promotions) whose destination another move of the tick
@@ -152,7 +154,57 @@ def plan_sync(pool, layer_idx: int, physical_indices, states) -> SyncPlan:
     the reference does, and may grow its tensors through the pool's own slot
     allocators."""
     plan = SyncPlan(int(layer_idx))
-    for logical_idx, (physical_idx, state) in enumerate(zip(physical_indices, states)):
+    physical = [int(x) for x in physical_indices]
+    target = np.asarray([int(x) for x in states], dtype=np.int64)
+    if len(physical) != len(target):
+        # zip() semantics of the reference loop
+        n = min(len(physical), len(target))
+        physical, target = physical[:n], target[:n]
+    if not pool.is_allocated():
+        return _plan_sync_loop(pool, plan, layer_idx, physical, target)
+    # Blocks that keep their tier only rewrite their state cell with the same
+    # value, so only the transitions are walked (in logical order, which is
+    # all the slot allocators see); the state row is written whole.  A
+    # transitioning block whose recorded location is not (layer, its logical
+    # index) would make the order of cell writes observable: then the exact
+    # per-block loop runs instead.
+    get = pool.physical_states.get
+    current = np.fromiter((-1 if (c := get(pidx)) is None else c for pidx in physical),
+                          dtype=np.int64, count=len(physical))
+    act = (((target == HOT_STATE) & ((current == WARM_STATE) | (current == COLD_STATE)))
+           | ((target == COLD_STATE) & (current != COLD_STATE))
+           | ((target == WARM_STATE) & ((current == HOT_STATE) | (current == COLD_STATE))))
+    moving = np.nonzero(act)[0]
+    for i in moving:
+        loc = pool.physical_locations.get(physical[i])
+        if loc is not None and (int(loc[0]), int(loc[1])) != (int(layer_idx), int(i)):
+            return _plan_sync_loop(pool, plan, layer_idx, physical, target)
+    for i in moving:
+        _transition(pool, plan, physical[i], int(target[i]))
+    plan.state_row = target.astype(np.int32)
+    return plan
+
+
+def _transition(pool, plan: SyncPlan, physical_idx: int, state: int) -> None:
+    """One iteration of the reference loop without set_block_state."""
+    current_state = pool.get_physical_state(physical_idx)
+    if state == HOT_STATE:
+        if current_state == WARM_STATE:
+            _promote_to_hot(pool, plan, physical_idx)
+        elif current_state == COLD_STATE:
+            raise KeyError(f"Physical block {physical_idx} cannot be promoted from COLD to HOT.")
+    elif state == COLD_STATE and current_state != COLD_STATE:
+        _demote_to_cold(pool, plan, physical_idx)
+    elif state == WARM_STATE:
+        if current_state == HOT_STATE:
+            _demote_to_warm(pool, plan, physical_idx)
+        elif current_state == COLD_STATE:
+            raise KeyError(f"Physical block {physical_idx} cannot be promoted from COLD to WARM.")
+
+
+def _plan_sync_loop(pool, plan: SyncPlan, layer_idx: int, physical, target) -> SyncPlan:
+    """The reference loop block by block, every cell write recorded in order."""
+    for logical_idx, (physical_idx, state) in enumerate(zip(physical, target)):
         physical_idx = int(physical_idx)
         state = int(state)
         current_state = pool.get_physical_state(physical_idx)
@@ -184,14 +236,25 @@ def _pools(pool) -> ops.TieredPools:
                            pool.k_scale, pool.k_zero, pool.v_scale, pool.v_zero)
 
 
-def _rows(slots, lengths, kv_heads: int, block_size: int) -> torch.Tensor:
+def _rows(slots, lengths, kv_heads: int, block_size: int) -> np.ndarray:
     """Flat row indices (slot, head, t < length) of [slots, heads, bs, *] tensors."""
-    out = []
-    for slot, length in zip(slots, lengths):
-        for h in range(kv_heads):
-            base = (slot * kv_heads + h) * block_size
-            out.extend(range(base, base + length))
-    return torch.tensor(out, dtype=torch.int64)
+    slots = np.asarray(slots, dtype=np.int64)
+    lengths = np.asarray(lengths, dtype=np.int64)
+    h = np.arange(kv_heads, dtype=np.int64)
+    t = np.arange(block_size, dtype=np.int64)
+    rows = (slots[:, None, None] * kv_heads + h[None, :, None]) * block_size + t[None, None, :]
+    return rows[np.broadcast_to(t[None, None, :] < lengths[:, None, None], rows.shape)]
+
+
+def _to_device(parts, dev):
+    """Several int64 host arrays in one pinned host->device copy."""
+    host = torch.from_numpy(np.concatenate([np.asarray(x, dtype=np.int64) for x in parts]))
+    buf = host.pin_memory().to(dev, non_blocking=True)
+    out, off = [], 0
+    for x in parts:
+        out.append(buf[off:off + len(x)])
+        off += len(x)
+    return out
 
 
 def apply_sync(pool, plan: SyncPlan, stream=None) -> dict:
@@ -209,44 +272,52 @@ def apply_sync(pool, plan: SyncPlan, stream=None) -> dict:
         sd, sp = set(staged_dem), set(staged_pro)
         direct_dem = [m for i, m in enumerate(plan.demotions) if i not in sd]
         direct_pro = [m for i, m in enumerate(plan.promotions) if i not in sp]
+        sdm = [plan.demotions[i] for i in staged_dem]
+        spm = [plan.promotions[i] for i in staged_pro]
+        # every slot list and staging row index of the tick in one copy
+        parts = []
+        for moves in (direct_dem, direct_pro):
+            for j in range(3):
+                parts.append([m[j] for m in moves])
+        for moves in (sdm, spm):
+            parts.append([m[0] for m in moves])
+            parts.append(list(range(len(moves))))
+            parts.append([m[2] for m in moves])
+            parts.append(_rows([m[1] for m in moves], [m[2] for m in moves], kvh, bs))
+            parts.append(_rows(range(len(moves)), [m[2] for m in moves], kvh, bs))
+        with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+            dev_parts = _to_device(parts, dev)
+        dd, dp = dev_parts[0:3], dev_parts[3:6]
+        sdd, spp = dev_parts[6:11], dev_parts[11:16]
+        i32 = lambda x: x.to(torch.int32)  # noqa: E731
         # phase 1: every move reads its source; direct moves write their slot
         # (no move of this tick reads it), staged moves write staging
         stage_w = stage_h = None
         if direct_dem:
-            h, w, n = zip(*direct_dem)
-            ops.demote_blocks_to_warm(pools, list(h), list(w), list(n), stream=stream)
-        if staged_dem:
-            moves = [plan.demotions[i] for i in staged_dem]
-            stage_w = ops.TieredPools.allocate(1, len(moves), kvh, bs, d, dev)
+            ops.demote_blocks_to_warm(pools, i32(dd[0]), i32(dd[1]), i32(dd[2]), stream=stream)
+        if sdm:
+            stage_w = ops.TieredPools.allocate(1, len(sdm), kvh, bs, d, dev)
             view = ops.TieredPools(pool.hot_k_pool, pool.hot_v_pool, stage_w.warm_k, stage_w.warm_v,
                                    stage_w.k_scale, stage_w.k_zero, stage_w.v_scale, stage_w.v_zero)
-            ops.demote_blocks_to_warm(view, [m[0] for m in moves], list(range(len(moves))),
-                                      [m[2] for m in moves], stream=stream)
+            ops.demote_blocks_to_warm(view, i32(sdd[0]), i32(sdd[1]), i32(sdd[2]), stream=stream)
         if direct_pro:
-            w, h, n = zip(*direct_pro)
-            ops.promote_blocks_to_hot(pools, list(w), list(h), list(n), stream=stream)
-        if staged_pro:
-            moves = [plan.promotions[i] for i in staged_pro]
-            stage_h = ops.TieredPools.allocate(len(moves), 1, kvh, bs, d, dev)
+            ops.promote_blocks_to_hot(pools, i32(dp[0]), i32(dp[1]), i32(dp[2]), stream=stream)
+        if spm:
+            stage_h = ops.TieredPools.allocate(len(spm), 1, kvh, bs, d, dev)
             view = ops.TieredPools(stage_h.hot_k, stage_h.hot_v, pool.warm_k_pool, pool.warm_v_pool,
                                    pool.k_scale, pool.k_zero, pool.v_scale, pool.v_zero)
-            ops.promote_blocks_to_hot(view, [m[0] for m in moves], list(range(len(moves))),
-                                      [m[2] for m in moves], stream=stream)
+            ops.promote_blocks_to_hot(view, i32(spp[0]), i32(spp[1]), i32(spp[2]), stream=stream)
         # phase 2: staged results into their slots, rows below the length only
         with torch.cuda.stream(stream) if stream is not None else _nullcontext():
-            if staged_dem:
-                moves = [plan.demotions[i] for i in staged_dem]
-                dst = _rows([m[1] for m in moves], [m[2] for m in moves], kvh, bs).to(dev)
-                src = _rows(range(len(moves)), [m[2] for m in moves], kvh, bs).to(dev)
+            if sdm:
+                dst, src = sdd[3], sdd[4]
                 for real, st, width in ((pool.warm_k_pool, stage_w.warm_k, d),
                                         (pool.warm_v_pool, stage_w.warm_v, d),
                                         (pool.k_scale, stage_w.k_scale, 1), (pool.k_zero, stage_w.k_zero, 1),
                                         (pool.v_scale, stage_w.v_scale, 1), (pool.v_zero, stage_w.v_zero, 1)):
                     real.view(-1, width).index_copy_(0, dst, st.view(-1, width).index_select(0, src))
-            if staged_pro:
-                moves = [plan.promotions[i] for i in staged_pro]
-                dst = _rows([m[1] for m in moves], [m[2] for m in moves], kvh, bs).to(dev)
-                src = _rows(range(len(moves)), [m[2] for m in moves], kvh, bs).to(dev)
+            if spm:
+                dst, src = spp[3], spp[4]
                 for real, st in ((pool.hot_k_pool, stage_h.hot_k), (pool.hot_v_pool, stage_h.hot_v)):
                     real.view(-1, d).index_copy_(0, dst, st.view(-1, d).index_select(0, src))
     _write_tables(pool, plan, stream)
@@ -271,20 +342,25 @@ def _write_tables(pool, plan: SyncPlan, stream=None) -> None:
     """The recorded cells of block_states / block_slot_indices / block_lengths,
     last write winning as in the reference, in one host->device copy."""
     groups = [(t, cells) for t, cells in _table_groups(pool, plan) if cells]
-    if not groups:
+    row = plan.state_row
+    if not groups and row is None:
         return
     width = int(pool.block_states.shape[1])
-    flat = []
+    parts = [np.asarray(row, dtype=np.int64)] if row is not None else []
     for _, cells in groups:
-        flat.extend(l * width + i for (l, i) in cells)
-        flat.extend(cells.values())
+        parts.append(np.fromiter((l * width + i for (l, i) in cells), dtype=np.int64, count=len(cells)))
+        parts.append(np.fromiter(cells.values(), dtype=np.int64, count=len(cells)))
     dev = pool.block_states.device
-    host = torch.tensor(flat, dtype=torch.int64)
+    host = torch.from_numpy(np.concatenate(parts))
     if dev.type == "cuda":
         host = host.pin_memory()
     with torch.cuda.stream(stream) if stream is not None else _nullcontext():
         buf = host.to(dev, non_blocking=True)
         off = 0
+        if row is not None:
+            n = len(row)
+            pool.block_states[plan.layer, :n].copy_(buf[:n])
+            off = n
         for table, cells in groups:
             n = len(cells)
             idx, val = buf[off:off + n], buf[off + n:off + 2 * n]

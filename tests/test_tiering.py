@@ -34,12 +34,37 @@ def test_bookkeeping_matches_reference(path):
     meta = pool.meta
     plan = tiering.plan_sync(pool, meta["layer"], meta["physical_indices"], meta["desired"])
     assert pool.bookkeeping() == meta["after"]
-    # the recorded cells turn the "before" tables into the "after" tables
+    # the recorded row and cells turn the "before" tables into the "after" tables
+    for name, t in _apply_cells(fx, plan).items():
+        np.testing.assert_array_equal(t, fx[f"after_{name}"], err_msg=name)
+
+
+def _apply_cells(fx, plan):
+    tables = {n: fx[f"before_{n}"].copy() for n in TABLES}
+    if plan.state_row is not None:
+        tables["block_states"][plan.layer, :len(plan.state_row)] = plan.state_row
     for name, cells in zip(TABLES, (plan.states, plan.slots, plan.lengths)):
-        table = fx[f"before_{name}"].copy()
         for (layer, logical), v in cells.items():
-            table[layer, logical] = v
-        np.testing.assert_array_equal(table, fx[f"after_{name}"], err_msg=name)
+            tables[name][layer, logical] = v
+    return tables
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=lambda p: os.path.basename(p)[:-4])
+def test_transition_walk_equals_block_by_block_loop(path):
+    """Walking only the transitions (the fast path) leaves the same
+    bookkeeping and tables as the block-by-block loop."""
+    fx = _load(path)
+    fast = CompactPoolStub(fx, "cpu")
+    slow = CompactPoolStub(fx, "cpu")
+    meta = fast.meta
+    plan_f = tiering.plan_sync(fast, meta["layer"], meta["physical_indices"], meta["desired"])
+    assert plan_f.state_row is not None  # the fixtures take the fast path
+    plan_s = tiering._plan_sync_loop(slow, tiering.SyncPlan(meta["layer"]), meta["layer"],
+                                     meta["physical_indices"], meta["desired"])
+    assert fast.bookkeeping() == slow.bookkeeping()
+    assert plan_f.demotions == plan_s.demotions and plan_f.promotions == plan_s.promotions
+    for name in TABLES:
+        np.testing.assert_array_equal(_apply_cells(fx, plan_f)[name], _apply_cells(fx, plan_s)[name])
 
 
 def test_fixtures_cover_slot_reuse_and_growth():
