@@ -25,6 +25,11 @@
  *                          329-361 (dense pool) demote_to_warm(), batched
  *   tkv_promote_to_hot     tierkv_policy.py:1087-1115 (compact) and 375-402
  *                          (dense) promote_to_hot(), batched
+ *   tkv_decode_attention_exchange
+ *                          the survey's context-sharded decode (one context
+ *                          split by block range over GPUs): decode, exchange
+ *                          of the (o, LSE) partials over NVLink peer memory
+ *                          and their merge in one launch per rank
  *   tkv_append_hot_tokens  tierkv_policy.py:934-967 write_hot_tokens() tensor
  *                          work plus the block-table writes of _set_metadata
  *                          (917-926) and set_block_entry (1016-1035), fused
@@ -225,6 +230,48 @@ typedef struct tkv_table_cell {
 int32_t tkv_append_hot_tokens(const tkv_pools* pools, int32_t hot_slot, int32_t start,
                               int32_t tokens, const void* key, const void* value,
                               const tkv_table_cell* cells, int32_t n_cells, void* stream);
+
+/* ---- context-sharded decode with a peer-memory exchange -------------------
+ * Each rank holds a contiguous block range of the same sequences; every rank
+ * launches tkv_decode_attention_exchange with its own tables and pools and
+ * the same epoch.  The last CTA of each (sequence, kv head) writes its
+ * normalised partial (o, LSE) into every rank's inbox with plain stores
+ * through CUDA IPC mappings (no multicast), publishes it with a release store
+ * of the epoch into the receiving rank's flag for (sender, unit), waits
+ * (acquire, bounded by timeout_ns; TKV_DEVERR_TIMEOUT when it runs out) for
+ * the flags of all ranks in its own inbox, and merges the world partials into
+ * args->out / out_lse (and the global LSE the score pass normalises with).
+ * Partials are double-buffered by epoch parity, so a rank may run one call
+ * ahead of the others.  Replaces the per-layer all-gather + merge. */
+#define TKV_EXCHANGE_MAX_RANKS 8
+
+typedef struct tkv_exchange {
+    int32_t  world;        /* ranks sharing the contexts, 1..8 */
+    int32_t  rank;
+    uint32_t epoch;        /* +1 per call, equal on every rank, never 0 */
+    int32_t  rows_cap;     /* the inboxes' capacity (their layout): rows ... */
+    int32_t  units_cap;    /* ... and (sequence, kv head) units, as allocated */
+    int32_t  reserved;
+    uint64_t timeout_ns;   /* bound of the wait for the peers; 0 = 2 s */
+    void*    inbox[TKV_EXCHANGE_MAX_RANKS];  /* rank q's inbox, mapped here */
+} tkv_exchange;
+
+/* Bytes of one rank's inbox for up to `rows` = batch * num_heads rows and
+ * `units` = batch * kv_heads (sequence, kv head) pairs at head_dim; every
+ * rank's inbox has the same capacities, passed in tkv_exchange. */
+size_t  tkv_exchange_bytes(int32_t world, int32_t rows, int32_t units, int32_t head_dim);
+
+/* Allocates a zeroed inbox of `bytes` on the current device and returns its
+ * CUDA IPC handle (TKV_IPC_HANDLE_BYTES bytes) for the other ranks. */
+#define TKV_IPC_HANDLE_BYTES 64
+int32_t tkv_exchange_alloc(size_t bytes, void** ptr_out, void* ipc_handle_out);
+/* Maps another rank's inbox into this process (peer access over NVLink). */
+int32_t tkv_exchange_open(const void* ipc_handle, void** ptr_out);
+int32_t tkv_exchange_close(void* mapped_ptr);
+int32_t tkv_exchange_free(void* ptr);
+
+int32_t tkv_decode_attention_exchange(const tkv_pools* pools, const tkv_decode_args* args,
+                                      const tkv_exchange* xc, void* stream);
 
 /* Reads and clears the device error bits (TKV_DEVERR_*) that decode calls
  * using this workspace have recorded.  Synchronizes the stream. */

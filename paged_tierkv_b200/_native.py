@@ -43,7 +43,16 @@ EXPORTED_SYMBOLS = (
     "tkv_read_device_errors",
     "tkv_decode_attention_noalloc",
     "tkv_append_hot_tokens",
+    "tkv_exchange_bytes",
+    "tkv_exchange_alloc",
+    "tkv_exchange_open",
+    "tkv_exchange_close",
+    "tkv_exchange_free",
+    "tkv_decode_attention_exchange",
 )
+
+TKV_EXCHANGE_MAX_RANKS = 8
+TKV_IPC_HANDLE_BYTES = 64
 
 TKV_APPEND_MAX_CELLS = 8
 
@@ -102,6 +111,19 @@ class TkvTableCell(ctypes.Structure):
     ]
 
 
+class TkvExchange(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("epoch", ctypes.c_uint32),
+        ("rows_cap", ctypes.c_int32),
+        ("units_cap", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("timeout_ns", ctypes.c_uint64),
+        ("inbox", ctypes.c_void_p * 8),
+    ]
+
+
 _LIB = None
 
 
@@ -141,6 +163,13 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
                                           vp], i32),
         "tkv_append_hot_tokens": ([ctypes.POINTER(TkvPools), i32, i32, i32, vp, vp,
                                    ctypes.POINTER(TkvTableCell), i32, vp], i32),
+        "tkv_exchange_bytes": ([i32, i32, i32, i32], ctypes.c_size_t),
+        "tkv_exchange_alloc": ([ctypes.c_size_t, ctypes.POINTER(vp), vp], i32),
+        "tkv_exchange_open": ([vp, ctypes.POINTER(vp)], i32),
+        "tkv_exchange_close": ([vp], i32),
+        "tkv_exchange_free": ([vp], i32),
+        "tkv_decode_attention_exchange": ([ctypes.POINTER(TkvPools), ctypes.POINTER(TkvDecodeArgs),
+                                           ctypes.POINTER(TkvExchange), vp], i32),
     }
     for name, (argtypes, restype) in sigs.items():
         fn = getattr(lib, name)

@@ -316,7 +316,8 @@ int32_t tkv_decode_plan(const tkv_pools* pools, const tkv_decode_args* args,
   return TKV_OK;
 }
 
-int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, void* stream) {
+static int32_t decode_impl(const tkv_pools* pools, const tkv_decode_args* a,
+                           const tkv_exchange* xc, void* stream) {
   Plan plan;
   int32_t st = make_plan(pools, a, &plan);
   if (st != TKV_OK) return st;
@@ -391,6 +392,15 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   p.group_size = plan.group_size;
   p.out_dtype = a->out_dtype;
   p.scale_log2 = a->scaling * kLog2e;
+  if (xc) {
+    p.x_world = xc->world;
+    p.x_rank = xc->rank;
+    p.x_epoch = xc->epoch;
+    p.x_rows_cap = xc->rows_cap;
+    p.x_units_cap = xc->units_cap;
+    p.x_timeout_ns = xc->timeout_ns;
+    for (int q = 0; q < xc->world; ++q) p.x_inbox[q] = reinterpret_cast<uint8_t*>(xc->inbox[q]);
+  }
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   st = cuda_status(launch_decode(p, maps, d, bs, pools->format, a->query_dtype, s));
@@ -406,6 +416,74 @@ int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, v
   sp.rows = a->batch * a->num_heads;
   if (a->max_blocks == 0) return TKV_OK;
   return cuda_status(launch_scores(sp, s));
+}
+
+int32_t tkv_decode_attention(const tkv_pools* pools, const tkv_decode_args* a, void* stream) {
+  return decode_impl(pools, a, nullptr, stream);
+}
+
+size_t tkv_exchange_bytes(int32_t world, int32_t rows, int32_t units, int32_t head_dim) {
+  if (world < 1 || world > TKV_EXCHANGE_MAX_RANKS || rows < 1 || units < 1 || head_dim < 1) return 0;
+  return xchg_total_bytes(world, rows, units, head_dim);
+}
+
+int32_t tkv_exchange_alloc(size_t bytes, void** ptr_out, void* ipc_handle_out) {
+  if (!ptr_out || !ipc_handle_out || bytes == 0) return TKV_ERR_INVALID;
+  static_assert(sizeof(cudaIpcMemHandle_t) == TKV_IPC_HANDLE_BYTES, "IPC handle size");
+  void* ptr = nullptr;
+  if (cudaMalloc(&ptr, bytes) != cudaSuccess) return TKV_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(ptr, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) {
+    cudaFree(ptr);
+    return TKV_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle_out, &h, sizeof(h));
+  *ptr_out = ptr;
+  return TKV_OK;
+}
+
+int32_t tkv_exchange_open(const void* ipc_handle, void** ptr_out) {
+  if (!ipc_handle || !ptr_out) return TKV_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* ptr = nullptr;
+  if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return TKV_ERR_CUDA;
+  *ptr_out = ptr;
+  return TKV_OK;
+}
+
+int32_t tkv_exchange_close(void* mapped_ptr) {
+  if (!mapped_ptr) return TKV_ERR_INVALID;
+  return cudaIpcCloseMemHandle(mapped_ptr) == cudaSuccess ? TKV_OK : TKV_ERR_CUDA;
+}
+
+int32_t tkv_exchange_free(void* ptr) {
+  if (!ptr) return TKV_ERR_INVALID;
+  return cudaFree(ptr) == cudaSuccess ? TKV_OK : TKV_ERR_CUDA;
+}
+
+int32_t tkv_decode_attention_exchange(const tkv_pools* pools, const tkv_decode_args* a,
+                                      const tkv_exchange* xc, void* stream) {
+  if (!xc || !a || !pools) return TKV_ERR_INVALID;
+  if (xc->world < 1 || xc->world > TKV_EXCHANGE_MAX_RANKS || xc->rank < 0 || xc->rank >= xc->world ||
+      xc->epoch == 0)
+    return TKV_ERR_INVALID;
+  for (int q = 0; q < xc->world; ++q)
+    if (!xc->inbox[q] || !aligned(xc->inbox[q], 256)) return TKV_ERR_INVALID;
+  const int64_t rows = (int64_t)a->batch * a->num_heads;
+  const int64_t units = (int64_t)a->batch * pools->kv_heads;
+  if (rows > xc->rows_cap || units > xc->units_cap) return TKV_ERR_INVALID;
+  // every unit's last CTA waits for the peers while holding an SM slot; the
+  // other CTAs must always find free slots
+  int sms = 0;
+  int32_t st = current_device_sms(&sms);
+  if (st != TKV_OK) return st;
+  int ctas = 0;
+  if (!cached_occupancy(pools->head_dim, pools->block_size, pools->format, a->query_dtype, &ctas) ||
+      ctas <= 0)
+    return TKV_ERR_CUDA;
+  if (units * 2 > (int64_t)sms * ctas) return TKV_ERR_UNSUPPORTED;
+  return decode_impl(pools, a, xc, stream);
 }
 
 int32_t tkv_merge_partials(const float* part_o, int64_t o_part_stride, const float* part_lse,

@@ -203,6 +203,24 @@ __device__ __forceinline__ void load_qfrag(uint32_t sq, int lane, int m, uint32_
   ldsm_x4(addr, b00, b01, b10, b11);
 }
 
+// ---------------------------------------------------------------- exchange
+// Rank q's inbox as mapped in this process: flags [world][units_cap], then
+// o [2][rows_cap][world][D] and lse [2][rows_cap][world] (epoch parity).
+__device__ __forceinline__ uint32_t* x_flags(const DecodeParams& p, int q) {
+  return reinterpret_cast<uint32_t*>(p.x_inbox[q]);
+}
+template <int D>
+__device__ __forceinline__ float* x_o(const DecodeParams& p, int q) {
+  return reinterpret_cast<float*>(p.x_inbox[q] + xchg_flags_bytes(p.x_world, p.x_units_cap)) +
+         (size_t)(p.x_epoch & 1u) * p.x_rows_cap * p.x_world * D;
+}
+template <int D>
+__device__ __forceinline__ float* x_lse(const DecodeParams& p, int q) {
+  return reinterpret_cast<float*>(p.x_inbox[q] + xchg_flags_bytes(p.x_world, p.x_units_cap) +
+                                  xchg_o_bytes(p.x_world, p.x_rows_cap, D)) +
+         (size_t)(p.x_epoch & 1u) * p.x_rows_cap * p.x_world;
+}
+
 // Merges `cnt` normalised partials (o, LSE) of the G rows row0.. of a
 // (sequence, kv head): part j of row r at po + ((r * rstride) + j0 + j) * D
 // and plse[r * rstride + j0 + j].  The result goes to the final output
@@ -215,7 +233,7 @@ template <int D, int NT>
 __device__ __forceinline__ void merge_parts(const float* po, const float* plse, int rstride,
                                             int j0, int cnt, size_t row0, int G, float* wsl,
                                             const DecodeParams& p, float* dst_o, float* dst_lse,
-                                            int dstride, int dj) {
+                                            int dstride, int dj, bool xout = false) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* hm = wsl + kMaxGroups * cnt;  // [G] max, [G] sum
   for (int e = threadIdx.x; e < G * cnt; e += NT) {
@@ -283,6 +301,13 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
       if (sp0 == 0)
         reinterpret_cast<float4*>(dst_o + (row * dstride + dj) * D)[v] = o;
       if (lane == 0) dst_lse[row * dstride + dj] = lse;
+    } else if (xout) {
+      // this rank's partial of the row into every rank's inbox
+      for (int q = 0; q < p.x_world; ++q) {
+        if (sp0 == 0)
+          reinterpret_cast<float4*>(x_o<D>(p, q) + (row * p.x_world + p.x_rank) * D)[v] = o;
+        if (lane == 0) x_lse<D>(p, q)[row * p.x_world + p.x_rank] = lse;
+      }
     } else {
       if (sp0 == 0) {
         const size_t base = row * D + 4 * v;
@@ -297,6 +322,36 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
       }
     }
   }
+}
+
+// Publishes this unit's partials (already stored into every inbox) with a
+// release store of the epoch into each rank's flag (sender, unit), waits --
+// bounded -- for every rank's flag in this rank's inbox, and merges the world
+// partials into the output.
+template <int D, int NT>
+__device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, size_t row0, int G,
+                                         float* wsl) {
+  __threadfence_system();
+  __syncthreads();
+  const int world = p.x_world;
+  if ((int)threadIdx.x < world)
+    st_release_sys(x_flags(p, threadIdx.x) + (size_t)p.x_rank * p.x_units_cap + unit, p.x_epoch);
+  if ((int)threadIdx.x < world) {
+    const uint32_t* f = x_flags(p, p.x_rank) + (size_t)threadIdx.x * p.x_units_cap + unit;
+    const uint64_t limit = p.x_timeout_ns ? p.x_timeout_ns : 2000000000ull;
+    const uint64_t t0 = globaltimer();
+    // a peer may already be one call ahead: wait until the flag reaches the epoch
+    while ((int32_t)(ld_acquire_sys(f) - p.x_epoch) < 0) {
+      if (globaltimer() - t0 > limit) {
+        atomicOr(p.err, 0x2u);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+  merge_parts<D, NT>(x_o<D>(p, p.x_rank), x_lse<D>(p, p.x_rank), world, 0, world, row0, G, wsl, p,
+                     nullptr, nullptr, 0, 0);
 }
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0
@@ -884,7 +939,12 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     const float on = L > 0.f ? o / L : 0.f;
     const float lse = L > 0.f ? (M + lg2(L)) * kLn2 : -INFINITY;
     const size_t row = (size_t)seq * Hq + (size_t)kvh * G + h;
-    if (nsplit == 1) {
+    if (nsplit == 1 && p.x_world > 0) {
+      for (int q = 0; q < p.x_world; ++q) {
+        x_o<D>(p, q)[(row * p.x_world + p.x_rank) * D + d] = on;
+        if (d == 0) x_lse<D>(p, q)[row * p.x_world + p.x_rank] = lse;
+      }
+    } else if (nsplit == 1) {
       store_out(p.out, p.out_dtype, row * D + d, on);
       if (d == 0) {
         if (p.out_lse) p.out_lse[row] = lse;
@@ -895,7 +955,12 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       if (d == 0) p.part_lse[row * nsplit + split] = lse;
     }
   }
-  if (nsplit == 1) return;
+  if (nsplit == 1) {
+    if (p.x_world > 0)
+      x_finish<D, Cfg::kThreads>(p, unit, (size_t)seq * Hq + (size_t)kvh * G, G,
+                                 reinterpret_cast<float*>(stages));
+    return;
+  }
 
   // ------------------------------------------------------------ split merge
   // The last CTA of each group of group_size splits merges the group's
@@ -927,7 +992,8 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     }
     __threadfence();
     merge_parts<D, Cfg::kThreads>(p.part_o, p.part_lse, nsplit, 0, nsplit, row0, G, wsl, p,
-                                  nullptr, nullptr, 0, 0);
+                                  nullptr, nullptr, 0, 0, p.x_world > 0);
+    if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl);
     return;
   }
   if (threadIdx.x == 0) atomicExch(ticket, 0u);
@@ -948,7 +1014,8 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   }
   __threadfence();
   merge_parts<D, Cfg::kThreads>(p.gpart_o, p.gpart_lse, ngroups, 0, ngroups, row0, G, wsl, p,
-                                nullptr, nullptr, 0, 0);
+                                nullptr, nullptr, 0, 0, p.x_world > 0);
+  if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl);
 }
 
 // ---------------------------------------------------------------- dispatch

@@ -68,6 +68,16 @@ struct DecodeParams {
   int32_t splits;
   int32_t chunk;              // blocks per claimed work chunk: 8, 16 or 32
   int32_t group_size;         // splits merged per group (= splits: one level)
+  // context-sharded exchange (x_world > 0): inbox of rank q mapped at x_inbox[q];
+  // layout: flags [world][units] u32 (256-byte padded), then o [2][rows][world][D]
+  // and lse [2][rows][world] fp32 (double-buffered by epoch parity)
+  int32_t x_world;
+  int32_t x_rank;
+  uint32_t x_epoch;
+  int32_t x_rows_cap;
+  int32_t x_units_cap;
+  uint64_t x_timeout_ns;
+  uint8_t* x_inbox[8];
   int32_t out_dtype;
   float scale_log2;           // scaling * log2(e)
 };
@@ -154,6 +164,18 @@ struct AppendParams {
   int32_t* cell_ptr[8];       // table + index, resolved on the host
   int32_t cell_val[8];
 };
+
+// Inbox layout of the context-sharded exchange (see DecodeParams::x_inbox).
+__host__ __device__ inline size_t xchg_flags_bytes(int world, int units) {
+  return ((size_t)world * units * 4 + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t xchg_o_bytes(int world, int rows, int d) {
+  return (size_t)2 * rows * world * d * 4;
+}
+__host__ __device__ inline size_t xchg_total_bytes(int world, int rows, int units, int d) {
+  return xchg_flags_bytes(world, units) + xchg_o_bytes(world, rows, d) +
+         ((size_t)2 * rows * world * 4 + 255) / 256 * 256;
+}
 
 cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);

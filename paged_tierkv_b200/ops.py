@@ -186,13 +186,17 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
                      num_key_value_groups: int, scaling: float, *, return_scores: bool = False,
                      return_lse: bool = False, out: torch.Tensor | None = None,
                      out_dtype: torch.dtype | None = None, num_splits: int = 0,
-                     chunk_blocks: int = 0, stream=None):
+                     chunk_blocks: int = 0, exchange=None, stream=None):
     """Tiered paged decode attention over a batch of sequences.
 
     query [B, Hq, D] or [B, Hq, 1, D]; tables [B, T] (or [T] for B = 1) int32;
     num_blocks: int (all sequences) or an int32 CUDA tensor [B].
     num_splits / chunk_blocks (8, 16 or 32): CTAs per (sequence, kv head) and
     blocks per claimed work chunk; 0 lets the planner choose.
+    exchange: a ``_native.TkvExchange`` (see ``sharding.PeerExchange``): this
+    rank holds one block range of every sequence; the partials of all ranks
+    are exchanged over peer memory and merged inside the same launch, and the
+    returned output, LSE and scores are those of the whole contexts.
     Returns (out [B, Hq, D], score_sums [B, Hq, T] or None, lse [B, Hq] or None).
     """
     if query.ndim == 4:
@@ -253,8 +257,13 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
     ws = workspace_for(query.device, st.value or 0, nbytes.value)
     args.workspace = ws.data_ptr()
     args.workspace_bytes = ws.numel()
-    N.check(lib.tkv_decode_attention(ctypes.byref(pstruct), ctypes.byref(args), st),
-            "tkv_decode_attention")
+    if exchange is not None:
+        N.check(lib.tkv_decode_attention_exchange(ctypes.byref(pstruct), ctypes.byref(args),
+                                                  ctypes.byref(exchange), st),
+                "tkv_decode_attention_exchange")
+    else:
+        N.check(lib.tkv_decode_attention(ctypes.byref(pstruct), ctypes.byref(args), st),
+                "tkv_decode_attention")
     return out, scores, lse
 
 

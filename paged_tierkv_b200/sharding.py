@@ -19,6 +19,7 @@ COLD blocks stay exact under sharding: each rank adds the analytic
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable
 
@@ -116,3 +117,107 @@ class ContextShardedDecode:
             w = torch.where(torch.isfinite(lse_local), w, torch.zeros_like(w))
             scores = scores * w.unsqueeze(-1)
         return ShardResult(out=out.view(b, hq, d), lse=lse, score_sums=scores)
+
+
+# ---------------------------------------------------------------------------
+# exchange over peer memory (one launch per rank instead of all-gather + merge)
+# ---------------------------------------------------------------------------
+
+class PeerExchange:
+    """This rank's inbox and the other ranks' inboxes mapped into this process
+    (CUDA IPC over NVLink; no multicast), for ``tkv_decode_attention_exchange``.
+
+    Capacities (``rows_cap`` = batch * num_heads, ``units_cap`` = batch *
+    kv_heads, ``head_dim``) fix the inbox layout and must be equal on every
+    rank.  ``next()`` returns the exchange descriptor of the next call; every
+    rank must make the same sequence of calls.  ``close()`` unmaps the peers'
+    inboxes after a barrier and frees this rank's.
+    """
+
+    def __init__(self, group=None, *, rows_cap: int, units_cap: int, head_dim: int,
+                 timeout_ns: int = 0, inboxes=None, rank: int | None = None):
+        from . import _native as N
+        self._N = N
+        lib = N.load()
+        self.group = group
+        self.rows_cap, self.units_cap, self.head_dim = int(rows_cap), int(units_cap), int(head_dim)
+        self.timeout_ns = int(timeout_ns)
+        self.epoch = 0
+        self._own = None
+        self._mapped = []
+        if inboxes is not None:
+            # caller-provided inbox addresses (e.g. several inboxes in one process)
+            self.world = len(inboxes)
+            self.rank = int(rank or 0)
+            self.inbox = [int(x) for x in inboxes]
+            return
+        import torch.distributed as dist
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > N.TKV_EXCHANGE_MAX_RANKS:
+            raise ValueError(f"at most {N.TKV_EXCHANGE_MAX_RANKS} ranks share a context")
+        nbytes = lib.tkv_exchange_bytes(self.world, self.rows_cap, self.units_cap, self.head_dim)
+        if nbytes == 0:
+            raise ValueError("invalid exchange capacities")
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * N.TKV_IPC_HANDLE_BYTES)()
+        N.check(lib.tkv_exchange_alloc(nbytes, ctypes.byref(ptr), handle), "tkv_exchange_alloc")
+        self._own = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.inbox = []
+        for q, h in enumerate(handles):
+            if q == self.rank:
+                self.inbox.append(self._own)
+                continue
+            buf = (ctypes.c_uint8 * N.TKV_IPC_HANDLE_BYTES).from_buffer_copy(h)
+            m = ctypes.c_void_p()
+            N.check(lib.tkv_exchange_open(buf, ctypes.byref(m)), "tkv_exchange_open")
+            self._mapped.append(m.value)
+            self.inbox.append(m.value)
+        dist.barrier(group=group)
+
+    def next(self):
+        """The descriptor of the next call (epochs run 1, 2, ...; never 0)."""
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        x = self._N.TkvExchange()
+        x.world, x.rank, x.epoch = self.world, self.rank, self.epoch
+        x.rows_cap, x.units_cap, x.timeout_ns = self.rows_cap, self.units_cap, self.timeout_ns
+        for q, ptr in enumerate(self.inbox):
+            x.inbox[q] = ptr
+        return x
+
+    def close(self) -> None:
+        lib = self._N.load()
+        if self._own is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            for m in self._mapped:
+                lib.tkv_exchange_close(m)
+            self._mapped = []
+            dist.barrier(group=self.group)
+            lib.tkv_exchange_free(self._own)
+            self._own = None
+
+
+class P2PContextDecode:
+    """Context-sharded decode whose exchange and merge run inside the decode
+    launch (``tkv_decode_attention_exchange``): one kernel per rank per call,
+    no collective.  Returns the same ShardResult as ContextShardedDecode, with
+    scores normalised over the whole contexts."""
+
+    def __init__(self, exchange: PeerExchange):
+        self.exchange = exchange
+
+    def __call__(self, query: torch.Tensor, block_table: torch.Tensor, block_states: torch.Tensor,
+                 block_lengths: torch.Tensor, pools, num_blocks, num_key_value_groups: int,
+                 scaling: float, *, out_dtype=torch.float16, return_scores: bool = False,
+                 out: torch.Tensor | None = None) -> ShardResult:
+        from . import ops
+        o, scores, lse = ops.decode_attention(query, block_table, block_states, block_lengths, pools,
+                                              num_blocks, num_key_value_groups, scaling,
+                                              return_scores=return_scores, return_lse=True,
+                                              out=out, out_dtype=out_dtype,
+                                              exchange=self.exchange.next())
+        return ShardResult(o, lse, scores)

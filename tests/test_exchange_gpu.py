@@ -1,0 +1,147 @@
+"""Context-sharded decode with the peer-memory exchange, on one GPU.
+
+No launch here waits for another launch: with one rank the kernel exchanges
+with itself; the two-rank case has the other rank's partials and flags
+written into the inbox by the host beforehand (what the peer's kernel would
+have stored), so the launch finds them published; the timeout case waits on a
+flag nothing sets and must come back with TKV_DEVERR_TIMEOUT.  The real
+two-process exchange over CUDA IPC is in test_sharding_gpu.py.
+"""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from tierkv_cases import make_case, oracle_decode, to_device  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from paged_tierkv_b200 import _native
+    _native.load(build_if_missing=True)
+
+
+def _inbox(world, rows, units, d):
+    from paged_tierkv_b200 import _native as N
+    n = N.load().tkv_exchange_bytes(world, rows, units, d)
+    return torch.zeros(n, dtype=torch.uint8, device="cuda")
+
+
+def _layout(world, rows, units, d):
+    flags = (world * units * 4 + 255) // 256 * 256
+    return flags, flags + 2 * rows * world * d * 4
+
+
+def _run(d, case, **kw):
+    from paged_tierkv_b200 import ops
+    return ops.decode_attention(d["query"], d["block_table"], d["block_states"], d["block_lengths"],
+                                d["pools"], d["num_blocks"], case["groups"], case["scaling"], **kw)
+
+
+@pytest.mark.parametrize("splits", [1, 5])
+def test_one_rank_exchange_equals_plain_decode(splits):
+    from paged_tierkv_b200 import sharding
+    case = make_case(seed=60 + splits, batch=2, q_heads=32, kv_heads=8, head_dim=128, num_blocks=45)
+    d = to_device(case)
+    ref, ref_s, ref_l = _run(d, case, num_splits=splits, return_scores=True, return_lse=True)
+    rows, units = 2 * 32, 2 * 8
+    box = _inbox(1, rows, units, 128)
+    ex = sharding.PeerExchange(rows_cap=rows, units_cap=units, head_dim=128,
+                               inboxes=[box.data_ptr()], rank=0)
+    for _ in range(3):  # epochs 1, 2, 3: both parities
+        out, s, lse = _run(d, case, num_splits=splits, return_scores=True, return_lse=True,
+                           exchange=ex.next())
+        torch.cuda.synchronize()
+        if splits == 1:  # one partial: the exchange merge is exact
+            assert torch.equal(out, ref)
+            assert torch.equal(lse, ref_l)
+            assert torch.equal(s, ref_s)
+        else:  # dynamic chunk claiming varies the partials from run to run
+            torch.testing.assert_close(out.float(), ref.float(), atol=2e-4, rtol=2e-3)
+            torch.testing.assert_close(lse, ref_l, atol=1e-5, rtol=1e-5)
+            torch.testing.assert_close(s, ref_s, atol=1e-6, rtol=1e-4)
+
+
+@pytest.mark.parametrize("splits", [1, 4])
+def test_two_ranks_with_the_peer_already_published(splits):
+    from paged_tierkv_b200 import ops, sharding
+    nb = 70
+    case = make_case(seed=80 + splits, batch=2, q_heads=32, kv_heads=8, head_dim=128, num_blocks=nb,
+                     max_blocks=nb)
+    ref, _, ref_scores = oracle_decode(case)
+    cut = 33
+    shards = []
+    for sl in (slice(0, cut), slice(cut, nb)):
+        shards.append(dict(case, block_table=np.ascontiguousarray(case["block_table"][:, sl]),
+                           block_states=np.ascontiguousarray(case["block_states"][:, sl]),
+                           block_lengths=np.ascontiguousarray(case["block_lengths"][:, sl])))
+    d0, d1 = to_device(shards[0]), to_device(shards[1])
+    d0["num_blocks"], d1["num_blocks"] = cut, nb - cut
+    rows, units, world, D = 2 * 32, 2 * 8, 2, 128
+    box0, box1 = _inbox(world, rows, units, D), _inbox(world, rows, units, D)
+    ex = sharding.PeerExchange(rows_cap=rows, units_cap=units, head_dim=D,
+                               inboxes=[box0.data_ptr(), box1.data_ptr()], rank=0)
+    flags_b, lse_off = _layout(world, rows, units, D)
+    for call in range(3):
+        x = ex.next()
+        par = x.epoch & 1
+        # what rank 1's launch would have stored into rank 0's inbox
+        o1 = torch.empty((2, 32, D), dtype=torch.float32, device="cuda")
+        _, _, l1 = ops.decode_attention(d1["query"], d1["block_table"], d1["block_states"],
+                                        d1["block_lengths"], d1["pools"], nb - cut, case["groups"],
+                                        case["scaling"], out=o1, out_dtype=torch.float32,
+                                        return_lse=True, num_splits=splits)
+        o_view = box0[flags_b:lse_off].view(torch.float32).view(2, rows, world, D)
+        l_view = box0[lse_off:lse_off + 2 * rows * world * 4].view(torch.float32).view(2, rows, world)
+        o_view[par, :, 1, :] = o1.view(rows, D)
+        l_view[par, :, 1] = l1.view(rows)
+        torch.cuda.synchronize()
+        box0[:flags_b].view(torch.int32)[units:2 * units] = x.epoch  # flags [sender 1][unit]
+        out, scores, lse = _run(d0, shards[0], num_splits=splits, return_scores=True,
+                                return_lse=True, exchange=x)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+        # rank 0's scores are normalised over the whole contexts
+        np.testing.assert_allclose(scores.cpu().numpy(), ref_scores[:, :, :cut], atol=1e-4, rtol=1e-3)
+        # rank 0 published to "rank 1": its partial and its flags
+        f1 = box1[:flags_b].view(torch.int32)[:units].cpu().numpy()
+        assert (f1 == x.epoch).all()
+        assert ops.read_device_errors() == 0
+
+
+def test_peer_that_never_publishes_times_out():
+    from paged_tierkv_b200 import _native as N
+    from paged_tierkv_b200 import ops, sharding
+    case = make_case(seed=90, batch=1, q_heads=8, kv_heads=2, head_dim=64, num_blocks=6)
+    d = to_device(case)
+    rows, units = 8, 2
+    box0, box1 = _inbox(2, rows, units, 64), _inbox(2, rows, units, 64)
+    ex = sharding.PeerExchange(rows_cap=rows, units_cap=units, head_dim=64,
+                               inboxes=[box0.data_ptr(), box1.data_ptr()], rank=0,
+                               timeout_ns=20_000_000)
+    ops.read_device_errors()  # clear
+    _run(d, case, exchange=ex.next())
+    torch.cuda.synchronize()
+    assert ops.read_device_errors() & N.TKV_DEVERR_TIMEOUT
+
+
+def test_exchange_argument_checks():
+    from paged_tierkv_b200 import sharding
+    case = make_case(seed=91, batch=2, q_heads=8, kv_heads=2, head_dim=64, num_blocks=6)
+    d = to_device(case)
+    box = _inbox(1, 16, 4, 64)
+    small = sharding.PeerExchange(rows_cap=8, units_cap=2, head_dim=64, inboxes=[box.data_ptr()], rank=0)
+    with pytest.raises(ValueError):  # batch 2 x 8 heads > rows_cap 8
+        _run(d, case, exchange=small.next())
+    x = sharding.PeerExchange(rows_cap=16, units_cap=4, head_dim=64, inboxes=[box.data_ptr()],
+                              rank=0).next()
+    x.epoch = 0
+    with pytest.raises(ValueError):
+        _run(d, case, exchange=x)
