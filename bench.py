@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--demote-blocks", type=int, default=65536,
                     help="demote: demoted blocks per launch (x 8 kv heads x K/V tiles)")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="c4 on several GPUs: partials exchanged over peer memory inside the "
+                         "decode launch (p2p) or NCCL all-gather + merge launch (nccl)")
     ap.add_argument("--no-graph", action="store_true",
                     help="c4: launch every layer from Python instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -405,13 +408,21 @@ def run_c4(a, rank, world, dist_on, device):
                                    seed=7000 + 97 * layer + rank, device=device)
         layers.append(wl)
         total_bytes += wl.algorithmic_bytes()
-    dec = sharding.ContextShardedDecode()
+    ex = None
+    if world > 1 and a.exchange == "p2p":
+        ex = sharding.PeerExchange(rows_cap=hq, units_cap=hkv, head_dim=d, device_epoch=True)
+        dec = sharding.P2PContextDecode(ex)
+    else:
+        dec = sharding.ContextShardedDecode()
     out = torch.empty((1, hq, d), dtype=torch.float16, device=device)
 
     def step():
         for wl in layers:
             if world == 1:
                 workloads.decode(wl, out=out)
+            elif ex is not None:
+                dec(wl.query, wl.block_table, wl.block_states, wl.block_lengths, wl.pools,
+                    wl.num_blocks, wl.groups, wl.scaling, out=out)
             else:
                 dec(wl.query, wl.block_table, wl.block_states, wl.block_lengths, wl.pools,
                     wl.num_blocks, wl.groups, wl.scaling)
@@ -448,6 +459,8 @@ def run_c4(a, rank, world, dist_on, device):
     if dist_on:
         torch.distributed.barrier()
     del graph
+    if ex is not None:
+        ex.close()
     t = torch.tensor([e0.elapsed_time(e1), float(total_bytes)], dtype=torch.float64, device=device)
     if dist_on:
         tb = t.clone()
@@ -464,10 +477,12 @@ def run_c4(a, rank, world, dist_on, device):
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": f"c4_ctx{ctx}_bs{bs}_l{a.layers}", "hot_blocks": n_hot,
                    "warm_blocks": n_warm, "partition": "byte-balanced contiguous block ranges",
-                   "exchange": "NCCL all_gather of packed (o, lse) per layer" if world > 1 else "none",
+                   "exchange": ("none" if world == 1 else
+                                "peer-memory stores + epoch flags inside the decode launch"
+                                if ex is not None else "NCCL all_gather of packed (o, lse) per layer"),
                    "cuda_graph": not a.no_graph},
         "GBps_all_gpus": round(float(t[1]) / (ms * 1e-3) / 1e9, 1),
-        "gpu_launches": a.steps * a.layers * (1 if world == 1 else 2),
+        "gpu_launches": a.steps * a.layers * (1 if (world == 1 or ex is not None) else 2),
     }
     print(json.dumps(line), flush=True)
 

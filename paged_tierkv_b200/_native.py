@@ -120,6 +120,7 @@ class TkvExchange(ctypes.Structure):
         ("units_cap", ctypes.c_int32),
         ("reserved", ctypes.c_int32),
         ("timeout_ns", ctypes.c_uint64),
+        ("epoch_dev", ctypes.c_void_p),
         ("inbox", ctypes.c_void_p * 8),
     ]
 

@@ -399,6 +399,7 @@ static int32_t decode_impl(const tkv_pools* pools, const tkv_decode_args* a,
     p.x_rows_cap = xc->rows_cap;
     p.x_units_cap = xc->units_cap;
     p.x_timeout_ns = xc->timeout_ns;
+    p.x_epoch_dev = xc->epoch_dev;
     for (int q = 0; q < xc->world; ++q) p.x_inbox[q] = reinterpret_cast<uint8_t*>(xc->inbox[q]);
   }
 
@@ -466,8 +467,9 @@ int32_t tkv_decode_attention_exchange(const tkv_pools* pools, const tkv_decode_a
                                       const tkv_exchange* xc, void* stream) {
   if (!xc || !a || !pools) return TKV_ERR_INVALID;
   if (xc->world < 1 || xc->world > TKV_EXCHANGE_MAX_RANKS || xc->rank < 0 || xc->rank >= xc->world ||
-      xc->epoch == 0)
+      (xc->epoch == 0 && !xc->epoch_dev))
     return TKV_ERR_INVALID;
+  if (xc->epoch_dev && !aligned(xc->epoch_dev, 4)) return TKV_ERR_INVALID;
   for (int q = 0; q < xc->world; ++q)
     if (!xc->inbox[q] || !aligned(xc->inbox[q], 256)) return TKV_ERR_INVALID;
   const int64_t rows = (int64_t)a->batch * a->num_heads;

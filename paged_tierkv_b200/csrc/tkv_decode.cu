@@ -206,19 +206,22 @@ __device__ __forceinline__ void load_qfrag(uint32_t sq, int lane, int m, uint32_
 // ---------------------------------------------------------------- exchange
 // Rank q's inbox as mapped in this process: flags [world][units_cap], then
 // o [2][rows_cap][world][D] and lse [2][rows_cap][world] (epoch parity).
+// The epoch of the call is read once per CTA at kernel start (thread 0: the
+// value in the parameters, or a plain global load from x_epoch_dev, which
+// nothing writes while the launch runs) and handed to these helpers by value.
 __device__ __forceinline__ uint32_t* x_flags(const DecodeParams& p, int q) {
   return reinterpret_cast<uint32_t*>(p.x_inbox[q]);
 }
 template <int D>
-__device__ __forceinline__ float* x_o(const DecodeParams& p, int q) {
+__device__ __forceinline__ float* x_o(const DecodeParams& p, int q, uint32_t epoch) {
   return reinterpret_cast<float*>(p.x_inbox[q] + xchg_flags_bytes(p.x_world, p.x_units_cap)) +
-         (size_t)(p.x_epoch & 1u) * p.x_rows_cap * p.x_world * D;
+         (size_t)(epoch & 1u) * p.x_rows_cap * p.x_world * D;
 }
 template <int D>
-__device__ __forceinline__ float* x_lse(const DecodeParams& p, int q) {
+__device__ __forceinline__ float* x_lse(const DecodeParams& p, int q, uint32_t epoch) {
   return reinterpret_cast<float*>(p.x_inbox[q] + xchg_flags_bytes(p.x_world, p.x_units_cap) +
                                   xchg_o_bytes(p.x_world, p.x_rows_cap, D)) +
-         (size_t)(p.x_epoch & 1u) * p.x_rows_cap * p.x_world;
+         (size_t)(epoch & 1u) * p.x_rows_cap * p.x_world;
 }
 
 // Merges `cnt` normalised partials (o, LSE) of the G rows row0.. of a
@@ -233,7 +236,8 @@ template <int D, int NT>
 __device__ __forceinline__ void merge_parts(const float* po, const float* plse, int rstride,
                                             int j0, int cnt, size_t row0, int G, float* wsl,
                                             const DecodeParams& p, float* dst_o, float* dst_lse,
-                                            int dstride, int dj, bool xout = false) {
+                                            int dstride, int dj, bool xout = false,
+                                            uint32_t epoch = 0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* hm = wsl + kMaxGroups * cnt;  // [G] max, [G] sum
   for (int e = threadIdx.x; e < G * cnt; e += NT) {
@@ -305,8 +309,8 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
       // this rank's partial of the row into every rank's inbox
       for (int q = 0; q < p.x_world; ++q) {
         if (sp0 == 0)
-          reinterpret_cast<float4*>(x_o<D>(p, q) + (row * p.x_world + p.x_rank) * D)[v] = o;
-        if (lane == 0) x_lse<D>(p, q)[row * p.x_world + p.x_rank] = lse;
+          reinterpret_cast<float4*>(x_o<D>(p, q, epoch) + (row * p.x_world + p.x_rank) * D)[v] = o;
+        if (lane == 0) x_lse<D>(p, q, epoch)[row * p.x_world + p.x_rank] = lse;
       }
     } else {
       if (sp0 == 0) {
@@ -330,18 +334,18 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
 // partials into the output.
 template <int D, int NT>
 __device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, size_t row0, int G,
-                                         float* wsl) {
+                                         float* wsl, uint32_t epoch) {
   __threadfence_system();
   __syncthreads();
   const int world = p.x_world;
   if ((int)threadIdx.x < world)
-    st_release_sys(x_flags(p, threadIdx.x) + (size_t)p.x_rank * p.x_units_cap + unit, p.x_epoch);
+    st_release_sys(x_flags(p, threadIdx.x) + (size_t)p.x_rank * p.x_units_cap + unit, epoch);
   if ((int)threadIdx.x < world) {
     const uint32_t* f = x_flags(p, p.x_rank) + (size_t)threadIdx.x * p.x_units_cap + unit;
     const uint64_t limit = p.x_timeout_ns ? p.x_timeout_ns : 2000000000ull;
     const uint64_t t0 = globaltimer();
     // a peer may already be one call ahead: wait until the flag reaches the epoch
-    while ((int32_t)(ld_acquire_sys(f) - p.x_epoch) < 0) {
+    while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
       if (globaltimer() - t0 > limit) {
         atomicOr(p.err, 0x2u);
         break;
@@ -350,8 +354,8 @@ __device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, siz
     }
   }
   __syncthreads();
-  merge_parts<D, NT>(x_o<D>(p, p.x_rank), x_lse<D>(p, p.x_rank), world, 0, world, row0, G, wsl, p,
-                     nullptr, nullptr, 0, 0);
+  merge_parts<D, NT>(x_o<D>(p, p.x_rank, epoch), x_lse<D>(p, p.x_rank, epoch), world, 0, world,
+                     row0, G, wsl, p, nullptr, nullptr, 0, 0);
 }
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0
@@ -372,7 +376,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   uint64_t* empty_bar = full_bar + Cfg::kStages;
   TileInfo* info = reinterpret_cast<TileInfo*>(smem + Cfg::kOffInfo);
   uint8_t* meta = smem + Cfg::kOffMeta;
-  // misc: [0] cold tokens, [1] last-CTA flag, [8..16) query exponents,
+  // misc: [0] cold tokens, [1] last-CTA flag, [2] exchange epoch, [8..16) query exponents,
   // [16..24) per-head sums of the staged fp16 query (as float bits)
   int* misc = reinterpret_cast<int*>(smem + Cfg::kOffMisc);
   __half* sqh = reinterpret_cast<__half*>(smem + Cfg::kOffQ);
@@ -424,6 +428,11 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     }
     misc[0] = 0;
     misc[1] = 0;
+    // the exchange epoch of this call (see x_o): a value, never an address,
+    // is taken from the parameters
+    uint32_t epoch = p.x_epoch;
+    if (p.x_world > 0 && p.x_epoch_dev != nullptr) epoch = __ldcg(p.x_epoch_dev);
+    misc[2] = (int)epoch;
     fence_mbar_init();
   }
   __syncthreads();  // barriers initialised; the consumers stage the query below
@@ -940,9 +949,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     const float lse = L > 0.f ? (M + lg2(L)) * kLn2 : -INFINITY;
     const size_t row = (size_t)seq * Hq + (size_t)kvh * G + h;
     if (nsplit == 1 && p.x_world > 0) {
+      const uint32_t epoch = (uint32_t)misc[2];
       for (int q = 0; q < p.x_world; ++q) {
-        x_o<D>(p, q)[(row * p.x_world + p.x_rank) * D + d] = on;
-        if (d == 0) x_lse<D>(p, q)[row * p.x_world + p.x_rank] = lse;
+        x_o<D>(p, q, epoch)[(row * p.x_world + p.x_rank) * D + d] = on;
+        if (d == 0) x_lse<D>(p, q, epoch)[row * p.x_world + p.x_rank] = lse;
       }
     } else if (nsplit == 1) {
       store_out(p.out, p.out_dtype, row * D + d, on);
@@ -958,7 +968,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   if (nsplit == 1) {
     if (p.x_world > 0)
       x_finish<D, Cfg::kThreads>(p, unit, (size_t)seq * Hq + (size_t)kvh * G, G,
-                                 reinterpret_cast<float*>(stages));
+                                 reinterpret_cast<float*>(stages), (uint32_t)misc[2]);
     return;
   }
 
@@ -991,9 +1001,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       atomicExch(chunk_ctr, 0u);
     }
     __threadfence();
+    const uint32_t epoch = (uint32_t)misc[2];
     merge_parts<D, Cfg::kThreads>(p.part_o, p.part_lse, nsplit, 0, nsplit, row0, G, wsl, p,
-                                  nullptr, nullptr, 0, 0, p.x_world > 0);
-    if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl);
+                                  nullptr, nullptr, 0, 0, p.x_world > 0, epoch);
+    if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl, epoch);
     return;
   }
   if (threadIdx.x == 0) atomicExch(ticket, 0u);
@@ -1013,9 +1024,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     atomicExch(chunk_ctr, 0u);
   }
   __threadfence();
+  const uint32_t epoch = (uint32_t)misc[2];
   merge_parts<D, Cfg::kThreads>(p.gpart_o, p.gpart_lse, ngroups, 0, ngroups, row0, G, wsl, p,
-                                nullptr, nullptr, 0, 0, p.x_world > 0);
-  if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl);
+                                nullptr, nullptr, 0, 0, p.x_world > 0, epoch);
+  if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl, epoch);
 }
 
 // ---------------------------------------------------------------- dispatch

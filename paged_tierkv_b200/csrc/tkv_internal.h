@@ -77,6 +77,7 @@ struct DecodeParams {
   int32_t x_rows_cap;
   int32_t x_units_cap;
   uint64_t x_timeout_ns;
+  const uint32_t* x_epoch_dev;  // when set, the epoch is read from here
   uint8_t* x_inbox[8];
   int32_t out_dtype;
   float scale_log2;           // scaling * log2(e)

@@ -135,7 +135,8 @@ class PeerExchange:
     """
 
     def __init__(self, group=None, *, rows_cap: int, units_cap: int, head_dim: int,
-                 timeout_ns: int = 0, inboxes=None, rank: int | None = None):
+                 timeout_ns: int = 0, inboxes=None, rank: int | None = None,
+                 device_epoch: bool = False):
         from . import _native as N
         self._N = N
         lib = N.load()
@@ -145,6 +146,10 @@ class PeerExchange:
         self.epoch = 0
         self._own = None
         self._mapped = []
+        # device_epoch: the epoch lives in device memory and advance() adds one
+        # in stream order, so CUDA graph replays see a new epoch every call
+        self.epoch_t = (torch.ones(1, dtype=torch.int32, device=torch.cuda.current_device())
+                        if device_epoch else None)
         if inboxes is not None:
             # caller-provided inbox addresses (e.g. several inboxes in one process)
             self.world = len(inboxes)
@@ -179,13 +184,22 @@ class PeerExchange:
 
     def next(self):
         """The descriptor of the next call (epochs run 1, 2, ...; never 0)."""
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
         x = self._N.TkvExchange()
-        x.world, x.rank, x.epoch = self.world, self.rank, self.epoch
+        if self.epoch_t is not None:
+            x.epoch_dev = self.epoch_t.data_ptr()
+        else:
+            self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+            x.epoch = self.epoch
+        x.world, x.rank = self.world, self.rank
         x.rows_cap, x.units_cap, x.timeout_ns = self.rows_cap, self.units_cap, self.timeout_ns
         for q, ptr in enumerate(self.inbox):
             x.inbox[q] = ptr
         return x
+
+    def advance(self) -> None:
+        """After a call with a device epoch: the next call's epoch (stream order)."""
+        if self.epoch_t is not None:
+            self.epoch_t.add_(1)
 
     def close(self) -> None:
         lib = self._N.load()
@@ -220,4 +234,5 @@ class P2PContextDecode:
                                               return_scores=return_scores, return_lse=True,
                                               out=out, out_dtype=out_dtype,
                                               exchange=self.exchange.next())
+        self.exchange.advance()
         return ShardResult(o, lse, scores)

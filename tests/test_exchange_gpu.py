@@ -145,3 +145,40 @@ def test_exchange_argument_checks():
     x.epoch = 0
     with pytest.raises(ValueError):
         _run(d, case, exchange=x)
+
+
+def test_device_epoch_under_graph_replay():
+    """The epoch in device memory advances in stream order, so replays of a
+    captured call each use a new epoch (and alternate the inbox parity)."""
+    from paged_tierkv_b200 import sharding
+    case = make_case(seed=95, batch=1, q_heads=32, kv_heads=8, head_dim=128, num_blocks=40)
+    d = to_device(case)
+    ref, _, ref_l = _run(d, case, num_splits=1, return_lse=True)
+    rows, units = 32, 8
+    box = _inbox(1, rows, units, 128)
+    ex = sharding.PeerExchange(rows_cap=rows, units_cap=units, head_dim=128,
+                               inboxes=[box.data_ptr()], rank=0, device_epoch=True)
+    dec = sharding.P2PContextDecode(ex)
+    out = torch.empty_like(ref)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        dec(d["query"], d["block_table"], d["block_states"], d["block_lengths"], d["pools"],
+            d["num_blocks"], case["groups"], case["scaling"], out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        dec(d["query"], d["block_table"], d["block_states"], d["block_lengths"], d["pools"],
+            d["num_blocks"], case["groups"], case["scaling"], out=out)
+    torch.cuda.synchronize()
+    for i in range(4):
+        with torch.cuda.stream(side):
+            out.zero_()
+            g.replay()
+        torch.cuda.synchronize()
+        # the planner may split the blocks: equal up to the merge's rounding
+        torch.testing.assert_close(out.float(), ref.float(), atol=2e-4, rtol=2e-3)
+    # the warm-up call, the capture (not run) and four replays: epoch 1 + 1 + 4
+    assert int(ex.epoch_t.item()) == 6
+    flags = box[:256].view(torch.int32)[:units]
+    assert (flags.cpu().numpy() == 5).all()
