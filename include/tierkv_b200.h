@@ -253,10 +253,9 @@ typedef struct tkv_exchange {
     int32_t  units_cap;    /* ... and (sequence, kv head) units, as allocated */
     int32_t  reserved;
     uint64_t timeout_ns;   /* bound of the wait for the peers; 0 = 2 s */
-    const uint32_t* epoch_dev;  /* optional device word holding the epoch (read
-                                   instead of `epoch`, e.g. by CUDA graph
-                                   replays); the caller advances it by one
-                                   after each call, in stream order */
+    uint32_t* epoch_dev;   /* optional device word holding the epoch (read
+                              instead of `epoch`, e.g. by CUDA graph replays);
+                              the launch advances it by one when it is done */
     void*    inbox[TKV_EXCHANGE_MAX_RANKS];  /* rank q's inbox, mapped here */
 } tkv_exchange;
 

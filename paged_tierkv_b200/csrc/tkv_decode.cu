@@ -328,14 +328,76 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
   }
 }
 
+// The world partials of the G rows row0.. (this rank's inbox, epoch parity)
+// merged into the output: one warp per head, every lane loading the <= 8 LSEs
+// and its float4 of every partial in one round of loads.
+template <int D, int NT>
+__device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int G, uint32_t epoch) {
+  constexpr int kVecs = D / 4;                 // float4 per row
+  constexpr int kLanesPerRow = kVecs < 32 ? kVecs : 32;
+  constexpr int kSplitLanes = 32 / kLanesPerRow;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = p.x_world;
+  const float* xo = x_o<D>(p, p.x_rank, epoch);
+  const float* xl = x_lse<D>(p, p.x_rank, epoch);
+  const int v = lane % kLanesPerRow;
+  const int q0 = lane / kLanesPerRow;
+  for (int h = warp; h < G; h += NT / 32) {
+    const size_t row = row0 + h;
+    float lse[8];
+    float4 o[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      lse[q] = q < W ? __ldcg(xl + row * W + q) : -INFINITY;
+      o[q] = (q < W && (q % kSplitLanes) == q0)
+                 ? __ldcg(reinterpret_cast<const float4*>(xo + (row * W + q) * D) + v)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) M = fmaxf(M, lse[q]);
+    float S = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float w = ex2((lse[q] - M) * kLog2e);  // 0 for absent / empty partials
+        S += w;
+        acc.x += w * o[q].x; acc.y += w * o[q].y; acc.z += w * o[q].z; acc.w += w * o[q].w;
+      }
+    }
+#pragma unroll
+    for (int off = kLanesPerRow; off < 32; off <<= 1) {
+      acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+      acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+      acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+      acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+    }
+    const float inv = S > 0.f ? 1.f / S : 0.f;
+    const float total = (M != -INFINITY && S > 0.f) ? M + logf(S) : -INFINITY;
+    if (q0 == 0) {
+      const size_t base = row * D + 4 * v;
+      store_out(p.out, p.out_dtype, base + 0, acc.x * inv);
+      store_out(p.out, p.out_dtype, base + 1, acc.y * inv);
+      store_out(p.out, p.out_dtype, base + 2, acc.z * inv);
+      store_out(p.out, p.out_dtype, base + 3, acc.w * inv);
+    }
+    if (lane == 0) {
+      if (p.out_lse) p.out_lse[row] = total;
+      if (p.lse_final) p.lse_final[row] = total;
+    }
+  }
+}
+
 // Publishes this unit's partials (already stored into every inbox) with a
 // release store of the epoch into each rank's flag (sender, unit), waits --
 // bounded -- for every rank's flag in this rank's inbox, and merges the world
-// partials into the output.
+// partials into the output.  The CTA barrier orders every thread's partial
+// stores before the flag writer's system-scope release (happens-before is
+// transitive through bar.sync), which the reader's acquire pairs with.
 template <int D, int NT>
 __device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, size_t row0, int G,
                                          float* wsl, uint32_t epoch) {
-  __threadfence_system();
   __syncthreads();
   const int world = p.x_world;
   if ((int)threadIdx.x < world)
@@ -354,8 +416,18 @@ __device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, siz
     }
   }
   __syncthreads();
-  merge_parts<D, NT>(x_o<D>(p, p.x_rank, epoch), x_lse<D>(p, p.x_rank, epoch), world, 0, world,
-                     row0, G, wsl, p, nullptr, nullptr, 0, 0);
+  x_merge<D, NT>(p, row0, G, epoch);
+  // A device epoch advances when the last unit of the launch is done: every
+  // CTA of the launch has read the epoch by then (at its start).
+  if (p.x_epoch_dev != nullptr && threadIdx.x == 0) {
+    __threadfence();
+    uint32_t* ticket = p.err + 1;
+    const uint32_t units = (uint32_t)p.batch * (uint32_t)p.kv_heads;
+    if (atomicAdd(ticket, 1u) == units - 1u) {
+      atomicExch(ticket, 0u);
+      atomicAdd(p.x_epoch_dev, 1u);
+    }
+  }
 }
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0

@@ -55,7 +55,7 @@ struct DecodeParams {
                               // (both reset by the last CTA of each sequence/kv head)
   float* lse_blk;             // optional [batch*num_heads, max_blocks]: per-block LSE
   float* lse_final;           // optional [batch*num_heads]: final LSE for the score pass
-  uint32_t* err;              // device error bits
+  uint32_t* err;              // device error bits; err[1]: exchange launch ticket
   int64_t table_stride;
   int64_t hot_slots;
   int64_t warm_slots;
@@ -77,7 +77,7 @@ struct DecodeParams {
   int32_t x_rows_cap;
   int32_t x_units_cap;
   uint64_t x_timeout_ns;
-  const uint32_t* x_epoch_dev;  // when set, the epoch is read from here
+  uint32_t* x_epoch_dev;      // when set, the epoch is read here and advanced by the launch
   uint8_t* x_inbox[8];
   int32_t out_dtype;
   float scale_log2;           // scaling * log2(e)

@@ -10,7 +10,10 @@ the GPUs of one node:
   own pools.  Each rank runs the decode kernel on its range and produces a
   normalised partial (o fp32, LSE); one all-gather of the packed
   [o | LSE] buffer (NCCL over NVLink) and the LSE-merge kernel give every rank
-  the full-context output.  Block scores need no second exchange:
+  the full-context output (``ContextShardedDecode``).  ``P2PContextDecode``
+  does the same inside the decode launch: partials are stored into every
+  rank's inbox over CUDA IPC peer memory, published with epoch flags and
+  merged by the same kernel.  Block scores need no second exchange:
   p_global = p_local * exp(lse_local - lse_global).
 
 COLD blocks stay exact under sharding: each rank adds the analytic
@@ -146,8 +149,8 @@ class PeerExchange:
         self.epoch = 0
         self._own = None
         self._mapped = []
-        # device_epoch: the epoch lives in device memory and advance() adds one
-        # in stream order, so CUDA graph replays see a new epoch every call
+        # device_epoch: the epoch lives in device memory and every launch
+        # advances it, so CUDA graph replays see a new epoch every call
         self.epoch_t = (torch.ones(1, dtype=torch.int32, device=torch.cuda.current_device())
                         if device_epoch else None)
         if inboxes is not None:
@@ -196,11 +199,6 @@ class PeerExchange:
             x.inbox[q] = ptr
         return x
 
-    def advance(self) -> None:
-        """After a call with a device epoch: the next call's epoch (stream order)."""
-        if self.epoch_t is not None:
-            self.epoch_t.add_(1)
-
     def close(self) -> None:
         lib = self._N.load()
         if self._own is not None:
@@ -234,5 +232,4 @@ class P2PContextDecode:
                                               return_scores=return_scores, return_lse=True,
                                               out=out, out_dtype=out_dtype,
                                               exchange=self.exchange.next())
-        self.exchange.advance()
         return ShardResult(o, lse, scores)
