@@ -30,6 +30,10 @@
  *                          split by block range over GPUs): decode, exchange
  *                          of the (o, LSE) partials over NVLink peer memory
  *                          and their merge in one launch per rank
+ *   tkv_prefill_lse /      modeling_llama.py:281-302 compute_prefill_block_scores()
+ *   tkv_prefill_block_scores  with tierkv_policy.py:1378-1388 compute_block_scores():
+ *                          exact prefill block scores without materialising
+ *                          the attention weights
  *   tkv_append_hot_tokens  tierkv_policy.py:934-967 write_hot_tokens() tensor
  *                          work plus the block-table writes of _set_metadata
  *                          (917-926) and set_block_entry (1016-1035), fused
@@ -275,6 +279,27 @@ int32_t tkv_exchange_free(void* ptr);
 
 int32_t tkv_decode_attention_exchange(const tkv_pools* pools, const tkv_decode_args* args,
                                       const tkv_exchange* xc, void* stream);
+
+/* ---- prefill block scores ------------------------------------------------
+ * q [batch, num_heads, tq, head_dim] and k [batch, kv_heads, tk, head_dim]
+ * fp16, contiguous, 16-byte aligned; head_dim 64 or 128; num_heads a
+ * multiple of kv_heads.  causal: key j is visible to query i iff
+ * j <= i + (tk - tq) (requires tk >= tq).
+ * tkv_prefill_lse writes lse [batch, num_heads, tq] fp32, the natural-log
+ * LSE of the scaled, masked logits (what flash attention returns).
+ * tkv_prefill_block_scores writes token_mass [tk] (the softmax mass each key
+ * receives, summed over batch, heads and queries) and block_scores
+ * [ceil(tk / block_size)]: token_mass / (batch * num_heads * tq) averaged over
+ * each block's keys -- the reference's mean of the eager attention weights
+ * over (batch, heads, queries), then per block (tierkv_policy.py:1378-1388). */
+int32_t tkv_prefill_lse(const void* q, const void* k, int32_t batch, int32_t num_heads,
+                        int32_t kv_heads, int32_t tq, int32_t tk, int32_t head_dim, float scaling,
+                        int32_t causal, float* lse, void* stream);
+int32_t tkv_prefill_block_scores(const void* q, const void* k, const float* lse, int32_t batch,
+                                 int32_t num_heads, int32_t kv_heads, int32_t tq, int32_t tk,
+                                 int32_t head_dim, float scaling, int32_t causal,
+                                 int32_t block_size, float* token_mass, float* block_scores,
+                                 void* stream);
 
 /* Reads and clears the device error bits (TKV_DEVERR_*) that decode calls
  * using this workspace have recorded.  Synchronizes the stream. */

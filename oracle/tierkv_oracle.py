@@ -267,3 +267,46 @@ def block_scores_from_probability_sums(score_sums, block_lengths, num_blocks: in
     lens = np.maximum(np.asarray(block_lengths)[:nb], 1).astype(np.float32)
     return (s / lens).astype(np.float32)
 
+
+
+# ---------------------------------------------------------------------------
+# Prefill block scores (modeling_llama.py:281-289 with tierkv_policy.py:1378-1388)
+# ---------------------------------------------------------------------------
+
+def prefill_lse(query, key, scaling: float, causal: bool = True):
+    """LSE (natural log) per query row of the scaled, causally masked logits.
+    query [B, Hq, Tq, D], key [B, Hkv, Tk, D]; key j is visible to query i iff
+    j <= i + (Tk - Tq).  Float64."""
+    q = np.asarray(query, np.float64)
+    k = np.asarray(key, np.float64)
+    b, hq, tq, _ = q.shape
+    g = hq // k.shape[1]
+    k = np.repeat(k, g, axis=1)                      # repeat_kv (modeling_llama.py:213-222)
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scaling
+    if causal:
+        tk = k.shape[2]
+        mask = np.arange(tk)[None, :] > (np.arange(tq)[:, None] + (tk - tq))
+        s = np.where(mask[None, None], -np.inf, s)
+    m = s.max(axis=-1, keepdims=True)
+    return (m + np.log(np.exp(s - m).sum(axis=-1, keepdims=True)))[..., 0]
+
+
+def prefill_block_scores(query, key, scaling: float, block_size: int, causal: bool = True):
+    """The reference's prefill scores on the eager weights, in float64:
+    weights = softmax(Q K^T * scaling + causal mask) (modeling_llama.py:225-245),
+    mean over (batch, heads, queries) per key, then the mean of each
+    block_size chunk of keys, the last one partial (tierkv_policy.py:1378-1388).
+    (The reference rounds the weights and the means to fp16.)"""
+    q = np.asarray(query, np.float64)
+    k = np.asarray(key, np.float64)
+    lse = prefill_lse(q, k, scaling, causal)
+    g = q.shape[1] // k.shape[1]
+    kk = np.repeat(k, g, axis=1)
+    s = np.einsum("bhqd,bhkd->bhqk", q, kk) * scaling
+    tq, tk = q.shape[2], k.shape[2]
+    w = np.exp(s - lse[..., None])
+    if causal:
+        mask = np.arange(tk)[None, :] > (np.arange(tq)[:, None] + (tk - tq))
+        w = np.where(mask[None, None], 0.0, w)
+    token = w.mean(axis=(0, 1, 2))
+    return np.array([token[i:i + block_size].mean() for i in range(0, tk, block_size)])

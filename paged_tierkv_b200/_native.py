@@ -49,6 +49,8 @@ EXPORTED_SYMBOLS = (
     "tkv_exchange_close",
     "tkv_exchange_free",
     "tkv_decode_attention_exchange",
+    "tkv_prefill_lse",
+    "tkv_prefill_block_scores",
 )
 
 TKV_EXCHANGE_MAX_RANKS = 8
@@ -171,6 +173,9 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
         "tkv_exchange_free": ([vp], i32),
         "tkv_decode_attention_exchange": ([ctypes.POINTER(TkvPools), ctypes.POINTER(TkvDecodeArgs),
                                            ctypes.POINTER(TkvExchange), vp], i32),
+        "tkv_prefill_lse": ([vp, vp, i32, i32, i32, i32, i32, i32, ctypes.c_float, i32, vp, vp], i32),
+        "tkv_prefill_block_scores": ([vp, vp, vp, i32, i32, i32, i32, i32, i32, ctypes.c_float, i32,
+                                      i32, vp, vp, vp], i32),
     }
     for name, (argtypes, restype) in sigs.items():
         fn = getattr(lib, name)

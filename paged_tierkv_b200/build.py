@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIBNAME = "libtierkv_b200.so"
-SOURCES = ["tkv_api.cu", "tkv_decode.cu", "tkv_quant.cu"]
+SOURCES = ["tkv_api.cu", "tkv_decode.cu", "tkv_quant.cu", "tkv_prefill.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

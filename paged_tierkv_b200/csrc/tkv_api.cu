@@ -628,6 +628,58 @@ int32_t tkv_append_hot_tokens(const tkv_pools* pools, int32_t hot_slot, int32_t 
   return cuda_status(launch_append(p, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+static int32_t prefill_params(const void* q, const void* k, int32_t batch, int32_t num_heads,
+                              int32_t kv_heads, int32_t tq, int32_t tk, int32_t head_dim,
+                              float scaling, int32_t causal, PrefillParams* p) {
+  if (!q || !k || !aligned(q, 16) || !aligned(k, 16)) return TKV_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return TKV_ERR_UNSUPPORTED;
+  if (batch < 1 || num_heads < 1 || kv_heads < 1 || num_heads % kv_heads != 0 || tq < 1 || tk < 1)
+    return TKV_ERR_INVALID;
+  if (causal && tk < tq) return TKV_ERR_INVALID;
+  std::memset(p, 0, sizeof(*p));
+  p->q = q;
+  p->k = k;
+  p->batch = batch;
+  p->num_heads = num_heads;
+  p->kv_heads = kv_heads;
+  p->groups = num_heads / kv_heads;
+  p->tq = tq;
+  p->tk = tk;
+  p->head_dim = head_dim;
+  p->q_offset = tk - tq;
+  p->causal = causal ? 1 : 0;
+  p->scaling = scaling;
+  int sms = 0;
+  return current_device_sms(&sms);
+}
+
+int32_t tkv_prefill_lse(const void* q, const void* k, int32_t batch, int32_t num_heads,
+                        int32_t kv_heads, int32_t tq, int32_t tk, int32_t head_dim, float scaling,
+                        int32_t causal, float* lse, void* stream) {
+  PrefillParams p;
+  int32_t st = prefill_params(q, k, batch, num_heads, kv_heads, tq, tk, head_dim, scaling, causal, &p);
+  if (st != TKV_OK) return st;
+  if (!lse) return TKV_ERR_INVALID;
+  p.lse = lse;
+  return cuda_status(launch_prefill_lse(p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int32_t tkv_prefill_block_scores(const void* q, const void* k, const float* lse, int32_t batch,
+                                 int32_t num_heads, int32_t kv_heads, int32_t tq, int32_t tk,
+                                 int32_t head_dim, float scaling, int32_t causal,
+                                 int32_t block_size, float* token_mass, float* block_scores,
+                                 void* stream) {
+  PrefillParams p;
+  int32_t st = prefill_params(q, k, batch, num_heads, kv_heads, tq, tk, head_dim, scaling, causal, &p);
+  if (st != TKV_OK) return st;
+  if (!lse || !token_mass || !block_scores || block_size < 1) return TKV_ERR_INVALID;
+  p.lse = const_cast<float*>(lse);
+  p.token_mass = token_mass;
+  p.block_scores = block_scores;
+  p.block_size = block_size;
+  return cuda_status(launch_prefill_scores(p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream) {
   if (!workspace || !bits_out) return TKV_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

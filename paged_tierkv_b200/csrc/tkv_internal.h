@@ -178,6 +178,28 @@ __host__ __device__ inline size_t xchg_total_bytes(int world, int rows, int unit
          ((size_t)2 * rows * world * 4 + 255) / 256 * 256;
 }
 
+struct PrefillParams {
+  const void* q;              // [batch, num_heads, tq, head_dim] fp16
+  const void* k;              // [batch, kv_heads, tk, head_dim] fp16
+  float* lse;                 // [batch, num_heads, tq] natural log
+  float* token_mass;          // [tk]
+  float* block_scores;        // [ceil(tk / block_size)]
+  int32_t batch;
+  int32_t num_heads;
+  int32_t kv_heads;
+  int32_t groups;
+  int32_t tq;
+  int32_t tk;
+  int32_t head_dim;
+  int32_t q_offset;           // tk - tq: query i sits at position i + q_offset
+  int32_t causal;
+  int32_t block_size;
+  float scaling;
+};
+
+cudaError_t launch_prefill_lse(const PrefillParams& p, cudaStream_t stream);
+cudaError_t launch_prefill_scores(const PrefillParams& p, cudaStream_t stream);
+
 cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 cudaError_t launch_promote(const DemoteParams& p, cudaStream_t stream);

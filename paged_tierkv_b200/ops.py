@@ -398,3 +398,62 @@ def promote_blocks_to_hot(pools: TieredPools, src_warm_slots, dst_hot_slots, len
     N.check(N.load().tkv_promote_to_hot(ctypes.byref(ps), src.data_ptr(), dst.data_ptr(),
                                         ln.data_ptr(), int(src.numel()), _stream(stream)),
             "tkv_promote_to_hot")
+
+
+# ---------------------------------------------------------------------------
+# prefill block scores
+# ---------------------------------------------------------------------------
+
+def _prefill_shapes(query: torch.Tensor, key: torch.Tensor):
+    if query.ndim != 4 or key.ndim != 4:
+        raise ValueError("query / key must have shape [batch, heads, tokens, head_dim].")
+    if query.dtype != torch.float16 or key.dtype != torch.float16:
+        raise ValueError("prefill block scores take fp16 query / key states.")
+    if not (query.is_cuda and key.is_cuda):
+        raise ValueError("prefill block scores require CUDA tensors.")
+    b, hq, tq, d = query.shape
+    if key.shape[0] != b or key.shape[3] != d or hq % key.shape[1] != 0:
+        raise ValueError("query / key shapes do not match.")
+    return b, hq, int(key.shape[1]), tq, int(key.shape[2]), d
+
+
+def _aligned16(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def prefill_lse(query: torch.Tensor, key: torch.Tensor, scaling: float, *, causal: bool = True,
+                stream=None) -> torch.Tensor:
+    """Natural-log LSE [B, Hq, Tq] fp32 of softmax(Q K^T * scaling [+ causal mask])."""
+    b, hq, hkv, tq, tk, d = _prefill_shapes(query, key)
+    q, k = _aligned16(query), _aligned16(key)
+    lse = torch.empty((b, hq, tq), dtype=torch.float32, device=query.device)
+    N.check(N.load().tkv_prefill_lse(q.data_ptr(), k.data_ptr(), b, hq, hkv, tq, tk, d,
+                                     float(scaling), int(bool(causal)), lse.data_ptr(),
+                                     _stream(stream)), "tkv_prefill_lse")
+    return lse
+
+
+def prefill_block_scores(query: torch.Tensor, key: torch.Tensor, scaling: float, block_size: int,
+                         *, lse: torch.Tensor | None = None, causal: bool = True,
+                         return_token_mass: bool = False, stream=None):
+    """Exact prefill block scores without attention weights: the mean over
+    (batch, heads, queries) of the softmax mass each key receives, averaged
+    per block of ``block_size`` keys (the reference's compute_block_scores on
+    the eager weights, tierkv_policy.py:1378-1388).  ``lse`` [B, Hq, Tq] fp32
+    (natural log) from the caller's flash attention skips the LSE pass."""
+    b, hq, hkv, tq, tk, d = _prefill_shapes(query, key)
+    q, k = _aligned16(query), _aligned16(key)
+    if lse is None:
+        lse = prefill_lse(q, k, scaling, causal=causal, stream=stream)
+    lse = lse.to(device=query.device, dtype=torch.float32).contiguous()
+    if tuple(lse.shape) != (b, hq, tq):
+        raise ValueError("lse must have shape [batch, num_heads, query_tokens].")
+    nb = (tk + int(block_size) - 1) // int(block_size)
+    mass = torch.empty(tk, dtype=torch.float32, device=query.device)
+    scores = torch.empty(nb, dtype=torch.float32, device=query.device)
+    N.check(N.load().tkv_prefill_block_scores(q.data_ptr(), k.data_ptr(), lse.data_ptr(), b, hq, hkv,
+                                              tq, tk, d, float(scaling), int(bool(causal)),
+                                              int(block_size), mass.data_ptr(), scores.data_ptr(),
+                                              _stream(stream)), "tkv_prefill_block_scores")
+    return (scores, mass) if return_token_mass else scores
