@@ -50,12 +50,14 @@ def parse():
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--sweep", action="store_true",
                     help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
-    ap.add_argument("--config", choices=["c5", "c4", "demote", "tick", "append"], default="c5",
+    ap.add_argument("--config", choices=["c5", "c4", "demote", "tick", "append", "prefill"],
+                    default="c5",
                     help="c5: data-parallel batches (default); c4: one 131k-token context "
                          "over 32 layers, sharded by block range across the GPUs; demote: "
                          "HOT->WARM demotion of 2^20 fp16 [16 x 128] tiles per GPU; tick: one "
                          "policy tick (storage sync) of a 2048-block layer; append: the "
-                         "decode-time KV append of one token")
+                         "decode-time KV append of one token; prefill: exact prefill block "
+                         "scores of one 8192-token layer")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--demote-blocks", type=int, default=65536,
                     help="demote: demoted blocks per launch (x 8 kv heads x K/V tiles)")
@@ -737,6 +739,78 @@ def run_tiering(a, rank, world, dist_on, device):
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(a, rank, device):
+    """Exact prefill block scores of one layer of configuration 3's prompt
+    (8192 tokens, 32 q / 8 kv heads, head_dim 128, block 16, causal):
+    ours with the LSE pass, ours given the LSE of torch's flash SDPA (what a
+    flash prefill returns), and the reference's way on the same GPU (eager
+    weights materialised by torch: QK^T, fp32 softmax, fp16 cast, means)."""
+    from paged_tierkv_b200 import _native, ops
+    _native.load(build_if_missing=True)
+    if rank != 0:
+        return
+    b, hq, hkv, t, d, bs = 1, 32, 8, 8192, 128, 16
+    gen = torch.Generator(device=device).manual_seed(21)
+    q = torch.randn((b, hq, t, d), generator=gen, device=device).to(torch.float16)
+    k = torch.randn((b, hkv, t, d), generator=gen, device=device).to(torch.float16)
+    v = torch.randn((b, hkv, t, d), generator=gen, device=device).to(torch.float16)
+    scaling = d ** -0.5
+    g = hq // hkv
+    kr, vr = k.repeat_interleave(g, dim=1), v.repeat_interleave(g, dim=1)
+    _, lse_flash = torch.ops.aten._scaled_dot_product_flash_attention(q, kr, vr, 0.0, True, False,
+                                                                      scale=scaling)[:2]
+    steps = max(3, min(a.steps, 20))
+
+    def timed(fn):
+        for _ in range(max(2, a.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def eager(cast=torch.float16):
+        w = torch.matmul(q, kr.transpose(2, 3)) * scaling
+        w = w + torch.full((t, t), float("-inf"), device=device).triu(1)
+        w = torch.softmax(w, dim=-1, dtype=torch.float32).to(cast)
+        tok = w.mean(dim=(0, 1, 2), dtype=torch.float32)
+        return torch.stack([c.mean() for c in torch.split(tok, bs)])
+
+    ms_full = timed(lambda: ops.prefill_block_scores(q, k, scaling, bs))
+    ms_cols = timed(lambda: ops.prefill_block_scores(q, k, scaling, bs, lse=lse_flash))
+    ms_eager = timed(eager)
+    ours = ops.prefill_block_scores(q, k, scaling, bs)
+    ref32 = eager(torch.float32)  # without the reference's fp16 rounding of the weights
+    rel = float(((ours - ref32).abs() / ref32.abs().clamp_min(1e-12)).max())
+    flops_pass = 2.0 * d * (t * (t + 1) / 2) * hq  # one causal Q K^T
+    peak = None
+    try:
+        with open(PEAKS) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    ach = 2 * flops_pass / (ms_full * 1e-3) / 1e12
+    line = {
+        "metric": "prefill block-score ms (one 8192-token layer, 32 q / 8 kv heads, D 128, causal)",
+        "value": round(ms_full, 3), "unit": "ms", "n_gpus": 1, "steps": steps, "warmup": a.warmup,
+        "ms_per_step": round(ms_full, 3), "higher_is_better": False, "scaling": "none",
+        "dtype": "fp16 mma, fp32 accumulate", "data": "synthetic N(0,1)",
+        "config": {"workload": "prefill_scores_t8192", "block_size": bs},
+        "given_flash_lse_ms": round(ms_cols, 3),
+        "torch_eager_weights_ms": round(ms_eager, 3),
+        "max_rel_diff_vs_fp32_eager": rel,
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(ach / peak, 4) if peak else None,
+                     "note": "mma.m16n8k16 (legacy tensor path); two causal Q K^T passes"},
+        "gpu_launches": steps * 4,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -761,6 +835,8 @@ def main():
             run_demote(a, rank, world, dist_on, device)
         elif a.config in ("tick", "append"):
             run_tiering(a, rank, world, dist_on, device)
+        elif a.config == "prefill":
+            run_prefill(a, rank, device)
         else:
             run_ours(a, rank, world, dist_on, device)
     finally:
