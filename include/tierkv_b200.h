@@ -300,6 +300,9 @@ int32_t tkv_prefill_block_scores(const void* q, const void* k, const float* lse,
                                  int32_t head_dim, float scaling, int32_t causal,
                                  int32_t block_size, float* token_mass, float* block_scores,
                                  void* stream);
+/* Reads and clears the error bits (TKV_DEVERR_TIMEOUT) the prefill kernels of
+ * the current device have recorded.  Synchronizes the stream. */
+int32_t tkv_prefill_read_errors(uint32_t* bits_out, void* stream);
 
 /* Reads and clears the device error bits (TKV_DEVERR_*) that decode calls
  * using this workspace have recorded.  Synchronizes the stream. */

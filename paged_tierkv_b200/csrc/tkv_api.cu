@@ -287,6 +287,20 @@ inline int32_t cuda_status(cudaError_t e) { return e == cudaSuccess ? TKV_OK : T
 
 }  // namespace
 
+bool tkv::encode_head_rows_map(CUtensorMap* map, const void* base, int64_t heads, int64_t rows,
+                               int head_dim) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {64, (cuuint64_t)rows, (cuuint64_t)(head_dim / 64), (cuuint64_t)heads};
+  cuuint64_t strides[3] = {(cuuint64_t)head_dim * 2, 128, (cuuint64_t)rows * head_dim * 2};
+  cuuint32_t box[4] = {64, 128, (cuuint32_t)(head_dim / 64), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 extern "C" {
 
 int32_t tkv_get_version(void) { return TKV_ABI_VERSION; }
@@ -628,6 +642,11 @@ int32_t tkv_append_hot_tokens(const tkv_pools* pools, int32_t hot_slot, int32_t 
   return cuda_status(launch_append(p, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+static bool prefill_maps(const PrefillParams& p, CUtensorMap maps[2]) {
+  return encode_head_rows_map(&maps[0], p.q, (int64_t)p.batch * p.num_heads, p.tq, p.head_dim) &&
+         encode_head_rows_map(&maps[1], p.k, (int64_t)p.batch * p.kv_heads, p.tk, p.head_dim);
+}
+
 static int32_t prefill_params(const void* q, const void* k, int32_t batch, int32_t num_heads,
                               int32_t kv_heads, int32_t tq, int32_t tk, int32_t head_dim,
                               float scaling, int32_t causal, PrefillParams* p) {
@@ -661,7 +680,9 @@ int32_t tkv_prefill_lse(const void* q, const void* k, int32_t batch, int32_t num
   if (st != TKV_OK) return st;
   if (!lse) return TKV_ERR_INVALID;
   p.lse = lse;
-  return cuda_status(launch_prefill_lse(p, reinterpret_cast<cudaStream_t>(stream)));
+  CUtensorMap maps[2];
+  if (!prefill_maps(p, maps)) return TKV_ERR_CUDA;
+  return cuda_status(launch_prefill_lse(p, maps, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int32_t tkv_prefill_block_scores(const void* q, const void* k, const float* lse, int32_t batch,
@@ -677,7 +698,23 @@ int32_t tkv_prefill_block_scores(const void* q, const void* k, const float* lse,
   p.token_mass = token_mass;
   p.block_scores = block_scores;
   p.block_size = block_size;
-  return cuda_status(launch_prefill_scores(p, reinterpret_cast<cudaStream_t>(stream)));
+  CUtensorMap maps[2];
+  if (!prefill_maps(p, maps)) return TKV_ERR_CUDA;
+  return cuda_status(launch_prefill_scores(p, maps, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int32_t tkv_prefill_read_errors(uint32_t* bits_out, void* stream) {
+  if (!bits_out) return TKV_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t* word = nullptr;
+  if (prefill_error_word(&word) != cudaSuccess) return TKV_ERR_CUDA;
+  uint32_t bits = 0;
+  if (cudaMemcpyAsync(&bits, word, sizeof(bits), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return TKV_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return TKV_ERR_CUDA;
+  if (cudaMemsetAsync(word, 0, sizeof(uint32_t), s) != cudaSuccess) return TKV_ERR_CUDA;
+  *bits_out = bits;
+  return TKV_OK;
 }
 
 int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream) {

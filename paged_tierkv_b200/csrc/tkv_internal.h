@@ -195,10 +195,23 @@ struct PrefillParams {
   int32_t causal;
   int32_t block_size;
   float scaling;
+  int32_t parts;              // column pass: CTAs per key tile
+  int32_t part_items;         // column pass: (head, query tile) items per CTA
+  uint32_t* err;              // the device's prefill error word (TKV_DEVERR_*)
 };
 
-cudaError_t launch_prefill_lse(const PrefillParams& p, cudaStream_t stream);
-cudaError_t launch_prefill_scores(const PrefillParams& p, cudaStream_t stream);
+// maps[0]: Q as [batch * num_heads][tq][head_dim]; maps[1]: K as
+// [batch * kv_heads][tk][head_dim] (encode_head_rows_map).
+cudaError_t launch_prefill_lse(const PrefillParams& p, const CUtensorMap maps[2],
+                               cudaStream_t stream);
+cudaError_t launch_prefill_scores(const PrefillParams& p, const CUtensorMap maps[2],
+                                  cudaStream_t stream);
+cudaError_t prefill_error_word(uint32_t** out);
+// 4-D tiled map over fp16 rows [heads][rows][head_dim]: dims {64, rows,
+// head_dim / 64, heads}, box {64, 128, head_dim / 64, 1}, 128-byte swizzle; a
+// box lands as [head_dim / 64][128][64] and rows past `rows` read as zero.
+bool encode_head_rows_map(CUtensorMap* map, const void* base, int64_t heads, int64_t rows,
+                          int head_dim);
 
 cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);

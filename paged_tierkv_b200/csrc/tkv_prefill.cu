@@ -7,206 +7,374 @@
 // from modeling_llama.py:281-289); with SDPA / flash prefill it falls back to
 // a sink + recency proxy (modeling_llama.py:291-302) because the weights never
 // exist.  Here the exact scores come from two tensor-core passes over Q K^T:
-//   lse_kernel      per query row: LSE of the scaled, causally masked logits
+//   LSE pass        per query row: LSE of the scaled, causally masked logits
 //                   (skipped when the caller's flash attention returns it);
-//   colsum_kernel   per key tile: sum over the group's query heads and every
-//                   query row of exp(s * scaling - LSE_q) -- the attention
-//                   mass each key receives -- accumulated per key;
+//   column pass     per key: sum over the group's query heads and every query
+//                   row of exp(s * scaling - LSE_q) -- the attention mass each
+//                   key receives -- accumulated per key;
 //   block_mean_kernel  token mass / (batch * heads * queries), then the mean
 //                   over each block's keys.
-// Both passes use mma.m16n8k16 (f16 in, f32 accumulate) with ldmatrix-fed
-// fragments; exponentials in the log2 domain.
+//
+// Both passes are one warp-specialised tcgen05 kernel.  A CTA keeps 128 rows
+// resident in shared memory as the MMA's A operand (M = 128): query rows for
+// the LSE pass, key rows for the column pass.  Warp 4 streams 128-row tiles of
+// the other operand (key tiles, or the (head, query tile) pairs that can see
+// the keys) through a ring of shared-memory stages by TMA; one thread of warp 5
+// issues tcgen05.mma (fp16 in, fp32 accumulate, N = 128) into one of two
+// 128-column TMEM accumulators; warps 0-3 read the accumulator with tcgen05.ld,
+// one thread per TMEM lane, i.e. per resident row, so the softmax statistics
+// need no cross-thread reduction.  Exponentials run in the log2 domain on the
+// MUFU unit, which bounds the kernel (one exp per logit; the MMA needs half the
+// time the 128 x 128 exps of a tile take).
+//
+// Every mbarrier wait is bounded (TKV_DEVERR_TIMEOUT in the prefill error
+// word); in-flight copies and MMAs are waited for before the CTA frees its
+// TMEM and exits.
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include "tierkv_b200.h"
 #include "tkv_internal.h"
 #include "tkv_ptx.cuh"
 
 namespace tkv {
 
+// Error bits (TKV_DEVERR_*) of the prefill kernels of this device.
+__device__ uint32_t g_tkv_prefill_err;
+
 constexpr float kLog2eP = 1.4426950408889634f;
+constexpr int kTileRows = 128;       // M of every MMA and the rows (N) of every streamed tile
+constexpr int kUmmaThreads = 192;    // warps 0-3 epilogue (TMEM lane quarters), 4 TMA, 5 MMA
+constexpr uint32_t kTmemCols = 256;  // two fp32 accumulators of 128 columns
+constexpr uint32_t kIdesc = umma_idesc_f16_f32(128, 128);
 
-// A 64-row tile of fp16 rows [row0, row0 + 64) x D from `src` (row stride D)
-// into shared memory with row stride D + 8 halves; rows >= rows_valid are zero.
 template <int D>
-__device__ __forceinline__ void stage_rows(__half* dst, const __half* src, int row0, int rows_valid) {
-  constexpr int kVec = D / 8;  // 16-byte vectors per row
-  for (int e = threadIdx.x; e < 64 * kVec; e += 128) {
-    const int r = e / kVec, c = e % kVec;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (row0 + r < rows_valid) v = __ldg(reinterpret_cast<const uint4*>(src + (size_t)(row0 + r) * D) + c);
-    *reinterpret_cast<uint4*>(dst + r * (D + 8) + 8 * c) = v;
+struct PfLayout {
+  static constexpr int kTile = kTileRows * D * 2;  // [D/64][128 rows][64] fp16, 128B-swizzled
+  static constexpr int kStages = D == 128 ? 2 : 4;
+  static constexpr int kBarOff = kTile * (1 + kStages);
+  // full[S], empty[S], resident, tfull[2], tempty[2], done
+  static constexpr int kNumBars = 2 * kStages + 6;
+  static constexpr int kLseOff = kBarOff + kNumBars * 8;
+  static constexpr int kTaddrOff = kLseOff + 2 * kTileRows * 4;
+  static constexpr int kBytes = kTaddrOff + 16 + 1024;  // + slack to align the base to 1024
+};
+
+// The CTA's share of a pass: the resident tile (map row, map head) and n
+// streamed tiles.
+struct PfWork {
+  int n;          // streamed tiles
+  int res_row, res_head;
+  int b, kvh;
+  int q0;         // LSE pass: first query row of the resident tile
+  int k0;         // column pass: first key of the resident tile
+  int qt_first, per_head, i0;  // column pass: item i -> (head hh, query tile)
+};
+
+// LSE pass: CTA = (batch, head, 128-query tile); item i = key tile i.  The
+// grid runs the query tiles that see the most keys first.
+__device__ __forceinline__ PfWork lse_work(const PrefillParams& p) {
+  PfWork w{};
+  const int nqt = (p.tq + kTileRows - 1) / kTileRows;
+  const int bh_count = p.batch * p.num_heads;
+  const int idx = blockIdx.x;
+  const int qt = p.causal ? nqt - 1 - idx / bh_count : idx / bh_count;
+  const int bh = idx % bh_count;
+  w.b = bh / p.num_heads;
+  w.kvh = (bh % p.num_heads) / p.groups;
+  w.q0 = qt * kTileRows;
+  w.res_row = w.q0;
+  w.res_head = bh;
+  const int last_key = p.causal ? min(p.tk, w.q0 + kTileRows + p.q_offset) : p.tk;
+  w.n = (last_key + kTileRows - 1) / kTileRows;
+  return w;
+}
+
+// Column pass: CTA = (batch, kv head, 128-key tile, part); the key tile's
+// items are the (query head of the group, 128-query tile) pairs that can see
+// its keys, cut into parts of p.part_items.  Key tiles with the most items run
+// first.
+__device__ __forceinline__ PfWork cols_work(const PrefillParams& p) {
+  PfWork w{};
+  const int kvb = p.batch * p.kv_heads;
+  const int idx = blockIdx.x;
+  const int kt = idx / (p.parts * kvb);
+  const int rem = idx % (p.parts * kvb);
+  const int part = rem / kvb;
+  const int bk = rem % kvb;
+  w.b = bk / p.kv_heads;
+  w.kvh = bk % p.kv_heads;
+  w.k0 = kt * kTileRows;
+  w.res_row = w.k0;
+  w.res_head = bk;
+  const int nqt = (p.tq + kTileRows - 1) / kTileRows;
+  w.qt_first = p.causal ? max(0, w.k0 - p.q_offset) / kTileRows : 0;
+  w.per_head = max(0, nqt - w.qt_first);
+  const int total = p.groups * w.per_head;
+  w.i0 = part * p.part_items;
+  w.n = max(0, min(total - w.i0, p.part_items));
+  return w;
+}
+
+// Column pass item i: query head and first query row.
+__device__ __forceinline__ void cols_item(const PrefillParams& p, const PfWork& w, int i, int& h,
+                                          int& q0) {
+  const int gi = w.i0 + i;
+  h = w.kvh * p.groups + gi / w.per_head;
+  q0 = (w.qt_first + gi % w.per_head) * kTileRows;
+}
+
+// log2-domain LSE of query row q of head h (+inf for rows past the end, whose
+// exponentials then vanish).
+__device__ __forceinline__ float lse2_of(const PrefillParams& p, int b, int h, int q) {
+  return q < p.tq ? __ldg(p.lse + ((size_t)b * p.num_heads + h) * p.tq + q) * kLog2eP : INFINITY;
+}
+
+__device__ __forceinline__ void tmem_wait_ld_into(uint32_t (&v)[32]) {
+  // the wait "rewrites" the registers, so no use of them moves above it
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]),
+                 "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]),
+                 "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]),
+                 "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]),
+                 "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]),
+                 "+r"(v[30]), "+r"(v[31])
+               :
+               : "memory");
+}
+
+template <int D, bool kCols>
+__global__ void __launch_bounds__(kUmmaThreads, 2)
+    umma_pass_kernel(const __grid_constant__ PrefillParams p,
+                     const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_k) {
+  using L = PfLayout<D>;
+  constexpr int S = L::kStages;
+  extern __shared__ uint8_t pf_raw[];
+  const uint32_t raw = smem_u32(pf_raw);
+  uint8_t* smem = pf_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* res_full = bars + 2 * S;
+  uint64_t* tfull = res_full + 1;
+  uint64_t* tempty = res_full + 3;
+  uint64_t* done = res_full + 5;
+  float* lse_s = reinterpret_cast<float*>(smem + L::kLseOff);
+  uint32_t* taddr_s = reinterpret_cast<uint32_t*>(smem + L::kTaddrOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const PfWork w = kCols ? cols_work(p) : lse_work(p);
+  if (w.n <= 0) return;  // CTA-uniform: an empty part of a short key tile
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(res_full, 1);
+    mbar_init(tfull, 1);
+    mbar_init(tfull + 1, 1);
+    mbar_init(tempty, 4 * 32);
+    mbar_init(tempty + 1, 4 * 32);
+    mbar_init(done, 1);
+    fence_mbar_init();
   }
-}
-
-// A fragments (16 rows x 16 dims, k-step ks) of a staged 64-row tile for the
-// warp's rows [16 w, 16 w + 16).
-template <int D>
-__device__ __forceinline__ void load_afrag(uint32_t base, int w, int lane, int ks, uint32_t (&a)[4]) {
-  const int j = lane >> 3, r = lane & 7;
-  const uint32_t addr = base + ((16 * w + r + 8 * (j & 1)) * (D + 8) + 16 * ks + 8 * (j >> 1)) * 2;
-  ldsm_x4(addr, a[0], a[1], a[2], a[3]);
-}
-
-// B fragments of k-steps 2m, 2m+1 for the 8 rows [8 n, 8 n + 8) of a staged tile.
-template <int D>
-__device__ __forceinline__ void load_bfrag(uint32_t base, int n, int lane, int m, uint32_t& b00,
-                                           uint32_t& b01, uint32_t& b10, uint32_t& b11) {
-  const uint32_t addr = base + ((8 * n + (lane & 7)) * (D + 8) + 32 * m + 8 * (lane >> 3)) * 2;
-  ldsm_x4(addr, b00, b01, b10, b11);
-}
-
-// ---------------------------------------------------------------- LSE pass
-// Grid (ceil(Tq / 64), num_heads, batch); warp w owns query rows 16 w .. 16 w + 15
-// of the tile (the M dimension), keys run over 64-key tiles (8 n-tiles).
-template <int D>
-__global__ void __launch_bounds__(128) lse_kernel(const PrefillParams p) {
-  __shared__ __align__(16) __half sq[64 * (D + 8)];
-  __shared__ __align__(16) __half sk[64 * (D + 8)];
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int kvh = h / p.groups;
-  const __half* q = reinterpret_cast<const __half*>(p.q) + ((size_t)b * p.num_heads + h) * p.tq * D;
-  const __half* k = reinterpret_cast<const __half*>(p.k) + ((size_t)b * p.kv_heads + kvh) * p.tk * D;
-  stage_rows<D>(sq, q, qt * 64, p.tq);
+  if (warp == 4) tmem_alloc(taddr_s, kTmemCols);
+  tc_fence_before();
   __syncthreads();
-  uint32_t afr[D / 16][4];
-#pragma unroll
-  for (int ks = 0; ks < D / 16; ++ks) load_afrag<D>(smem_u32(sq), warp, lane, ks, afr[ks]);
-  const float c = p.scaling * kLog2eP;
-  // this thread's rows: query 16 w + g and 16 w + g + 8 (positions with the causal offset)
-  const int q_lo = qt * 64 + 16 * warp + g, q_hi = q_lo + 8;
-  const int pos_lo = q_lo + p.q_offset, pos_hi = q_hi + p.q_offset;
-  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
-  const int last_key = min(p.tk, (p.causal ? qt * 64 + 63 + p.q_offset + 1 : p.tk));
-  for (int k0 = 0; k0 < last_key; k0 += 64) {
-    __syncthreads();
-    stage_rows<D>(sk, k, k0, p.tk);
-    __syncthreads();
-    float s[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s[n][i] = 0.f;
-#pragma unroll
-      for (int m = 0; m < D / 32; ++m) {
-        uint32_t b00, b01, b10, b11;
-        load_bfrag<D>(smem_u32(sk), n, lane, m, b00, b01, b10, b11);
-        mma_16816(s[n], afr[2 * m][0], afr[2 * m][1], afr[2 * m][2], afr[2 * m][3], b00, b01);
-        mma_16816(s[n], afr[2 * m + 1][0], afr[2 * m + 1][1], afr[2 * m + 1][2], afr[2 * m + 1][3],
-                  b10, b11);
-      }
-    }
-    float mx_lo = -INFINITY, mx_hi = -INFINITY;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int key = k0 + 8 * n + 2 * t + i;
-        const bool ok_lo = key < p.tk && (!p.causal || key <= pos_lo);
-        const bool ok_hi = key < p.tk && (!p.causal || key <= pos_hi);
-        s[n][i] = ok_lo ? s[n][i] * c : -INFINITY;
-        s[n][2 + i] = ok_hi ? s[n][2 + i] * c : -INFINITY;
-        mx_lo = fmaxf(mx_lo, s[n][i]);
-        mx_hi = fmaxf(mx_hi, s[n][2 + i]);
-      }
-    }
-#pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
-      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
-    }
-    const float nm_lo = fmaxf(m_lo, mx_lo), nm_hi = fmaxf(m_hi, mx_hi);
-    if (nm_lo != -INFINITY) l_lo *= ex2(m_lo - nm_lo);
-    if (nm_hi != -INFINITY) l_hi *= ex2(m_hi - nm_hi);
-    m_lo = nm_lo;
-    m_hi = nm_hi;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        if (m_lo != -INFINITY) l_lo += ex2(s[n][i] - m_lo);
-        if (m_hi != -INFINITY) l_hi += ex2(s[n][2 + i] - m_hi);
-      }
-    }
-  }
-#pragma unroll
-  for (int off = 1; off < 4; off <<= 1) {
-    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
-    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
-  }
-  if (t == 0) {
-    float* out = p.lse + ((size_t)b * p.num_heads + h) * p.tq;
-    const float kLn2 = 0.6931471805599453f;
-    if (q_lo < p.tq) out[q_lo] = l_lo > 0.f ? (m_lo + lg2(l_lo)) * kLn2 : -INFINITY;
-    if (q_hi < p.tq) out[q_hi] = l_hi > 0.f ? (m_hi + lg2(l_hi)) * kLn2 : -INFINITY;
-  }
-}
+  tc_fence_after();
+  const uint32_t tmem = *taddr_s;
 
-// ---------------------------------------------------------------- column sums
-// Grid (ceil(Tk / 64), kv_heads, batch); warp w owns keys 16 w .. 16 w + 15 of
-// the tile (the M dimension of S^T = K Q^T); the loop runs over the group's
-// query heads and the 64-row query tiles that can see the tile's keys.
-template <int D>
-__global__ void __launch_bounds__(128) colsum_kernel(const PrefillParams p) {
-  __shared__ __align__(16) __half sk[64 * (D + 8)];
-  __shared__ __align__(16) __half sq[64 * (D + 8)];
-  __shared__ float slse[64];
-  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const __half* k = reinterpret_cast<const __half*>(p.k) + ((size_t)b * p.kv_heads + kvh) * p.tk * D;
-  stage_rows<D>(sk, k, kt * 64, p.tk);
-  __syncthreads();
-  uint32_t afr[D / 16][4];
-#pragma unroll
-  for (int ks = 0; ks < D / 16; ++ks) load_afrag<D>(smem_u32(sk), warp, lane, ks, afr[ks]);
-  const float c = p.scaling * kLog2eP;
-  const int key_lo = kt * 64 + 16 * warp + g, key_hi = key_lo + 8;
-  float sum_lo = 0.f, sum_hi = 0.f;
-  // the first query that sees this tile's first key
-  const int q_first = p.causal ? max(0, kt * 64 - p.q_offset) : 0;
-  for (int hh = 0; hh < p.groups; ++hh) {
-    const int h = kvh * p.groups + hh;
-    const __half* q = reinterpret_cast<const __half*>(p.q) + ((size_t)b * p.num_heads + h) * p.tq * D;
-    const float* lse = p.lse + ((size_t)b * p.num_heads + h) * p.tq;
-    for (int q0 = (q_first / 64) * 64; q0 < p.tq; q0 += 64) {
-      __syncthreads();
-      stage_rows<D>(sq, q, q0, p.tq);
-      if (threadIdx.x < 64) {
-        const int qi = q0 + threadIdx.x;
-        slse[threadIdx.x] = qi < p.tq ? lse[qi] * kLog2eP : INFINITY;  // +inf: no mass
+  if (warp == 4) {
+    // ---- TMA producer
+    if (lane == 0) {
+      const CUtensorMap* rmap = kCols ? &tm_k : &tm_q;
+      const CUtensorMap* smap = kCols ? &tm_q : &tm_k;
+      prefetch_tensormap(rmap);
+      prefetch_tensormap(smap);
+      mbar_arrive_expect_tx(res_full, L::kTile);
+      tma_load_4d(smem, rmap, 0, w.res_row, 0, w.res_head, res_full);
+      bool ok = true;
+      int issued = 0;
+      for (int i = 0; i < w.n; ++i) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait(empty + s, ((i / S) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        int row, head;
+        if (kCols) {
+          int h;
+          cols_item(p, w, i, h, row);
+          head = w.b * p.num_heads + h;
+        } else {
+          row = i * kTileRows;
+          head = w.b * p.kv_heads + w.kvh;
+        }
+        mbar_arrive_expect_tx(full + s, L::kTile);
+        tma_load_4d(smem + L::kTile * (1 + s), smap, 0, row, 0, head, full + s);
+        issued = i + 1;
       }
-      __syncthreads();
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int m = 0; m < D / 32; ++m) {
-          uint32_t b00, b01, b10, b11;
-          load_bfrag<D>(smem_u32(sq), n, lane, m, b00, b01, b10, b11);
-          mma_16816(s, afr[2 * m][0], afr[2 * m][1], afr[2 * m][2], afr[2 * m][3], b00, b01);
-          mma_16816(s, afr[2 * m + 1][0], afr[2 * m + 1][1], afr[2 * m + 1][2], afr[2 * m + 1][3],
-                    b10, b11);
+      // no copy may still be landing in shared memory when the CTA exits
+      ok = mbar_wait(res_full, 0) && ok;
+      for (int i = max(0, issued - S); i < issued; ++i) ok = mbar_wait(full + i % S, (i / S) & 1) && ok;
+      if (!ok) atomicOr(p.err, TKV_DEVERR_TIMEOUT);
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ---- MMA issuer: S^T tile (kCols) or S tile = resident (A) x streamed (B)^T
+    if (lane == 0) {
+      bool ok = mbar_wait(res_full, 0);
+      const uint32_t a_base = smem_u32(smem);
+      for (int i = 0; ok && i < w.n; ++i) {
+        const int s = i % S, acc = i & 1;
+        if (!mbar_wait(full + s, (i / S) & 1) ||
+            (i >= 2 && !mbar_wait(tempty + acc, ((i >> 1) - 1) & 1))) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        const uint32_t b_base = smem_u32(smem + L::kTile * (1 + s));
+        const uint32_t d = tmem + (uint32_t)(acc * kTileRows);
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int ql = 8 * n + 2 * t + i;          // query row in the tile
-          const int pos = q0 + ql + p.q_offset;      // its position
-          const float l2 = slse[ql];
-          if (key_lo < p.tk && (!p.causal || key_lo <= pos)) sum_lo += ex2(s[i] * c - l2);
-          if (key_hi < p.tk && (!p.causal || key_hi <= pos)) sum_hi += ex2(s[2 + i] * c - l2);
+        for (int ks = 0; ks < D / 16; ++ks) {
+          // 64-element K chunks are 128 rows x 128 bytes apart; K steps of 16 are 32 bytes
+          const uint32_t off = (uint32_t)((ks >> 2) * kTileRows * 128 + (ks & 3) * 32);
+          umma_f16(d, umma_desc_k_sw128(a_base + off), umma_desc_k_sw128(b_base + off), kIdesc,
+                   ks > 0 ? 1u : 0u);
         }
+        umma_commit(empty + s);
+        umma_commit(tfull + acc);
+      }
+      umma_commit(done);  // every MMA issued above has completed once this phase does
+      ok = mbar_wait(done, 0) && ok;
+      if (!ok) atomicOr(p.err, TKV_DEVERR_TIMEOUT);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: thread t owns TMEM lane t = resident row t
+    const int t = threadIdx.x;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    const float c = p.scaling * kLog2eP;
+    bool ok = true;
+    if (kCols) {
+      const int key = w.k0 + t;
+      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+      int h, q0;
+      cols_item(p, w, 0, h, q0);
+      float lnext = lse2_of(p, w.b, h, q0 + t);  // thread t stages column t's LSE
+      for (int i = 0; i < w.n; ++i) {
+        float* ls = lse_s + (i & 1) * kTileRows;
+        ls[t] = lnext;
+        cols_item(p, w, i, h, q0);
+        if (i + 1 < w.n) {
+          int h1, q1;
+          cols_item(p, w, i + 1, h1, q1);
+          lnext = lse2_of(p, w.b, h1, q1 + t);
+        }
+        named_barrier(1, 4 * 32);
+        const int acc = i & 1;
+        // after a timeout the loop keeps its shape (no waits), so every thread
+        // meets the same named barriers and whole warps run tcgen05.ld
+        if (ok && !mbar_wait(tfull + acc, (i >> 1) & 1)) ok = false;
+        __syncwarp();
+        tc_fence_after();
+        // causal: query column j sees this row's key iff j >= jmin
+        const bool diag = p.causal && q0 + p.q_offset < w.k0 + kTileRows - 1;
+        const int jmin = key - p.q_offset - q0;
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + 32 * c4), v);
+          tmem_wait_ld_into(v);
+          if (c4 == 3) {
+            tc_fence_before();
+            mbar_arrive(tempty + acc);
+          }
+          const float* l = ls + 32 * c4;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(l + j);
+            float x0 = fmaf(__uint_as_float(v[j]), c, -l4.x);
+            float x1 = fmaf(__uint_as_float(v[j + 1]), c, -l4.y);
+            float x2 = fmaf(__uint_as_float(v[j + 2]), c, -l4.z);
+            float x3 = fmaf(__uint_as_float(v[j + 3]), c, -l4.w);
+            if (diag) {
+              const int col = 32 * c4 + j;
+              x0 = col >= jmin ? x0 : -INFINITY;
+              x1 = col + 1 >= jmin ? x1 : -INFINITY;
+              x2 = col + 2 >= jmin ? x2 : -INFINITY;
+              x3 = col + 3 >= jmin ? x3 : -INFINITY;
+            }
+            sum0 += ex2(x0);
+            sum1 += ex2(x1);
+            sum2 += ex2(x2);
+            sum3 += ex2(x3);
+          }
+        }
+      }
+      if (ok && key < p.tk) atomicAdd(p.token_mass + key, (sum0 + sum1) + (sum2 + sum3));
+    } else {
+      const int q = w.q0 + t;
+      const int qpos = q + p.q_offset;
+      float m = -INFINITY, l = 0.f;
+      for (int i = 0; i < w.n; ++i) {
+        const int acc = i & 1;
+        if (ok && !mbar_wait(tfull + acc, (i >> 1) & 1)) ok = false;
+        __syncwarp();
+        tc_fence_after();
+        const int k0 = i * kTileRows;
+        // CTA-uniform: does any key of the tile fall outside some row's view?
+        const bool edge =
+            k0 + kTileRows > p.tk || (p.causal && k0 + kTileRows - 1 > w.q0 + p.q_offset);
+        const int jmax = (p.causal ? min(p.tk, qpos + 1) : p.tk) - k0;  // columns j < jmax count
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + 32 * c4), v);
+          tmem_wait_ld_into(v);
+          if (c4 == 3) {
+            tc_fence_before();
+            mbar_arrive(tempty + acc);
+          }
+          float x[32];
+          float cm = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            x[j] = __uint_as_float(v[j]) * c;
+            if (edge) x[j] = 32 * c4 + j < jmax ? x[j] : -INFINITY;
+            cm = fmaxf(cm, x[j]);
+          }
+          const float mn = fmaxf(m, cm);
+          if (mn != -INFINITY) {
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              s0 += ex2(x[j] - mn);
+              s1 += ex2(x[j + 1] - mn);
+              s2 += ex2(x[j + 2] - mn);
+              s3 += ex2(x[j + 3] - mn);
+            }
+            l = l * ex2(m - mn) + ((s0 + s1) + (s2 + s3));
+            m = mn;
+          }
+        }
+      }
+      if (ok && q < p.tq) {
+        const float kLn2 = 0.6931471805599453f;
+        p.lse[(size_t)w.res_head * p.tq + q] = l > 0.f ? (m + lg2(l)) * kLn2 : -INFINITY;
       }
     }
+    if (!ok) atomicOr(p.err, TKV_DEVERR_TIMEOUT);
   }
-#pragma unroll
-  for (int off = 1; off < 4; off <<= 1) {
-    sum_lo += __shfl_xor_sync(0xffffffffu, sum_lo, off);
-    sum_hi += __shfl_xor_sync(0xffffffffu, sum_hi, off);
-  }
-  if (t == 0) {
-    if (key_lo < p.tk) atomicAdd(p.token_mass + key_lo, sum_lo);
-    if (key_hi < p.tk) atomicAdd(p.token_mass + key_hi, sum_hi);
+
+  // every TMEM read and MMA of the CTA has completed: free the accumulators
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_free(tmem, kTmemCols);
   }
 }
 
@@ -222,22 +390,50 @@ __global__ void block_mean_kernel(const float* token_mass, int tk, int block_siz
   block_scores[blk] = sum / (float)(k1 - k0);
 }
 
-cudaError_t launch_prefill_lse(const PrefillParams& p, cudaStream_t stream) {
-  const dim3 grid((unsigned)((p.tq + 63) / 64), (unsigned)p.num_heads, (unsigned)p.batch);
-  if (p.head_dim == 128) lse_kernel<128><<<grid, 128, 0, stream>>>(p);
-  else if (p.head_dim == 64) lse_kernel<64><<<grid, 128, 0, stream>>>(p);
-  else return cudaErrorInvalidValue;
+cudaError_t prefill_error_word(uint32_t** out) {
+  return cudaGetSymbolAddress(reinterpret_cast<void**>(out), g_tkv_prefill_err);
+}
+
+template <int D, bool kCols>
+static cudaError_t launch_umma(PrefillParams p, const CUtensorMap maps[2], long long grid,
+                               cudaStream_t stream) {
+  if (grid <= 0 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+  cudaError_t e = prefill_error_word(&p.err);
+  if (e != cudaSuccess) return e;
+  auto kern = umma_pass_kernel<D, kCols>;
+  // the shared-memory opt-in is per function and device; it is idempotent
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PfLayout<D>::kBytes);
+  if (e != cudaSuccess) return e;
+  kern<<<(unsigned)grid, kUmmaThreads, PfLayout<D>::kBytes, stream>>>(p, maps[0], maps[1]);
   return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_scores(const PrefillParams& p, cudaStream_t stream) {
+cudaError_t launch_prefill_lse(const PrefillParams& p, const CUtensorMap maps[2],
+                               cudaStream_t stream) {
+  const long long grid = (long long)((p.tq + kTileRows - 1) / kTileRows) * p.batch * p.num_heads;
+  if (p.head_dim == 128) return launch_umma<128, false>(p, maps, grid, stream);
+  if (p.head_dim == 64) return launch_umma<64, false>(p, maps, grid, stream);
+  return cudaErrorInvalidValue;
+}
+
+// Items (query head, query tile) per column-pass CTA: enough to amortise the
+// CTA's resident-tile load and TMEM setup, few enough that the longest key
+// tiles split over several SMs.
+constexpr int kColsPartItems = 32;
+
+cudaError_t launch_prefill_scores(const PrefillParams& p_in, const CUtensorMap maps[2],
+                                  cudaStream_t stream) {
+  PrefillParams p = p_in;
   cudaError_t e = cudaMemsetAsync(p.token_mass, 0, sizeof(float) * (size_t)p.tk, stream);
   if (e != cudaSuccess) return e;
-  const dim3 grid((unsigned)((p.tk + 63) / 64), (unsigned)p.kv_heads, (unsigned)p.batch);
-  if (p.head_dim == 128) colsum_kernel<128><<<grid, 128, 0, stream>>>(p);
-  else if (p.head_dim == 64) colsum_kernel<64><<<grid, 128, 0, stream>>>(p);
+  const int nqt = (p.tq + kTileRows - 1) / kTileRows;
+  const int nkt = (p.tk + kTileRows - 1) / kTileRows;
+  p.part_items = kColsPartItems;
+  p.parts = (p.groups * nqt + p.part_items - 1) / p.part_items;
+  const long long grid = (long long)nkt * p.parts * p.batch * p.kv_heads;
+  if (p.head_dim == 128) e = launch_umma<128, true>(p, maps, grid, stream);
+  else if (p.head_dim == 64) e = launch_umma<64, true>(p, maps, grid, stream);
   else return cudaErrorInvalidValue;
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int nb = (p.tk + p.block_size - 1) / p.block_size;
   const float inv = 1.f / ((float)p.batch * (float)p.num_heads * (float)p.tq);

@@ -1,7 +1,7 @@
 // tkv_ptx.cuh -- thin inline-PTX wrappers for sm_100a used by the tiered
-// decode kernels: mbarriers with bounded waits, TMA tile loads and 1-D bulk
-// copies (never with cluster multicast), ldmatrix / movmatrix / mma.sync and
-// the MUFU exp2 / log2.
+// kernels: mbarriers with bounded waits, TMA tile loads and 1-D bulk copies
+// (never with cluster multicast), ldmatrix / movmatrix / mma.sync, tcgen05
+// (TMEM allocation, MMA, commit, TMEM loads) and the MUFU exp2 / log2.
 #pragma once
 
 #include <cuda.h>
@@ -103,6 +103,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, int32_t z, int32_t w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
   asm volatile(
@@ -198,6 +207,88 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
 template <int M>
 __device__ __forceinline__ uint32_t swz(uint32_t off) {
   return off ^ (((off >> 7) & M) << 4);
+}
+
+// ---- tcgen05: tensor memory and the 5th-generation tensor cores ------------------
+// Tensor memory (TMEM) is 128 lanes x 512 columns of 32-bit cells per SM; an
+// address holds the lane in bits [16, 32) and the column in [0, 16).  Warp w
+// of a CTA may read lanes [32 (w % 4), 32 (w % 4) + 32) only.
+
+// Allocates `cols` columns (a power of two >= 32) for the CTA; executed by one
+// whole warp, which must also free them.  The base address lands in *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand stored the way a TMA
+// SWIZZLE_128B box lands: rows of 128 bytes (64 fp16 of K), 16-byte chunks
+// XOR-ed with the row index mod 8, groups of 8 rows 1024 bytes apart (the
+// stride byte offset).  The leading byte offset is unused for this layout
+// (encoded as 1); bits 46-48 carry the descriptor version 1; bits 61-63 the
+// layout type 2 (128-byte swizzle).  K steps of 16 elements inside the
+// 128-byte row advance the start address by 32 bytes.
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of kind::f16 with fp16 A and B (both K-major) and an
+// fp32 accumulator: bits 4-5 accumulator format (1 = f32), 7-9 / 10-12 the A /
+// B formats (0 = f16), 15 / 16 the majors (0 = K), 17-22 N / 8, 24-28 M / 16.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T; issued by a single thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The mbarrier receives one arrival once every tcgen05 operation this thread
+// issued before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 consecutive columns of this thread's TMEM lane (32x32b shape, x32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 }  // namespace tkv

@@ -293,6 +293,14 @@ def read_device_errors(device=None, stream=None) -> int:
     return int(bits.value)
 
 
+def read_prefill_errors(stream=None) -> int:
+    """Read and clear the error bits the prefill kernels of the current device recorded."""
+    st = _stream(stream)
+    bits = ctypes.c_uint32()
+    N.check(N.load().tkv_prefill_read_errors(ctypes.byref(bits), st), "tkv_prefill_read_errors")
+    return int(bits.value)
+
+
 def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor, *, out_dtype=torch.float16,
                    return_lse: bool = False, out: torch.Tensor | None = None, stream=None):
     """LSE merge: part_o [P, R, D] fp32, part_lse [P, R] fp32 -> out [R, D] (+ lse [R]).

@@ -54,12 +54,15 @@ def test_gpu_scores_match_reference_and_oracle(name):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("b,hq,hkv,tq,tk,d,bs", [
-    (1, 32, 8, 300, 300, 128, 16),   # ragged tiles, group 4
-    (2, 8, 1, 129, 129, 64, 32),     # group 8
-    (1, 16, 16, 70, 200, 128, 16),   # a query block after a 130-token prefix
+@pytest.mark.parametrize("b,hq,hkv,tq,tk,d,bs,causal", [
+    (1, 32, 8, 300, 300, 128, 16, True),    # ragged tiles, group 4
+    (2, 8, 1, 129, 129, 64, 32, True),      # group 8
+    (1, 16, 16, 70, 200, 128, 16, True),    # a query block after a 130-token prefix
+    (1, 16, 2, 640, 640, 64, 16, True),     # 40 items per key tile: two column-pass parts
+    (1, 8, 2, 700, 700, 128, 16, True),     # more key tiles than pipeline stages
+    (2, 4, 2, 90, 333, 128, 32, False),     # bidirectional, ragged
 ])
-def test_gpu_scores_at_larger_sizes(b, hq, hkv, tq, tk, d, bs):
+def test_gpu_scores_at_larger_sizes(b, hq, hkv, tq, tk, d, bs, causal):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     from paged_tierkv_b200 import ops
@@ -68,15 +71,22 @@ def test_gpu_scores_at_larger_sizes(b, hq, hkv, tq, tk, d, bs):
     k = rng.standard_normal((b, hkv, tk, d)).astype(np.float16)
     scaling = d ** -0.5
     qd, kd = torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda()
-    scores, mass = ops.prefill_block_scores(qd, kd, scaling, bs, return_token_mass=True)
-    np.testing.assert_allclose(scores.cpu().numpy(), orc.prefill_block_scores(q, k, scaling, bs),
+    ops.read_prefill_errors()  # clear
+    lse_gpu = ops.prefill_lse(qd, kd, scaling, causal=causal)
+    lse_ref = orc.prefill_lse(q, k, scaling, causal=causal)
+    np.testing.assert_allclose(lse_gpu.cpu().numpy(), lse_ref, rtol=1e-5, atol=2e-4)
+    scores, mass = ops.prefill_block_scores(qd, kd, scaling, bs, causal=causal,
+                                            return_token_mass=True)
+    np.testing.assert_allclose(scores.cpu().numpy(),
+                               orc.prefill_block_scores(q, k, scaling, bs, causal=causal),
                                rtol=1e-3, atol=1e-7)
     # every query row's mass sums to one
     np.testing.assert_allclose(mass.sum().item(), b * hq * tq, rtol=1e-4)
     # an LSE supplied by the caller (here the oracle's) gives the same scores
-    lse = torch.from_numpy(orc.prefill_lse(q, k, scaling).astype(np.float32)).cuda()
-    again = ops.prefill_block_scores(qd, kd, scaling, bs, lse=lse)
+    lse = torch.from_numpy(lse_ref.astype(np.float32)).cuda()
+    again = ops.prefill_block_scores(qd, kd, scaling, bs, lse=lse, causal=causal)
     np.testing.assert_allclose(again.cpu().numpy(), scores.cpu().numpy(), rtol=1e-4, atol=1e-8)
+    assert ops.read_prefill_errors() == 0
 
 
 @pytest.mark.gpu
