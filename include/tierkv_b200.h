@@ -283,8 +283,8 @@ int32_t tkv_decode_attention_exchange(const tkv_pools* pools, const tkv_decode_a
 /* ---- prefill block scores ------------------------------------------------
  * q [batch, num_heads, tq, head_dim] and k [batch, kv_heads, tk, head_dim]
  * fp16, contiguous, 16-byte aligned; head_dim 64 or 128; num_heads a
- * multiple of kv_heads.  causal: key j is visible to query i iff
- * j <= i + (tk - tq) (requires tk >= tq).
+ * multiple of kv_heads; scaling finite and > 0.  causal: key j is visible
+ * to query i iff j <= i + (tk - tq) (requires tk >= tq).
  * tkv_prefill_lse writes lse [batch, num_heads, tq] fp32, the natural-log
  * LSE of the scaled, masked logits (what flash attention returns).
  * tkv_prefill_block_scores writes token_mass [tk] (the softmax mass each key

@@ -655,6 +655,7 @@ static int32_t prefill_params(const void* q, const void* k, int32_t batch, int32
   if (batch < 1 || num_heads < 1 || kv_heads < 1 || num_heads % kv_heads != 0 || tq < 1 || tk < 1)
     return TKV_ERR_INVALID;
   if (causal && tk < tq) return TKV_ERR_INVALID;
+  if (!(scaling > 0.f) || !std::isfinite(scaling)) return TKV_ERR_INVALID;
   std::memset(p, 0, sizeof(*p));
   p->q = q;
   p->k = k;

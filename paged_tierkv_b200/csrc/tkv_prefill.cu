@@ -17,15 +17,17 @@
 //
 // Both passes are one warp-specialised tcgen05 kernel.  A CTA keeps 128 rows
 // resident in shared memory as the MMA's A operand (M = 128): query rows for
-// the LSE pass, key rows for the column pass.  Warp 4 streams 128-row tiles of
+// the LSE pass, key rows for the column pass.  Warp 8 streams 128-row tiles of
 // the other operand (key tiles, or the (head, query tile) pairs that can see
-// the keys) through a ring of shared-memory stages by TMA; one thread of warp 5
+// the keys) through a ring of shared-memory stages by TMA; one thread of warp 9
 // issues tcgen05.mma (fp16 in, fp32 accumulate, N = 128) into one of two
-// 128-column TMEM accumulators; warps 0-3 read the accumulator with tcgen05.ld,
-// one thread per TMEM lane, i.e. per resident row, so the softmax statistics
-// need no cross-thread reduction.  Exponentials run in the log2 domain on the
-// MUFU unit, which bounds the kernel (one exp per logit; the MMA needs half the
-// time the 128 x 128 exps of a tile take).
+// 128-column TMEM accumulators; warps 0-7 read the accumulator with tcgen05.ld,
+// one thread per TMEM lane (resident row) and column half, so the softmax
+// statistics need no cross-thread reduction until the two halves of a row
+// merge at the end.  Exponentials run in the log2 domain on the MUFU unit
+// (a share of the LSE pass's on the FMA pipe), which bounds the kernel: one
+// exp per logit, while the MMA of a tile takes half the time its 128 x 128
+// exps do.
 //
 // Every mbarrier wait is bounded (TKV_DEVERR_TIMEOUT in the prefill error
 // word); in-flight copies and MMAs are waited for before the CTA frees its
@@ -44,7 +46,14 @@ __device__ uint32_t g_tkv_prefill_err;
 
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr int kTileRows = 128;       // M of every MMA and the rows (N) of every streamed tile
-constexpr int kUmmaThreads = 192;    // warps 0-3 epilogue (TMEM lane quarters), 4 TMA, 5 MMA
+// Warps 0-7 read the accumulators: warp w reads TMEM lanes 32 (w % 4) .. (its
+// lane quarter) in columns 64 (w / 4) .. (its warpgroup's half); warp 8 is
+// the TMA producer, warp 9 the MMA issuer.
+constexpr int kEpiThreads = 256;
+constexpr int kProdWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kUmmaThreads = kEpiThreads + 64;
+constexpr int kHalfCols = kTileRows / 2;
 constexpr uint32_t kTmemCols = 256;  // two fp32 accumulators of 128 columns
 constexpr uint32_t kIdesc = umma_idesc_f16_f32(128, 128);
 
@@ -56,7 +65,8 @@ struct PfLayout {
   // full[S], empty[S], resident, tfull[2], tempty[2], done
   static constexpr int kNumBars = 2 * kStages + 6;
   static constexpr int kLseOff = kBarOff + kNumBars * 8;
-  static constexpr int kTaddrOff = kLseOff + 2 * kTileRows * 4;
+  // column pass: per epilogue warp a ring of 2 x 64 LSEs; LSE pass: [128][2] merge
+  static constexpr int kTaddrOff = kLseOff + (kEpiThreads / 32) * 2 * kHalfCols * 4;
   static constexpr int kBytes = kTaddrOff + 16 + 1024;  // + slack to align the base to 1024
 };
 
@@ -143,6 +153,76 @@ __device__ __forceinline__ void tmem_wait_ld_into(uint32_t (&v)[32]) {
                : "memory");
 }
 
+// Logits per 32 whose exp2 runs on the FMA pipe (ex2_fma) instead of MUFU.
+// MUFU retires 16 exp2 per SM clock; in the LSE pass it is the busiest pipe
+// while the FMA and ALU pipes idle, so a share of its exps moves over.  The
+// column pass gains nothing from it (it does not saturate MUFU) and keeps all
+// its exps on MUFU.
+constexpr int kLseFmaExps = 4;
+constexpr int kColsFmaExps = 0;
+
+// Logit j of a 32-chunk takes the FMA-pipe exp2 when kFma of 32 do (every
+// (32 / kFma)-th logit).
+template <int kFma>
+__device__ __forceinline__ float ex2_mix(float x, int j) {
+  static_assert(kFma == 0 || (32 % kFma == 0 && kFma <= 16), "exps per 32");
+  if (kFma > 0 && j % (32 / (kFma > 0 ? kFma : 1)) == 32 / (kFma > 0 ? kFma : 1) - 1)
+    return ex2_fma(x);
+  return ex2(x);
+}
+
+// Column pass, 32 logits of one key row: sum += exp2(s c - LSE2_j); with kMask
+// only the columns j with j + rel >= 0 (those whose query sees the key).
+template <bool kMask>
+__device__ __forceinline__ void cols_chunk(const uint32_t (&v)[32], const float* l, float c,
+                                           int rel, float (&sum)[4]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 l4 = *reinterpret_cast<const float4*>(l + j);
+    float x0 = fmaf(__uint_as_float(v[j]), c, -l4.x);
+    float x1 = fmaf(__uint_as_float(v[j + 1]), c, -l4.y);
+    float x2 = fmaf(__uint_as_float(v[j + 2]), c, -l4.z);
+    float x3 = fmaf(__uint_as_float(v[j + 3]), c, -l4.w);
+    if (kMask) {
+      x0 = j + rel >= 0 ? x0 : -INFINITY;
+      x1 = j + 1 + rel >= 0 ? x1 : -INFINITY;
+      x2 = j + 2 + rel >= 0 ? x2 : -INFINITY;
+      x3 = j + 3 + rel >= 0 ? x3 : -INFINITY;
+    }
+    sum[0] += ex2_mix<kColsFmaExps>(x0, j);
+    sum[1] += ex2_mix<kColsFmaExps>(x1, j + 1);
+    sum[2] += ex2_mix<kColsFmaExps>(x2, j + 2);
+    sum[3] += ex2_mix<kColsFmaExps>(x3, j + 3);
+  }
+}
+
+// LSE pass, 32 logits of one query row, online in the log2 domain: m is the
+// running max of s c, l the sum of exp2(s c - m).  With kMask only columns
+// j < jmax count.  The max is taken on the raw logits (c > 0), so each logit
+// costs one FFMA ahead of its exp2.
+template <bool kMask>
+__device__ __forceinline__ void lse_chunk(uint32_t (&v)[32], float c, int jmax, float& m,
+                                          float& l) {
+  float cm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (kMask && j >= jmax) v[j] = __float_as_uint(-INFINITY);
+    cm = fmaxf(cm, __uint_as_float(v[j]));
+  }
+  const float mn = fmaxf(m, cm * c);
+  if (mn == -INFINITY) return;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    s0 += ex2_mix<kLseFmaExps>(fmaf(__uint_as_float(v[j]), c, -mn), j);
+    s1 += ex2_mix<kLseFmaExps>(fmaf(__uint_as_float(v[j + 1]), c, -mn), j + 1);
+    s2 += ex2_mix<kLseFmaExps>(fmaf(__uint_as_float(v[j + 2]), c, -mn), j + 2);
+    s3 += ex2_mix<kLseFmaExps>(fmaf(__uint_as_float(v[j + 3]), c, -mn), j + 3);
+  }
+  l = l * ex2(m - mn) + ((s0 + s1) + (s2 + s3));
+  m = mn;
+}
+
 template <int D, bool kCols>
 __global__ void __launch_bounds__(kUmmaThreads, 2)
     umma_pass_kernel(const __grid_constant__ PrefillParams p,
@@ -175,18 +255,18 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     mbar_init(res_full, 1);
     mbar_init(tfull, 1);
     mbar_init(tfull + 1, 1);
-    mbar_init(tempty, 4 * 32);
-    mbar_init(tempty + 1, 4 * 32);
+    mbar_init(tempty, kEpiThreads);
+    mbar_init(tempty + 1, kEpiThreads);
     mbar_init(done, 1);
     fence_mbar_init();
   }
-  if (warp == 4) tmem_alloc(taddr_s, kTmemCols);
+  if (warp == kProdWarp) tmem_alloc(taddr_s, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *taddr_s;
 
-  if (warp == 4) {
+  if (warp == kProdWarp) {
     // ---- TMA producer
     if (lane == 0) {
       const CUtensorMap* rmap = kCols ? &tm_k : &tm_q;
@@ -222,7 +302,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       if (!ok) atomicOr(p.err, TKV_DEVERR_TIMEOUT);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---- MMA issuer: S^T tile (kCols) or S tile = resident (A) x streamed (B)^T
     if (lane == 0) {
       bool ok = mbar_wait(res_full, 0);
@@ -253,72 +333,64 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     }
     __syncwarp();
   } else {
-    // ---- epilogue: thread t owns TMEM lane t = resident row t
+    // ---- epilogue: thread t owns resident row t % 128 (its TMEM lane) in
+    // the accumulator columns [cb, cb + 64) of its warpgroup
     const int t = threadIdx.x;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    const int row = t & (kTileRows - 1);
+    const int cb = (t >> 7) * kHalfCols;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const float c = p.scaling * kLog2eP;
     bool ok = true;
     if (kCols) {
-      const int key = w.k0 + t;
-      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+      const int key = w.k0 + row;
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
       int h, q0;
       cols_item(p, w, 0, h, q0);
-      float lnext = lse2_of(p, w.b, h, q0 + t);  // thread t stages column t's LSE
+      // each warp stages the LSEs of its 64 query columns in its own ring (lane
+      // l: columns l and l + 32 of the half), prefetched one item ahead, so no
+      // barrier spans more than the warp
+      float* ring = lse_s + warp * 2 * kHalfCols;
+      float ln0 = lse2_of(p, w.b, h, q0 + cb + lane);
+      float ln1 = lse2_of(p, w.b, h, q0 + cb + 32 + lane);
       for (int i = 0; i < w.n; ++i) {
-        float* ls = lse_s + (i & 1) * kTileRows;
-        ls[t] = lnext;
+        float* ls = ring + (i & 1) * kHalfCols;
+        ls[lane] = ln0;
+        ls[32 + lane] = ln1;
         cols_item(p, w, i, h, q0);
         if (i + 1 < w.n) {
           int h1, q1;
           cols_item(p, w, i + 1, h1, q1);
-          lnext = lse2_of(p, w.b, h1, q1 + t);
+          ln0 = lse2_of(p, w.b, h1, q1 + cb + lane);
+          ln1 = lse2_of(p, w.b, h1, q1 + cb + 32 + lane);
         }
-        named_barrier(1, 4 * 32);
+        __syncwarp();
         const int acc = i & 1;
-        // after a timeout the loop keeps its shape (no waits), so every thread
-        // meets the same named barriers and whole warps run tcgen05.ld
+        // after a timeout the loop keeps its shape (no waits), so whole warps
+        // run tcgen05.ld and every thread meets the final barriers
         if (ok && !mbar_wait(tfull + acc, (i >> 1) & 1)) ok = false;
         __syncwarp();
         tc_fence_after();
-        // causal: query column j sees this row's key iff j >= jmin
+        // causal: query column j sees this row's key iff j >= key - q_offset - q0
         const bool diag = p.causal && q0 + p.q_offset < w.k0 + kTileRows - 1;
-        const int jmin = key - p.q_offset - q0;
-#pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
           uint32_t v[32];
-          tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + 32 * c4), v);
+          const int col0 = cb + 32 * c2;
+          tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + col0), v);
           tmem_wait_ld_into(v);
-          if (c4 == 3) {
+          if (c2 == 1) {
             tc_fence_before();
             mbar_arrive(tempty + acc);
           }
-          const float* l = ls + 32 * c4;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(l + j);
-            float x0 = fmaf(__uint_as_float(v[j]), c, -l4.x);
-            float x1 = fmaf(__uint_as_float(v[j + 1]), c, -l4.y);
-            float x2 = fmaf(__uint_as_float(v[j + 2]), c, -l4.z);
-            float x3 = fmaf(__uint_as_float(v[j + 3]), c, -l4.w);
-            if (diag) {
-              const int col = 32 * c4 + j;
-              x0 = col >= jmin ? x0 : -INFINITY;
-              x1 = col + 1 >= jmin ? x1 : -INFINITY;
-              x2 = col + 2 >= jmin ? x2 : -INFINITY;
-              x3 = col + 3 >= jmin ? x3 : -INFINITY;
-            }
-            sum0 += ex2(x0);
-            sum1 += ex2(x1);
-            sum2 += ex2(x2);
-            sum3 += ex2(x3);
-          }
+          if (diag) cols_chunk<true>(v, ls + 32 * c2, c, col0 - (key - p.q_offset - q0), sum);
+          else cols_chunk<false>(v, ls + 32 * c2, c, 0, sum);
         }
       }
-      if (ok && key < p.tk) atomicAdd(p.token_mass + key, (sum0 + sum1) + (sum2 + sum3));
+      if (ok && key < p.tk) atomicAdd(p.token_mass + key, (sum[0] + sum[1]) + (sum[2] + sum[3]));
     } else {
-      const int q = w.q0 + t;
+      const int q = w.q0 + row;
       const int qpos = q + p.q_offset;
-      float m = -INFINITY, l = 0.f;
+      float m = -INFINITY, l = 0.f;  // running max (scaled, log2 domain) and sum of this half
       for (int i = 0; i < w.n; ++i) {
         const int acc = i & 1;
         if (ok && !mbar_wait(tfull + acc, (i >> 1) & 1)) ok = false;
@@ -329,41 +401,33 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
         const bool edge =
             k0 + kTileRows > p.tk || (p.causal && k0 + kTileRows - 1 > w.q0 + p.q_offset);
         const int jmax = (p.causal ? min(p.tk, qpos + 1) : p.tk) - k0;  // columns j < jmax count
-#pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
           uint32_t v[32];
-          tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + 32 * c4), v);
+          const int col0 = cb + 32 * c2;
+          tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + col0), v);
           tmem_wait_ld_into(v);
-          if (c4 == 3) {
+          if (c2 == 1) {
             tc_fence_before();
             mbar_arrive(tempty + acc);
           }
-          float x[32];
-          float cm = -INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            x[j] = __uint_as_float(v[j]) * c;
-            if (edge) x[j] = 32 * c4 + j < jmax ? x[j] : -INFINITY;
-            cm = fmaxf(cm, x[j]);
-          }
-          const float mn = fmaxf(m, cm);
-          if (mn != -INFINITY) {
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              s0 += ex2(x[j] - mn);
-              s1 += ex2(x[j + 1] - mn);
-              s2 += ex2(x[j + 2] - mn);
-              s3 += ex2(x[j + 3] - mn);
-            }
-            l = l * ex2(m - mn) + ((s0 + s1) + (s2 + s3));
-            m = mn;
-          }
+          if (edge) lse_chunk<true>(v, c, jmax - col0, m, l);
+          else lse_chunk<false>(v, c, 0, m, l);
         }
       }
-      if (ok && q < p.tq) {
+      // merge the two warpgroups' halves of each row
+      float* mrg = lse_s;  // [128][2]
+      if (cb != 0) {
+        mrg[2 * row] = m;
+        mrg[2 * row + 1] = l;
+      }
+      named_barrier(1, kEpiThreads);
+      if (cb == 0 && ok && q < p.tq) {
+        const float m1 = mrg[2 * row], l1 = mrg[2 * row + 1];
+        const float mm = fmaxf(m, m1);
+        const float ls = mm == -INFINITY ? 0.f : l * ex2(m - mm) + l1 * ex2(m1 - mm);
         const float kLn2 = 0.6931471805599453f;
-        p.lse[(size_t)w.res_head * p.tq + q] = l > 0.f ? (m + lg2(l)) * kLn2 : -INFINITY;
+        p.lse[(size_t)w.res_head * p.tq + q] = ls > 0.f ? (mm + lg2(ls)) * kLn2 : -INFINITY;
       }
     }
     if (!ok) atomicOr(p.err, TKV_DEVERR_TIMEOUT);
@@ -372,7 +436,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
   // every TMEM read and MMA of the CTA has completed: free the accumulators
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kProdWarp) {
     tc_fence_after();
     tmem_free(tmem, kTmemCols);
   }

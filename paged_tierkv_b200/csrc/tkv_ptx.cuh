@@ -185,6 +185,32 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// exp2 on the FMA and ALU pipes (Cody-Waite range reduction, as in
+// FlashAttention-4's software exponential): x = j + f with j = rint(x) taken
+// from the low mantissa bits of x + 1.5 * 2^23, 2^f for f in [-0.5, 0.5] from
+// a degree-4 polynomial, 2^j added to its exponent field.  The coefficients
+// are a least-squares fit of 2^f weighted toward minimax relative error
+// (Lawson iterations on 400 Chebyshev nodes); evaluated in float32 Horner form
+// the relative error stays below 3e-6.  x is clamped at -126, so x = -inf
+// gives 2^-126-scale values (below 1.2e-38) rather than 0, and the exponent
+// arithmetic never leaves the positive normal / subnormal encodings.
+constexpr float kExp2Poly0 = 0.9999992847442627f;
+constexpr float kExp2Poly1 = 0.6931217908859253f;
+constexpr float kExp2Poly2 = 0.240247443318367f;
+constexpr float kExp2Poly3 = 0.05591785907745361f;
+constexpr float kExp2Poly4 = 0.009570101276040077f;
+__device__ __forceinline__ float ex2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;  // 1.5 * 2^23: t's low mantissa bits hold rint(x)
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(kExp2Poly4, f, kExp2Poly3);
+  p = fmaf(p, f, kExp2Poly2);
+  p = fmaf(p, f, kExp2Poly1);
+  p = fmaf(p, f, kExp2Poly0);
+  // (bits(t) << 23) == rint(x) << 23: the 1.5 * 2^23 offset shifts out
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -99,5 +99,7 @@ def test_prefill_scores_reject_bad_inputs():
         ops.prefill_block_scores(q.float(), q, 0.125, 16)
     with pytest.raises(ValueError):
         ops.prefill_block_scores(q, torch.zeros((1, 3, 8, 64), dtype=torch.float16, device="cuda"), 0.125, 16)
+    with pytest.raises(ValueError):  # the scale must be positive
+        ops.prefill_block_scores(q, q, -0.125, 16)
     with pytest.raises(ValueError):  # causal with fewer keys than queries
         ops.prefill_block_scores(q, torch.zeros((1, 4, 4, 64), dtype=torch.float16, device="cuda"), 0.125, 16)
