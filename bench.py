@@ -794,6 +794,12 @@ def run_prefill(a, rank, device):
     except Exception:
         pass
     ach = 2 * flops_pass / (ms_full * 1e-3) / 1e12
+    # exp2 evaluations the two passes make: every logit of every 128 x 128
+    # (query tile, key tile) pair that the causal mask does not skip whole
+    nt = (t + 127) // 128
+    tiles = hq * nt * (nt + 1) // 2
+    exps = 2 * tiles * 128 * 128
+    exp_peak = 16 * 148 * 1.965e9  # MUFU: 16 exp2 per SM clock, 148 SMs, max SM clock
     line = {
         "metric": "prefill block-score ms (one 8192-token layer, 32 q / 8 kv heads, D 128, causal)",
         "value": round(ms_full, 3), "unit": "ms", "n_gpus": 1, "steps": steps, "warmup": a.warmup,
@@ -805,8 +811,15 @@ def run_prefill(a, rank, device):
         "max_rel_diff_vs_fp32_eager": rel,
         "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(ach / peak, 4) if peak else None,
-                     "note": "mma.m16n8k16 (legacy tensor path); two causal Q K^T passes"},
-        "gpu_launches": steps * 4,
+                     "note": "tcgen05 UMMA; two causal Q K^T passes; the binding unit is the "
+                             "exp2 unit (exp_roofline)"},
+        "exp_roofline": {"exps": exps, "achieved": round(exps / (ms_full * 1e-3) / 1e12, 3),
+                         "peak": round(exp_peak / 1e12, 3), "unit": "Texp2/s",
+                         "frac": round(exps / (ms_full * 1e-3) / exp_peak, 4),
+                         "note": "peak = 16 MUFU exp2 per SM clock x 148 SMs at the 1965 MHz "
+                                 "max clock (nominal); 1/8 of the LSE pass's exps run on the "
+                                 "FMA pipe instead"},
+        "gpu_launches": steps * 3,
     }
     print(json.dumps(line), flush=True)
 
