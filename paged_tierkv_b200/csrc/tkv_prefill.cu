@@ -165,9 +165,9 @@ constexpr int kColsFmaExps = 0;
 // (32 / kFma)-th logit).
 template <int kFma>
 __device__ __forceinline__ float ex2_mix(float x, int j) {
-  static_assert(kFma == 0 || (32 % kFma == 0 && kFma <= 16), "exps per 32");
-  if (kFma > 0 && j % (32 / (kFma > 0 ? kFma : 1)) == 32 / (kFma > 0 ? kFma : 1) - 1)
-    return ex2_fma(x);
+  constexpr int kStride = 32 / (kFma > 0 ? kFma : 1);
+  static_assert(kFma == 0 || (kFma <= 16 && kStride * kFma == 32), "exps per 32");
+  if (kFma > 0 && j % kStride == kStride - 1) return ex2_fma(x);
   return ex2(x);
 }
 
