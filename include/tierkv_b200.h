@@ -37,6 +37,10 @@
  *   tkv_append_hot_tokens  tierkv_policy.py:934-967 write_hot_tokens() tensor
  *                          work plus the block-table writes of _set_metadata
  *                          (917-926) and set_block_entry (1016-1035), fused
+ *   tkv_store_prefill_blocks  tierkv_policy.py:1722-1766
+ *                          append_prefill_with_policy(): the tensor work of its
+ *                          per-block write_hot_tokens (934-967) and
+ *                          write_warm_block (969-1002) calls, one launch
  *
  * Pool layout (the reference's, tierkv_policy.py:129-135 and 835-841):
  *   hot_k / hot_v     [hot_slots,  kv_heads, block_size, head_dim] fp16
@@ -234,6 +238,25 @@ typedef struct tkv_table_cell {
 int32_t tkv_append_hot_tokens(const tkv_pools* pools, int32_t hot_slot, int32_t start,
                               int32_t tokens, const void* key, const void* value,
                               const tkv_table_cell* cells, int32_t n_cells, void* stream);
+
+/* The data movement of a prefilled layer in one launch.  `blocks` is a
+ * device int32 array of `count` entries of 4: (state, slot, first token,
+ * length).  State 0 (HOT): rows [first, first + length) of key / value
+ * ([kv_heads, tokens, head_dim] fp16, contiguous, 16-byte aligned) go to rows
+ * [0, length) of HOT slot `slot` and its rows [length, block_size) are zeroed
+ * (write_hot_tokens, tierkv_policy.py:934-967).  State 1 (WARM, Format R):
+ * the same rows are quantized into WARM slot `slot` bit-exactly as
+ * quantize_fp16_to_int8 (21-36) with per-row fp16 scale and zero point, and
+ * rows [length, block_size) get code 0, scale 1, zero 0 (write_warm_block,
+ * 969-1002).  0 <= length <= block_size and first + length <= tokens; an
+ * entry with another state, a slot outside its pool or a token range outside
+ * the input is skipped.  No two entries may name the same slot of a pool.
+ * Pools absent from the call (no WARM entry) may have null pointers and 0
+ * slots.  Replaces the tensor work of tierkv_policy.py:1722-1766; the slot
+ * bookkeeping stays with the caller. */
+int32_t tkv_store_prefill_blocks(const tkv_pools* pools, const void* key, const void* value,
+                                 int32_t tokens, const int32_t* blocks, int32_t count,
+                                 void* stream);
 
 /* ---- context-sharded decode with a peer-memory exchange -------------------
  * Each rank holds a contiguous block range of the same sequences; every rank

@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "tkv_prefill_lse",
     "tkv_prefill_block_scores",
     "tkv_prefill_read_errors",
+    "tkv_store_prefill_blocks",
 )
 
 TKV_EXCHANGE_MAX_RANKS = 8
@@ -178,6 +179,7 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
         "tkv_prefill_block_scores": ([vp, vp, vp, i32, i32, i32, i32, i32, i32, ctypes.c_float, i32,
                                       i32, vp, vp, vp], i32),
         "tkv_prefill_read_errors": ([ctypes.POINTER(ctypes.c_uint32), vp], i32),
+        "tkv_store_prefill_blocks": ([ctypes.POINTER(TkvPools), vp, vp, i32, vp, i32, vp], i32),
     }
     for name, (argtypes, restype) in sigs.items():
         fn = getattr(lib, name)

@@ -182,13 +182,34 @@ class LayerState:
 
 
 class BlockAllocator:
-    """allocate_block of the reference's BlockManager (csrc/block_manager.cpp:36-50):
-    LIFO over a free list initialised N-1, ..., 0."""
+    """The reference's BlockManager (csrc/block_manager.cpp:36-105): LIFO
+    allocation over a free list initialised N-1, ..., 0, and per sequence the
+    list of (physical block, state) its blocks were allocated with (HOT) and
+    later set to (update_block_state)."""
 
     def __init__(self, total_blocks: int | None = None, free=None):
         self.free = list(free) if free is not None else list(range(int(total_blocks) - 1, -1, -1))
+        self.tables: dict = {}  # seq_id -> [[physical, state], ...]
 
     def allocate_block(self, seq_id) -> int:
         if not self.free:
             raise RuntimeError("No free physical blocks available.")
-        return self.free.pop()
+        physical = self.free.pop()
+        self.tables.setdefault(seq_id, []).append([physical, 0])
+        return physical
+
+    def update_block_state(self, seq_id, logical_id: int, state: int) -> None:
+        blocks = self.tables.get(seq_id)
+        if blocks is None:
+            raise RuntimeError("Sequence not found for state update.")
+        if logical_id < 0 or logical_id >= len(blocks):
+            raise RuntimeError("Logical block ID out of range.")
+        if int(state) not in (0, 1, 2):
+            raise RuntimeError("Invalid block state.")
+        blocks[logical_id][1] = int(state)
+
+    def get_physical_indices(self, seq_id) -> list:
+        return [b[0] for b in self.tables.get(seq_id, [])]
+
+    def get_states(self, seq_id) -> list:
+        return [b[1] for b in self.tables.get(seq_id, [])]

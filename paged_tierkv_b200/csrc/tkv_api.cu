@@ -642,6 +642,51 @@ int32_t tkv_append_hot_tokens(const tkv_pools* pools, int32_t hot_slot, int32_t 
   return cuda_status(launch_append(p, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int32_t tkv_store_prefill_blocks(const tkv_pools* pools, const void* key, const void* value,
+                                 int32_t tokens, const int32_t* blocks, int32_t count,
+                                 void* stream) {
+  if (!pools || !key || !value || tokens < 0 || count < 0 || (count > 0 && !blocks))
+    return TKV_ERR_INVALID;
+  if (pools->format != TKV_FORMAT_R) return TKV_ERR_UNSUPPORTED;
+  if (pools->head_dim != 64 && pools->head_dim != 128) return TKV_ERR_UNSUPPORTED;
+  if (pools->kv_heads <= 0 || pools->block_size <= 0 || pools->hot_slots < 0 ||
+      pools->warm_slots < 0)
+    return TKV_ERR_INVALID;
+  if (pools->hot_slots > 0 && (!pools->hot_k || !pools->hot_v || !aligned(pools->hot_k, 16) ||
+                               !aligned(pools->hot_v, 16)))
+    return TKV_ERR_INVALID;
+  if (pools->warm_slots > 0 &&
+      (!pools->warm_k || !pools->warm_v || !pools->k_scale || !pools->k_zero || !pools->v_scale ||
+       !pools->v_zero || !aligned(pools->warm_k, 16) || !aligned(pools->warm_v, 16) ||
+       !aligned(pools->k_scale, 2) || !aligned(pools->k_zero, 2) || !aligned(pools->v_scale, 2) ||
+       !aligned(pools->v_zero, 2)))
+    return TKV_ERR_INVALID;
+  if (!aligned(key, 16) || !aligned(value, 16) || (count > 0 && !aligned(blocks, 4)))
+    return TKV_ERR_INVALID;
+  if (count == 0) return TKV_OK;
+  PrefillStoreParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.key = key;
+  p.value = value;
+  p.hot_k = pools->hot_k;
+  p.hot_v = pools->hot_v;
+  p.warm_k = pools->warm_k;
+  p.warm_v = pools->warm_v;
+  p.k_scale = pools->k_scale;
+  p.k_zero = pools->k_zero;
+  p.v_scale = pools->v_scale;
+  p.v_zero = pools->v_zero;
+  p.blocks = blocks;
+  p.hot_slots = pools->hot_slots;
+  p.warm_slots = pools->warm_slots;
+  p.count = count;
+  p.tokens = tokens;
+  p.kv_heads = pools->kv_heads;
+  p.block_size = pools->block_size;
+  p.head_dim = pools->head_dim;
+  return cuda_status(launch_store_prefill(p, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 static bool prefill_maps(const PrefillParams& p, CUtensorMap maps[2]) {
   return encode_head_rows_map(&maps[0], p.q, (int64_t)p.batch * p.num_heads, p.tq, p.head_dim) &&
          encode_head_rows_map(&maps[1], p.k, (int64_t)p.batch * p.kv_heads, p.tk, p.head_dim);

@@ -215,6 +215,29 @@ bool encode_head_rows_map(CUtensorMap* map, const void* base, int64_t heads, int
 
 cudaError_t launch_demote(const DemoteParams& p, int format, cudaStream_t stream);
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
+
+// tkv_store_prefill_blocks: entries (state, slot, first token, length).
+struct PrefillStoreParams {
+  const void* key;            // [kv_heads, tokens, head_dim] fp16
+  const void* value;
+  void* hot_k;
+  void* hot_v;
+  void* warm_k;
+  void* warm_v;
+  void* k_scale;
+  void* k_zero;
+  void* v_scale;
+  void* v_zero;
+  const int32_t* blocks;      // [count][4]
+  int64_t hot_slots;
+  int64_t warm_slots;
+  int32_t count;
+  int32_t tokens;
+  int32_t kv_heads;
+  int32_t block_size;
+  int32_t head_dim;
+};
+cudaError_t launch_store_prefill(const PrefillStoreParams& p, cudaStream_t stream);
 cudaError_t launch_promote(const DemoteParams& p, cudaStream_t stream);
 
 }  // namespace tkv

@@ -11,6 +11,7 @@
 // parallelism), and the per-element work is one multiply by the scale's
 // reciprocal plus exact fp16 steps.  Rows are independent; the grid strides
 // over rows.
+#include <algorithm>
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -461,6 +462,105 @@ __global__ void __launch_bounds__(128) append_kernel(const AppendParams p) {
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
   append_kernel<<<dim3((unsigned)p.kv_heads, 2), 128, 0, stream>>>(p);
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- prefill store
+// The launch's rows are r = (2 e + kind) * R + rr for entry e, tensor kind
+// (K = 0, V = 1) and rr = kv_head * block_size + t < R = kv_heads *
+// block_size.  Row t < length of an entry reads input row (kv_head, first +
+// t); HOT entries store it (rows past the length store zeros), WARM entries
+// quantize it (rows past the length get code 0, scale 1, zero 0).  Every lane
+// runs the row quantizer, whose lanes exchange values by shuffles, and stores
+// only for WARM rows.  rows < 2^31 per launch (the host splits), so the row
+// arithmetic is 32-bit.
+template <int D>
+__global__ void __launch_bounds__(256) store_prefill_kernel(const PrefillStoreParams p,
+                                                            uint32_t rows) {
+  constexpr int LPR = lanes_per_row<D>();
+  using L = RowLayout<D, LPR>;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LPR;
+  const uint32_t bs = (uint32_t)p.block_size;
+  const uint32_t R = (uint32_t)p.kv_heads * bs;
+  const uint32_t warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const uint32_t wstride = gridDim.x * (blockDim.x >> 5) * L::RPW;
+  for (uint32_t r0 = warp * L::RPW; r0 < rows; r0 += wstride) {
+    const uint32_t r = r0 + lane / LPR;
+    bool ok = r < rows;
+    int state = -1, kind = 0, len = 0, first = 0;
+    int64_t slot = 0;
+    uint32_t rr = 0;
+    if (ok) {
+      const uint32_t item = r / R;
+      rr = r - item * R;
+      const int32_t* e = p.blocks + 4 * (size_t)(item >> 1);
+      kind = (int)(item & 1u);
+      state = e[0];
+      slot = e[1];
+      first = e[2];
+      len = e[3];
+      ok = ((state == 0 && slot >= 0 && slot < p.hot_slots) ||
+            (state == 1 && slot >= 0 && slot < p.warm_slots)) &&
+           len >= 0 && len <= (int)bs && first >= 0 && first <= p.tokens - len;
+    }
+    const uint32_t head = rr / bs, t = rr - (rr / bs) * bs;
+    const bool valid = ok && (int)t < len;
+    uint4 raw[L::V];
+    const __half* src = reinterpret_cast<const __half*>(kind ? p.value : p.key) +
+                        ((int64_t)head * p.tokens + first + (int64_t)t) * D + sub * 8;
+#pragma unroll
+    for (int v = 0; v < L::V; ++v)
+      raw[v] = valid ? *reinterpret_cast<const uint4*>(src + v * LPR * 8) : make_uint4(0u, 0u, 0u, 0u);
+    const bool warm = ok && state == 1;
+    const int64_t out_row = (ok ? slot : 0) * R + rr;
+    uint8_t* wp = warm ? reinterpret_cast<uint8_t*>(kind ? p.warm_v : p.warm_k) + out_row * D : nullptr;
+    __half* sp = warm ? reinterpret_cast<__half*>(kind ? p.v_scale : p.k_scale) + out_row : nullptr;
+    __half* zp = warm ? reinterpret_cast<__half*>(kind ? p.v_zero : p.k_zero) + out_row : nullptr;
+    quantize_store<D, LPR>(raw, wp, sp, zp, warm && valid, sub);
+    if (warm && !valid) {
+#pragma unroll
+      for (int v = 0; v < L::V; ++v)
+        *reinterpret_cast<uint2*>(wp + (sub + LPR * v) * 8) = make_uint2(0u, 0u);
+      if (sub == 0) {
+        *sp = __float2half_rn(1.f);
+        *zp = __float2half_rn(0.f);
+      }
+    }
+    if (ok && state == 0) {
+      __half* hp = reinterpret_cast<__half*>(kind ? p.hot_v : p.hot_k) + out_row * D + sub * 8;
+#pragma unroll
+      for (int v = 0; v < L::V; ++v) *reinterpret_cast<uint4*>(hp + v * LPR * 8) = raw[v];
+    }
+  }
+}
+
+cudaError_t launch_store_prefill(const PrefillStoreParams& p_in, cudaStream_t stream) {
+  if (p_in.count <= 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t per_entry = 2 * (int64_t)p_in.kv_heads * p_in.block_size;
+  const int64_t max_entries = 0x7fffffffLL / per_entry;
+  const int threads = 256;
+  for (int64_t e0 = 0; e0 < p_in.count; e0 += max_entries) {
+    PrefillStoreParams p = p_in;
+    p.blocks = p_in.blocks + 4 * e0;
+    p.count = (int32_t)std::min<int64_t>(max_entries, p_in.count - e0);
+    const uint32_t rows = (uint32_t)(p.count * per_entry);
+    auto grid = [&](int lpr) {
+      const int64_t per_block = (int64_t)threads / lpr;
+      const int64_t b = ((int64_t)rows + per_block - 1) / per_block;
+      return (unsigned)(b < (int64_t)sms * 16 ? b : (int64_t)sms * 16);
+    };
+    switch (p.head_dim) {
+      case 64: store_prefill_kernel<64><<<grid(lanes_per_row<64>()), threads, 0, stream>>>(p, rows); break;
+      case 128: store_prefill_kernel<128><<<grid(lanes_per_row<128>()), threads, 0, stream>>>(p, rows); break;
+      default: return cudaErrorInvalidValue;
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace tkv

@@ -30,6 +30,13 @@ same way: ``plan_append`` replays the bookkeeping (block-manager allocation,
 slot allocation, dictionaries) and ``apply_append`` issues one fused launch
 per block touched -- the new rows, the zeroed tail rows and every block-table
 cell the reference writes one element at a time.
+
+So is the prefill (``append_prefill_with_policy``, tierkv_policy.py:1722-1766,
+whose per-block ``write_hot_tokens`` / ``write_warm_block`` /
+``register_cold_block`` calls each run their own torch kernels):
+``plan_prefill`` replays the loop's bookkeeping and ``apply_prefill`` stores
+every block of the layer -- HOT rows copied, WARM rows quantized, tails
+cleared -- in one launch and writes the table cells in one copy.
 """
 
 from __future__ import annotations
@@ -529,3 +536,206 @@ def append_to_layer(self, seq_id: int, key_states: torch.Tensor, value_states: t
     steps, allocated_new_block = plan_append(self, seq_id, key_states, value_states)
     apply_append(self.kv_pool, steps)
     return allocated_new_block
+
+
+# ---------------------------------------------------------------------------
+# prefill with policy
+# ---------------------------------------------------------------------------
+
+@dataclass
+class PrefillPlan:
+    """A prefilled layer: the bookkeeping's table cells (and promotions of
+    blocks a stale WARM state left behind), and per written block one entry
+    (state, slot, first token, length) in the reference's order."""
+
+    plan: SyncPlan
+    entries: list = field(default_factory=list)
+    key: torch.Tensor | None = None    # [kv_heads, tokens, head_dim] fp16, contiguous
+    value: torch.Tensor | None = None
+
+
+def _prefill_kv(pool, key_states: torch.Tensor, value_states: torch.Tensor):
+    """The checks of _coerce_kv (tierkv_policy.py:780-791) for the whole layer
+    (every block's chunk has the layer's shape but for its token count), the
+    fp16 conversion, and one contiguous copy at most."""
+    if key_states.shape != value_states.shape:
+        raise ValueError("Key and value tensors must have identical shape.")
+    if key_states.ndim != 4 or key_states.shape[0] != 1:
+        raise ValueError("KV tensors must have shape [1, kv_heads, tokens, head_dim].")
+    if key_states.dtype != torch.float16:
+        key_states = key_states.to(torch.float16)
+    if value_states.dtype != torch.float16:
+        value_states = value_states.to(torch.float16)
+    return key_states.contiguous(), value_states.contiguous()
+
+
+def _hot_block(pool, plan: SyncPlan, physical_idx: int, key, length: int) -> int:
+    """write_hot_tokens(physical_idx, 0, chunk) (tierkv_policy.py:934-967)
+    without its tensor work; returns the slot."""
+    physical_idx = pool._check_physical_idx(physical_idx)
+    pool._ensure_metadata(key)
+    current_state = pool.get_physical_state(physical_idx)
+    if current_state == COLD_STATE:
+        raise KeyError(f"Physical block {physical_idx} is COLD and cannot be promoted.")
+    if current_state == WARM_STATE:
+        _promote_to_hot(pool, plan, physical_idx)
+    slot_idx = pool.physical_slots.get(physical_idx)
+    if slot_idx is None or current_state is None:
+        slot_idx = pool._alloc_hot_slot()
+    pool.hot_storage.add(physical_idx)
+    pool.warm_storage.discard(physical_idx)
+    pool.cold_storage.discard(physical_idx)
+    _metadata(pool, plan, physical_idx, HOT_STATE, slot_idx, length)
+    return int(slot_idx)
+
+
+def _warm_block(pool, plan: SyncPlan, physical_idx: int, key, length: int) -> int:
+    """write_warm_block (tierkv_policy.py:969-1002) without its tensor work;
+    returns the slot."""
+    physical_idx = pool._check_physical_idx(physical_idx)
+    pool._ensure_metadata(key)
+    current_state = pool.get_physical_state(physical_idx)
+    if current_state == HOT_STATE:
+        pool._free_hot_slot(pool.physical_slots.get(physical_idx, -1))
+    elif current_state == WARM_STATE:
+        pool._free_warm_slot(pool.physical_slots.get(physical_idx, -1))
+    elif current_state == COLD_STATE:
+        raise KeyError(f"Physical block {physical_idx} is COLD and cannot be promoted.")
+    slot_idx = pool._alloc_warm_slot()
+    pool.hot_storage.discard(physical_idx)
+    pool.warm_storage.add(physical_idx)
+    pool.cold_storage.discard(physical_idx)
+    _metadata(pool, plan, physical_idx, WARM_STATE, slot_idx, length)
+    return int(slot_idx)
+
+
+def _cold_block(pool, plan: SyncPlan, physical_idx: int, length: int) -> None:
+    """register_cold_block (tierkv_policy.py:1004-1014)."""
+    physical_idx = pool._check_physical_idx(physical_idx)
+    state = pool.get_physical_state(physical_idx)
+    if state == HOT_STATE:
+        pool._free_hot_slot(pool.physical_slots.get(physical_idx, -1))
+    elif state == WARM_STATE:
+        pool._free_warm_slot(pool.physical_slots.get(physical_idx, -1))
+    pool.hot_storage.discard(physical_idx)
+    pool.warm_storage.discard(physical_idx)
+    pool.cold_storage.add(physical_idx)
+    _metadata(pool, plan, physical_idx, COLD_STATE, -1, int(length))
+
+
+def plan_prefill(self, seq_id: int, key_states: torch.Tensor, value_states: torch.Tensor,
+                 block_scores: torch.Tensor, out: PrefillPlan | None = None) -> PrefillPlan:
+    """The loop of append_prefill_with_policy (tierkv_policy.py:1722-1766) on a
+    runtime (``layer_states``, ``block_manager``, ``kv_pool``, ``block_size``,
+    ``max_blocks_per_layer``, ``_desired_prefill_states``): block-manager
+    allocation and state updates, slot allocation (growing the pool through
+    its own allocators), dictionaries, storage sets and table cells exactly as
+    the reference leaves them, with the tensor work recorded in ``out``
+    (filled in place, so a failure part-way leaves the part done)."""
+    if key_states.shape[-2] != value_states.shape[-2]:
+        raise ValueError("Key and value states must have the same sequence length.")
+    pool = self.kv_pool
+    layer_state = self.layer_states[seq_id]
+    if layer_state.num_blocks != 0 or layer_state.open_physical_idx is not None:
+        raise RuntimeError("append_prefill_with_policy expects an empty layer cache.")
+    block_size = int(self.block_size)
+    total_tokens = int(key_states.shape[-2])
+    num_blocks = -(-total_tokens // block_size)
+    if num_blocks > self.max_blocks_per_layer:
+        raise RuntimeError(f"Layer {seq_id} exceeded max_blocks_per_layer={self.max_blocks_per_layer}.")
+    desired_states = self._desired_prefill_states(num_blocks, block_scores)
+    out = out if out is not None else PrefillPlan(SyncPlan(int(seq_id)))
+    plan = out.plan
+    for logical_idx, desired_state in enumerate(desired_states):
+        physical_idx = self.block_manager.allocate_block(seq_id)
+        if desired_state != HOT_STATE:
+            self.block_manager.update_block_state(seq_id, logical_idx, desired_state)
+        start = logical_idx * block_size
+        length = min(start + block_size, total_tokens) - start
+        if desired_state in (HOT_STATE, WARM_STATE) or (desired_state == COLD_STATE
+                                                         and not pool.is_allocated()):
+            if out.key is None:  # the reference checks each chunk as it writes it
+                pool._check_physical_idx(physical_idx)
+                key, value = _prefill_kv(pool, key_states, value_states)
+                out.key, out.value = key[0], value[0]
+        if desired_state == HOT_STATE:
+            slot = _hot_block(pool, plan, physical_idx, out.key[None], length)
+            out.entries.append((HOT_STATE, slot, start, length))
+        elif desired_state == WARM_STATE:
+            slot = _warm_block(pool, plan, physical_idx, out.key[None], length)
+            out.entries.append((WARM_STATE, slot, start, length))
+        elif desired_state == COLD_STATE:
+            if not pool.is_allocated():
+                slot = _hot_block(pool, plan, physical_idx, out.key[None], length)
+                out.entries.append((HOT_STATE, slot, start, length))
+                _demote_to_cold(pool, plan, physical_idx)
+            else:
+                _cold_block(pool, plan, physical_idx, length)
+        else:
+            raise ValueError(f"Unsupported desired state: {desired_state}")
+        _set_block_entry(pool, plan, seq_id, logical_idx, physical_idx, desired_state)
+    layer_state.num_blocks = num_blocks
+    layer_state.open_physical_idx = None
+    layer_state.open_token_count = 0
+    return out
+
+
+def _pools_struct(pool):
+    """The pools as a tkv_pools struct; a pool not allocated yet is passed as
+    null with 0 slots."""
+    from . import _native as N
+    hk, wk = pool.hot_k_pool, pool.warm_k_pool
+    ref = hk if hk is not None else wk
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    return N.TkvPools(ptr(hk), ptr(pool.hot_v_pool), ptr(wk), ptr(pool.warm_v_pool),
+                      ptr(pool.k_scale), ptr(pool.k_zero), ptr(pool.v_scale), ptr(pool.v_zero),
+                      0 if hk is None else int(hk.shape[0]), 0 if wk is None else int(wk.shape[0]),
+                      int(ref.shape[1]), int(ref.shape[2]), int(ref.shape[3]), ops.FORMAT_R)
+
+
+def apply_prefill(pool, pplan: PrefillPlan, stream=None) -> int:
+    """The recorded promotions (if any), every block's rows in one launch of
+    the prefill store kernel, and the table cells in one host->device copy.
+    Returns the number of store entries."""
+    import ctypes
+    from . import _native as N
+    plan = pplan.plan
+    if plan.promotions:
+        w, h, n = zip(*plan.promotions)
+        ops.promote_blocks_to_hot(_pools(pool), list(w), list(h), list(n), stream=stream)
+    # a slot written twice keeps the last write (each write covers the whole
+    # slot: rows below its length and the cleared rest)
+    last = {}
+    for e in pplan.entries:
+        last[(e[0], e[1])] = e
+    entries = list(last.values())
+    if entries:
+        key, value = pplan.key, pplan.value
+        if not (key.is_cuda and pool.hot_k_pool is not None and pool.hot_k_pool.is_cuda):
+            raise ValueError("TierKV prefill storage requires CUDA tensors.")
+        host = torch.tensor(entries, dtype=torch.int32).pin_memory()
+        with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+            dev = host.to(key.device, non_blocking=True)
+        ps = _pools_struct(pool)
+        N.check(N.load().tkv_store_prefill_blocks(ctypes.byref(ps), key.data_ptr(), value.data_ptr(),
+                                                   int(key.shape[1]), dev.data_ptr(), len(entries),
+                                                   ops._stream(stream)),
+                "tkv_store_prefill_blocks")
+        pplan._keep = (host, dev)  # the entry list lives as long as the plan
+    _write_tables(pool, plan, stream)
+    return len(entries)
+
+
+def append_prefill_with_policy(self, seq_id: int, key_states: torch.Tensor,
+                               value_states: torch.Tensor, block_scores: torch.Tensor) -> None:
+    """Method-compatible replacement of TieredKVRuntime.append_prefill_with_policy
+    (tierkv_policy.py:1722-1766): ``TieredKVRuntime.append_prefill_with_policy =
+    paged_tierkv_b200.tiering.append_prefill_with_policy``.  If the reference
+    loop would fail part-way, the blocks before the failure are stored as the
+    reference stores them, then the error is raised."""
+    pplan = PrefillPlan(SyncPlan(int(seq_id)))
+    try:
+        plan_prefill(self, seq_id, key_states, value_states, block_scores, out=pplan)
+    finally:
+        if pplan.entries or pplan.plan.promotions or pplan.plan.states:
+            apply_prefill(self.kv_pool, pplan)

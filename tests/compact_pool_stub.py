@@ -48,3 +48,42 @@ def CompactPoolStub(fixture, device="cpu") -> CompactPool:
 
 def BlockManagerStub(free) -> BlockAllocator:
     return BlockAllocator(free=free)
+
+
+def desired_prefill_states(policy_mode, hot_budget, warm_budget, demoted_state, num_blocks,
+                           block_scores):
+    """TieredKVRuntime._desired_prefill_states (tierkv_policy.py:1695-1720): the
+    first and last blocks stay HOT, the best-scored others fill the HOT budget,
+    the next best the WARM budget (hot_warm_cold), the rest go to the demoted
+    tier; layers of at most two blocks, or policy hot_only, stay all HOT."""
+    num_blocks = int(num_blocks)
+    if policy_mode == "hot_only" or num_blocks <= 2:
+        return [0] * num_blocks
+    if block_scores.ndim != 1 or len(block_scores) != num_blocks:
+        raise ValueError("block_scores must be a 1D tensor matching prefill block count.")
+    reserved = {0, num_blocks - 1}
+    cands = sorted((i for i in range(num_blocks) if i not in reserved),
+                   key=lambda i: float(block_scores[i]), reverse=True)
+    extra = max(int(hot_budget) - len(reserved), 0)
+    hot = set(cands[:extra])
+    if policy_mode == "hot_warm_cold":
+        warm = set(cands[extra:extra + max(int(warm_budget), 0)])
+        return [0 if (i in reserved or i in hot) else (1 if i in warm else 2) for i in range(num_blocks)]
+    return [0 if (i in reserved or i in hot) else int(demoted_state) for i in range(num_blocks)]
+
+
+class PrefillRuntimeStub:
+    """The attributes and the policy method of TieredKVRuntime that
+    append_prefill_with_policy uses."""
+
+    def __init__(self, pool, block_manager, layer_states, block_size, max_blocks_per_layer):
+        self.kv_pool = pool
+        self.block_manager = block_manager
+        self.layer_states = layer_states
+        self.block_size = block_size
+        self.max_blocks_per_layer = max_blocks_per_layer
+        self.policy_mode, self.hot_budget, self.warm_budget, self.demoted_state = "hot_warm", 2, 0, 1
+
+    def _desired_prefill_states(self, num_blocks, block_scores):
+        return desired_prefill_states(self.policy_mode, self.hot_budget, self.warm_budget,
+                                      self.demoted_state, num_blocks, block_scores)

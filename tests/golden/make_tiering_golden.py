@@ -28,6 +28,13 @@ LIFO from a free list initialised N-1..0), its state, then a recorded
 sequence of multi-token and one-token appends on both layers (block
 boundaries, pool growth, an open block demoted to WARM and appended to again,
 which promotes it) with their inputs, return values and the state after.
+
+``prefill_policy.npz`` records ``TieredKVRuntime.append_prefill_with_policy``
+(tierkv_policy.py:1722-1766, called unbound on a stand-in runtime with the
+reference's own ``_desired_prefill_states``, 1695-1720): a pool with a
+prefilled layer, its state, then prefills of further layers under the three
+policy modes (partial last block, one- and two-block layers, WARM pool
+growth) with their inputs and scores, the desired states, and the state after.
 """
 
 from __future__ import annotations
@@ -230,6 +237,91 @@ def build_append(tp, torch, *, seed=404, kv_heads=2, head_dim=64, block_size=16,
     return out
 
 
+class _PrefillBlockManager(_BlockManager):
+    """csrc/block_manager.cpp:36-77: LIFO allocation, per-sequence (physical,
+    state) lists, update_block_state."""
+
+    def __init__(self, n):
+        super().__init__(n)
+        self.tables = {}
+
+    def allocate_block(self, seq_id):
+        p = super().allocate_block(seq_id)
+        self.tables.setdefault(seq_id, []).append([p, HOT])
+        return p
+
+    def update_block_state(self, seq_id, logical_id, state):
+        self.tables[seq_id][logical_id][1] = int(state)
+
+
+# (layer, tokens, policy_mode, hot_budget, warm_budget) of the recorded calls
+PREFILL_CALLS = [
+    (1, 150, "hot_warm_cold", 4, 3),   # 10 blocks, the last partial: HOT / WARM / COLD
+    (2, 37, "hot_warm", 2, 0),         # 3 blocks: the middle one demoted to WARM
+    (3, 20, "hot_warm_cold", 4, 3),    # 2 blocks: all HOT whatever the scores
+    (4, 64, "hot_warm_cold", 3, 0),    # 4 blocks: one extra HOT, one COLD
+    (5, 200, "hot_warm", 3, 0),        # 13 blocks: the WARM pool grows several times
+]
+
+
+def build_prefill(tp, torch, *, seed=505, kv_heads=2, head_dim=64, block_size=16, layers=6):
+    """append_prefill_with_policy (tierkv_policy.py:1722-1766) called unbound on a
+    stand-in runtime: state before, the recorded calls with their inputs and
+    the desired states they produced, state after."""
+    import types as _types
+    gen = torch.Generator().manual_seed(seed)
+    max_blocks = 16
+    pool = tp.CompactTieredKVTensorPool(num_layers=layers, block_size=block_size,
+                                        max_seq_len=block_size * max_blocks,
+                                        pool_blocks=layers * max_blocks, pool_chunk_blocks=2)
+    bm = _PrefillBlockManager(layers * max_blocks)
+    rt = _types.SimpleNamespace(layer_states={i: tp.LayerRuntimeState() for i in range(layers)},
+                                block_manager=bm, kv_pool=pool, block_size=block_size,
+                                max_blocks_per_layer=max_blocks, policy_mode="hot_warm",
+                                hot_budget=2, warm_budget=0, demoted_state=WARM)
+    rt._desired_prefill_states = _types.MethodType(tp.TieredKVRuntime._desired_prefill_states, rt)
+
+    def kv(tokens):
+        k = torch.randn((1, kv_heads, tokens, head_dim), generator=gen).to(torch.float16)
+        v = torch.randn((1, kv_heads, tokens, head_dim), generator=gen).to(torch.float16)
+        return k, v
+
+    # set-up: layer 0 prefilled with one WARM block, so both pools exist
+    k, v = kv(40)
+    tp.TieredKVRuntime.append_prefill_with_policy(rt, 0, k, v, torch.tensor([0.9, 0.1, 0.5]))
+    before_book, before = _state(pool)
+    before_layers = _layer_states(rt)
+    before_bm = {"free": list(bm.free), "tables": {str(k2): v2 for k2, v2 in bm.tables.items()}}
+    calls, inputs = [], {}
+    for i, (layer, tokens, mode, hot, warm) in enumerate(PREFILL_CALLS):
+        rt.policy_mode, rt.hot_budget, rt.warm_budget = mode, hot, warm
+        nb = -(-tokens // block_size)
+        scores = torch.rand(nb, generator=gen)
+        k, v = kv(tokens)
+        inputs[f"in_{i}_k"], inputs[f"in_{i}_v"] = k.numpy(), v.numpy()
+        inputs[f"in_{i}_scores"] = scores.numpy()
+        desired = rt._desired_prefill_states(nb, scores)
+        tp.TieredKVRuntime.append_prefill_with_policy(rt, layer, k, v, scores)
+        calls.append({"layer": layer, "tokens": tokens, "policy_mode": mode, "hot_budget": hot,
+                      "warm_budget": warm, "index": i, "desired": [int(x) for x in desired]})
+    after_book, after = _state(pool)
+    meta = {
+        "seed": seed, "kv_heads": kv_heads, "head_dim": head_dim, "block_size": block_size,
+        "num_layers": layers, "max_blocks_per_layer": max_blocks, "pool_blocks": int(pool.pool_blocks),
+        "max_hot_slots": int(pool.max_hot_slots), "max_warm_slots": int(pool.max_warm_slots),
+        "hot_chunk_slots": int(pool.hot_chunk_slots), "warm_chunk_slots": int(pool.warm_chunk_slots),
+        "before": before_book, "after": after_book, "before_layers": before_layers,
+        "after_layers": _layer_states(rt), "before_bm": before_bm,
+        "after_bm": {"free": list(bm.free), "tables": {str(k2): v2 for k2, v2 in bm.tables.items()}},
+        "calls": calls,
+    }
+    out = {"meta": np.array(json.dumps(meta))}
+    out.update({f"before_{k2}": v2 for k2, v2 in before.items()})
+    out.update({f"after_{k2}": v2 for k2, v2 in after.items()})
+    out.update(inputs)
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of a Paged_TierKV checkout (read-only)")
@@ -247,6 +339,10 @@ def main(argv=None) -> int:
     path = os.path.join(HERE, "append_decode.npz")
     np.savez_compressed(path, **out)
     print("append_decode", os.path.getsize(path), "bytes")
+    out = build_prefill(tp, torch)
+    path = os.path.join(HERE, "prefill_policy.npz")
+    np.savez_compressed(path, **out)
+    print("prefill_policy", os.path.getsize(path), "bytes")
     return 0
 
 
