@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--sweep", action="store_true",
                     help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
-    ap.add_argument("--config", choices=["c5", "c4", "demote", "tick", "append", "prefill"],
+    ap.add_argument("--config", choices=["c5", "c4", "demote", "tick", "append", "prefill",
+                                         "prefill_store"],
                     default="c5",
                     help="c5: data-parallel batches (default); c4: one 131k-token context "
                          "over 32 layers, sharded by block range across the GPUs; demote: "
@@ -739,6 +740,160 @@ def run_tiering(a, rank, world, dist_on, device):
     print(json.dumps(line), flush=True)
 
 
+def _torch_quantize_r(x):
+    """quantize_fp16_to_int8 (tierkv_policy.py:21-36) as the reference runs it:
+    one fp16 torch op per step."""
+    mn = x.amin(dim=-1, keepdim=True)
+    mx = x.amax(dim=-1, keepdim=True)
+    scale = (mx - mn) / 255.0
+    scale = torch.where(scale == 0, torch.ones_like(scale), scale)
+    zp = -torch.round(mn / scale)
+    q = torch.clamp(torch.round(x / scale) + zp, 0, 255).to(torch.uint8)
+    return q, scale, zp
+
+
+def run_prefill_store(a, rank, device):
+    """The storage half of a prefill with policy (append_prefill_with_policy,
+    tierkv_policy.py:1722-1766) for one layer of an 8192-token prompt (512
+    blocks of [16 x 128] x 8 kv heads; 25 % HOT, 50 % WARM, 25 % COLD by
+    seeded scores): ours (bookkeeping replay, one store launch, one table
+    copy) against the same bookkeeping followed by the reference's per-block
+    tensor work (row copies and tail fills for HOT blocks, the torch
+    quantizer's ops for WARM blocks, one element write per table cell)."""
+    import types
+    from paged_tierkv_b200 import _native, compact_pool, ops, tiering
+    _native.load(build_if_missing=True)
+    if rank != 0:
+        return
+    bs, hkv, d, tokens = 16, 8, 128, 8192
+    nb = tokens // bs
+    steps = max(3, min(a.steps, 20))
+    warm = max(2, a.warmup)
+    layers = 2 * (steps + warm) + 2
+    pool = compact_pool.CompactPool(num_layers=layers, block_size=bs, kv_heads=hkv, head_dim=d,
+                                    max_blocks_per_layer=nb, max_hot_slots=layers * nb,
+                                    max_warm_slots=layers * nb, hot_chunk_slots=layers * nb,
+                                    warm_chunk_slots=layers * nb, device=device)
+    rt = types.SimpleNamespace(layer_states={i: compact_pool.LayerState() for i in range(layers)},
+                               block_manager=compact_pool.BlockAllocator(layers * nb), kv_pool=pool,
+                               block_size=bs, max_blocks_per_layer=nb)
+    gen = torch.Generator(device=device).manual_seed(29)
+    k = torch.randn((1, hkv, tokens, d), generator=gen, device=device).to(torch.float16)
+    v = torch.randn((1, hkv, tokens, d), generator=gen, device=device).to(torch.float16)
+    scores = torch.rand(nb, generator=torch.Generator().manual_seed(29))
+    order = sorted(range(1, nb - 1), key=lambda i: float(scores[i]), reverse=True)
+    desired = [2] * nb
+    for i in [0, nb - 1] + order[:nb // 4 - 2]:
+        desired[i] = 0
+    for i in order[nb // 4 - 2:nb // 4 - 2 + nb // 2]:
+        desired[i] = 1
+    rt._desired_prefill_states = lambda n, sc: list(desired)
+    layer = [0]
+
+    def ours():
+        tiering.append_prefill_with_policy(rt, layer[0], k, v, scores)
+        layer[0] += 1
+
+    def per_block():
+        pp = tiering.plan_prefill(rt, layer[0], k, v, scores)
+        layer[0] += 1
+        key, val = pp.key, pp.value
+        for state, slot, first, n in pp.entries:
+            if state == 0:
+                for src, dst in ((key, pool.hot_k_pool), (val, pool.hot_v_pool)):
+                    dst[slot, :, :n, :].copy_(src[:, first:first + n, :])
+                    if n < bs:
+                        dst[slot, :, n:, :].zero_()
+            else:
+                for src, dst, sc, zp in ((key, pool.warm_k_pool, pool.k_scale, pool.k_zero),
+                                         (val, pool.warm_v_pool, pool.v_scale, pool.v_zero)):
+                    q, s_, z_ = _torch_quantize_r(src[:, first:first + n, :].contiguous())
+                    dst[slot, :, :n, :].copy_(q)
+                    sc[slot, :, :n, :].copy_(s_)
+                    zp[slot, :, :n, :].copy_(z_)
+        for table, cells in tiering._table_groups(pool, pp.plan):
+            for (lay, logical), val_ in cells.items():
+                table[lay, logical] = val_
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) * 1e3 / steps, e0.elapsed_time(e1) / steps
+
+    ms, dev_ms = timed(ours)
+    # the store kernel alone: the last layer's entries stored again (same bytes)
+    import ctypes
+    from paged_tierkv_b200 import _native as N
+    ents = torch.tensor(_last_entries(pool, layer[0] - 1, bs), dtype=torch.int32, device=device)
+    ps = tiering._pools_struct(pool)
+    kc, vc = k[0].contiguous(), v[0].contiguous()
+    lib = N.load()
+
+    def store():
+        N.check(lib.tkv_store_prefill_blocks(ctypes.byref(ps), kc.data_ptr(), vc.data_ptr(), tokens,
+                                              ents.data_ptr(), int(ents.shape[0]), ops._stream(None)),
+                "tkv_store_prefill_blocks")
+
+    for _ in range(5):
+        store()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(50):
+        store()
+    e1.record()
+    torch.cuda.synchronize()
+    kernel_ms = e0.elapsed_time(e1) / 50
+    ms_pb, dev_pb = timed(per_block)
+    n_hot = desired.count(0)
+    n_warm = desired.count(1)
+    hbm_peak = None
+    try:
+        with open(PEAKS) as f:
+            hbm_peak = float(json.load(f)["hbm_gbs"])
+    except Exception:
+        pass
+    alg = 2 * hkv * d * 2 * tokens * (n_hot + n_warm) / nb + n_hot * 2 * hkv * bs * d * 2 \
+        + n_warm * 2 * hkv * bs * (d + 4)
+    line = {
+        "metric": "prefill storage ms per layer (append_prefill_with_policy, 8192 tokens, "
+                  "8 kv heads x 128, block 16)",
+        "value": round(ms, 3), "unit": "ms", "n_gpus": 1, "steps": steps, "warmup": warm,
+        "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "none",
+        "dtype": "fp16 -> fp16 / u8", "data": "synthetic N(0,1)",
+        "config": {"workload": "prefill_store_8192", "blocks": nb, "hot": n_hot, "warm": n_warm,
+                   "cold": nb - n_hot - n_warm, "algorithmic_bytes": int(alg)},
+        "device_ms": round(dev_ms, 4),
+        "roofline": {"bound": "hbm", "achieved": round(alg / (kernel_ms * 1e-3) / 1e9, 1),
+                     "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(alg / (kernel_ms * 1e-3) / 1e9 / hbm_peak, 4) if hbm_peak else None,
+                     "kernel": "tkv::store_prefill_kernel<128>", "kernel_ms": round(kernel_ms, 4),
+                     "traffic": None},
+        "per_block": {"ms": round(ms_pb, 3), "device_ms": round(dev_pb, 3),
+                      "what": "same bookkeeping, then the reference's per-block tensor work "
+                              "(row copies, tail fills, torch quantizer ops, one element write "
+                              "per table cell)"},
+        "gpu_launches": steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _last_entries(pool, layer, bs):
+    """(state, slot, first token, length) of a stored layer's HOT / WARM blocks."""
+    st = pool.block_states[layer].tolist()
+    sl = pool.block_slot_indices[layer].tolist()
+    ln = pool.block_lengths[layer].tolist()
+    return [(s, q, i * bs, n) for i, (s, q, n) in enumerate(zip(st, sl, ln)) if s in (0, 1)]
+
+
 def run_prefill(a, rank, device):
     """Exact prefill block scores of one layer of configuration 3's prompt
     (8192 tokens, 32 q / 8 kv heads, head_dim 128, block 16, causal):
@@ -850,6 +1005,8 @@ def main():
             run_tiering(a, rank, world, dist_on, device)
         elif a.config == "prefill":
             run_prefill(a, rank, device)
+        elif a.config == "prefill_store":
+            run_prefill_store(a, rank, device)
         else:
             run_ours(a, rank, world, dist_on, device)
     finally:

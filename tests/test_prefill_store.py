@@ -169,5 +169,5 @@ def test_prefill_store_kernel_against_oracle(head_dim, block_size):
                 assert not warm[slot, :, n:].any()
                 assert (sc[slot, :, n:] == 1).all() and (zp[slot, :, n:] == 0).all()
     # untouched slots keep their stale bytes (the skipped entries wrote nothing)
-    assert (hk[1].view(np.uint16) == 0x0707).all()
+    assert (hk[1] == 7).all()
     assert (wk[2] == 7).all()
