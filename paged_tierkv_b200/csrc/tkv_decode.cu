@@ -663,6 +663,11 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   for (int i = 0; i < Cfg::kKS; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  // WARM V enters the tensor cores as exact fp16 (1024 + code), so acc also
+  // collects sum_t w_t (1024 + zero_t) per head (w = P * V scale as the MMA
+  // sees it, fp16); this lane's share of that sum, heads 2t, 2t+1, is
+  // subtracted once before the merge
+  float vcorr[2] = {0.f, 0.f};
 
   const int g = lane >> 2;
   const int t = lane & 3;
@@ -789,7 +794,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       // plus the per-token V scale and (1024 + zero)).
       uint32_t vf[Cfg::kSub][D / 64][16];
       float vsc[Cfg::kSub][2];
-      uint32_t vzp[Cfg::kSub][2];
+      float vzc[Cfg::kSub][2];  // 1024 + V zero point of tokens g, g + 8
       if (hot) {
 #pragma unroll
         for (int u = 0; u < Cfg::kSub; ++u) {
@@ -814,15 +819,11 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           if (FMT == kFmtR) {
             vsc[u][0] = __half2float(ms[2 * BS + 16 * u + g]);
             vsc[u][1] = __half2float(ms[2 * BS + 16 * u + g + 8]);
-            const __half o1024 = __float2half_rn(1024.f);
-            const __half* vz = ms + 3 * BS;
-            vzp[u][0] = (uint32_t)__half_as_ushort(__hadd(vz[r0], o1024)) |
-                        ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 1], o1024)) << 16);
-            vzp[u][1] = (uint32_t)__half_as_ushort(__hadd(vz[r0 + 8], o1024)) |
-                        ((uint32_t)__half_as_ushort(__hadd(vz[r0 + 9], o1024)) << 16);
+            vzc[u][0] = 1024.f + __half2float(ms[3 * BS + 16 * u + g]);
+            vzc[u][1] = 1024.f + __half2float(ms[3 * BS + 16 * u + g + 8]);
           } else {
             vsc[u][0] = vsc[u][1] = ti.vs;
-            vzp[u][0] = vzp[u][1] = 0x64806480u;
+            vzc[u][0] = vzc[u][1] = 1152.f;  // int8 codes are flipped to biased bytes
           }
 #pragma unroll
           for (int kk = 0; kk < D / 64; ++kk) {
@@ -870,6 +871,8 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
           acc[i][0] *= alpha[0]; acc[i][1] *= alpha[1];
           acc[i][2] *= alpha[0]; acc[i][3] *= alpha[1];
         }
+        vcorr[0] *= alpha[0];
+        vcorr[1] *= alpha[1];
       }
       float pr[Cfg::kSub][4];
       float ps[2] = {0.f, 0.f};
@@ -928,9 +931,16 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       } else {
 #pragma unroll
         for (int u = 0; u < Cfg::kSub; ++u) {
-          const uint32_t pb0 = movmatrix_t(pack_half2(pr[u][0] * vsc[u][0], pr[u][1] * vsc[u][0]));
-          const uint32_t pb1 = movmatrix_t(pack_half2(pr[u][2] * vsc[u][1], pr[u][3] * vsc[u][1]));
-          const uint32_t z01 = vzp[u][0], z23 = vzp[u][1];
+          const uint32_t w01 = pack_half2(pr[u][0] * vsc[u][0], pr[u][1] * vsc[u][0]);
+          const uint32_t w23 = pack_half2(pr[u][2] * vsc[u][1], pr[u][3] * vsc[u][1]);
+          const uint32_t pb0 = movmatrix_t(w01);
+          const uint32_t pb1 = movmatrix_t(w23);
+          {
+            const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&w01));
+            const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&w23));
+            vcorr[0] = fmaf(f01.x, vzc[u][0], fmaf(f23.x, vzc[u][1], vcorr[0]));
+            vcorr[1] = fmaf(f01.y, vzc[u][0], fmaf(f23.y, vzc[u][1], vcorr[1]));
+          }
 #pragma unroll
           for (int kk = 0; kk < D / 64; ++kk) {
             // token j: codes of dims 0..3 in word 2j, dims 4..7 in word 2j+1
@@ -949,10 +959,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint32_t sel = (i & 1) ? 0x4342u : 0x4140u;
-              const uint32_t a0 = hsub2_u32(__byte_perm(xl[i >> 1], kMagic, sel), z01);
-              const uint32_t a1 = hsub2_u32(__byte_perm(xh[i >> 1], kMagic, sel), z01);
-              const uint32_t a2 = hsub2_u32(__byte_perm(yl[i >> 1], kMagic, sel), z23);
-              const uint32_t a3 = hsub2_u32(__byte_perm(yh[i >> 1], kMagic, sel), z23);
+              const uint32_t a0 = __byte_perm(xl[i >> 1], kMagic, sel);
+              const uint32_t a1 = __byte_perm(xh[i >> 1], kMagic, sel);
+              const uint32_t a2 = __byte_perm(yl[i >> 1], kMagic, sel);
+              const uint32_t a3 = __byte_perm(yh[i >> 1], kMagic, sel);
               mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb0, pb1);
             }
           }
@@ -970,6 +980,13 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   for (int off = 4; off < 32; off <<= 1) {
     l[0] += __shfl_xor_sync(0xffffffffu, l[0], off);
     l[1] += __shfl_xor_sync(0xffffffffu, l[1], off);
+    vcorr[0] += __shfl_xor_sync(0xffffffffu, vcorr[0], off);
+    vcorr[1] += __shfl_xor_sync(0xffffffffu, vcorr[1], off);
+  }
+#pragma unroll
+  for (int i = 0; i < Cfg::kKS; ++i) {
+    acc[i][0] -= vcorr[0]; acc[i][1] -= vcorr[1];
+    acc[i][2] -= vcorr[0]; acc[i][3] -= vcorr[1];
   }
   __syncthreads();  // every stage is drained: the ring becomes merge scratch
   float* sm_m = reinterpret_cast<float*>(stages);
