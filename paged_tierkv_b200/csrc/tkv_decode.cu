@@ -232,6 +232,13 @@ __device__ __forceinline__ float* x_lse(const DecodeParams& p, int q, uint32_t e
 // wsl is shared scratch of kMaxGroups * (cnt + 2) floats.  One warp per
 // head: a lane owns 4 dims (a float4 of every part's row) and, for head_dim
 // 64, every other part; the loop keeps 8 independent 16-byte loads in flight.
+// Partial rows each lane loads per round of the split merge (the merge is
+// latency-bound: one round trip per round).
+#ifndef TKV_MERGE_DEPTH
+#define TKV_MERGE_DEPTH 16
+#endif
+constexpr int kMergeDepth = TKV_MERGE_DEPTH;
+
 template <int D, int NT>
 __device__ __forceinline__ void merge_parts(const float* po, const float* plse, int rstride,
                                             int j0, int cnt, size_t row0, int G, float* wsl,
@@ -277,12 +284,13 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
     const float4* src = reinterpret_cast<const float4*>(po + (row * rstride + j0) * D) + v;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     int sp = sp0;
-    for (; sp + 7 * kSplitLanes < cnt; sp += 8 * kSplitLanes) {
-      float4 x[8];
+    for (; sp + (kMergeDepth - 1) * kSplitLanes < cnt; sp += kMergeDepth * kSplitLanes) {
+      float4 x[kMergeDepth];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = __ldcg(src + (size_t)(sp + k * kSplitLanes) * kVecs);
+      for (int k = 0; k < kMergeDepth; ++k)
+        x[k] = __ldcg(src + (size_t)(sp + k * kSplitLanes) * kVecs);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < kMergeDepth; ++k) {
         const float w = wsl[h * cnt + sp + k * kSplitLanes];
         o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
       }
