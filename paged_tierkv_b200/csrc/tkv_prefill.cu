@@ -46,18 +46,31 @@ __device__ uint32_t g_tkv_prefill_err;
 
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr int kTileRows = 128;       // M of every MMA and the rows (N) of every streamed tile
-// Warps 0-7 read the accumulators: warp w reads TMEM lanes 32 (w % 4) .. (its
-// lane quarter) in columns 64 (w / 4) .. (its warpgroup's half); warp 8 is
-// the TMA producer, warp 9 the MMA issuer.
-constexpr int kEpiThreads = 256;
-constexpr int kProdWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kUmmaThreads = kEpiThreads + 64;
-constexpr int kHalfCols = kTileRows / 2;
+// The epilogue is WG warpgroups: warp w < 4 WG reads TMEM lanes 32 (w % 4) ..
+// (its lane quarter) in the accumulator columns [128 / WG * (w / 4), + 128 /
+// WG) of its warpgroup; warp 4 WG is the TMA producer, warp 4 WG + 1 the MMA
+// issuer.  Warpgroups per pass (build-time): more of them keep more exp2
+// streams in flight per SM, at fewer registers per thread.
+#ifndef TKV_PF_WG_LSE
+#define TKV_PF_WG_LSE 2
+#endif
+#ifndef TKV_PF_WG_COLS
+#define TKV_PF_WG_COLS 2
+#endif
+template <int WG>
+struct PfWarps {
+  static_assert(WG == 1 || WG == 2 || WG == 4, "warpgroups");
+  static constexpr int kEpiThreads = 128 * WG;
+  static constexpr int kProdWarp = 4 * WG;
+  static constexpr int kMmaWarp = 4 * WG + 1;
+  static constexpr int kThreads = kEpiThreads + 64;
+  static constexpr int kCols = kTileRows / WG;   // accumulator columns per warpgroup
+  static constexpr int kChunks = kCols / 32;     // 32-column TMEM loads per item
+};
 constexpr uint32_t kTmemCols = 256;  // two fp32 accumulators of 128 columns
 constexpr uint32_t kIdesc = umma_idesc_f16_f32(128, 128);
 
-template <int D>
+template <int D, int WG>
 struct PfLayout {
   static constexpr int kTile = kTileRows * D * 2;  // [D/64][128 rows][64] fp16, 128B-swizzled
   static constexpr int kStages = D == 128 ? 2 : 4;
@@ -65,8 +78,9 @@ struct PfLayout {
   // full[S], empty[S], resident, tfull[2], tempty[2], done
   static constexpr int kNumBars = 2 * kStages + 6;
   static constexpr int kLseOff = kBarOff + kNumBars * 8;
-  // column pass: per epilogue warp a ring of 2 x 64 LSEs; LSE pass: [128][2] merge
-  static constexpr int kTaddrOff = kLseOff + (kEpiThreads / 32) * 2 * kHalfCols * 4;
+  // column pass: per epilogue warp a ring of 2 x kCols LSEs (4 KB in all);
+  // LSE pass: the other warpgroups' (max, sum) per row, [WG - 1][128][2]
+  static constexpr int kTaddrOff = kLseOff + 4 * WG * 2 * PfWarps<WG>::kCols * 4;
   static constexpr int kBytes = kTaddrOff + 16 + 1024;  // + slack to align the base to 1024
 };
 
@@ -126,13 +140,21 @@ __device__ __forceinline__ PfWork cols_work(const PrefillParams& p) {
   return w;
 }
 
-// Column pass item i: query head and first query row.
-__device__ __forceinline__ void cols_item(const PrefillParams& p, const PfWork& w, int i, int& h,
-                                          int& q0) {
-  const int gi = w.i0 + i;
-  h = w.kvh * p.groups + gi / w.per_head;
-  q0 = (w.qt_first + gi % w.per_head) * kTileRows;
-}
+// Walks a column-pass CTA's items in order without a division per item:
+// (query head of the group, query tile), query tiles innermost.
+struct ItemIter {
+  int hh, qt;
+  __device__ __forceinline__ void start(const PfWork& w, int i) {
+    hh = (w.i0 + i) / w.per_head;
+    qt = w.qt_first + (w.i0 + i) % w.per_head;
+  }
+  __device__ __forceinline__ void next(const PfWork& w) {
+    if (++qt == w.qt_first + w.per_head) {
+      qt = w.qt_first;
+      ++hh;
+    }
+  }
+};
 
 // log2-domain LSE of query row q of head h (+inf for rows past the end, whose
 // exponentials then vanish).
@@ -223,13 +245,18 @@ __device__ __forceinline__ void lse_chunk(uint32_t (&v)[32], float c, int jmax, 
   m = mn;
 }
 
-template <int D, bool kCols>
-__global__ void __launch_bounds__(kUmmaThreads, 2)
+template <int D, bool kCols, int WG>
+__global__ void __launch_bounds__(PfWarps<WG>::kThreads, 2)
     umma_pass_kernel(const __grid_constant__ PrefillParams p,
                      const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k) {
-  using L = PfLayout<D>;
+  using L = PfLayout<D, WG>;
+  using Wp = PfWarps<WG>;
   constexpr int S = L::kStages;
+  constexpr int kEpiThreads = Wp::kEpiThreads;
+  constexpr int kProdWarp = Wp::kProdWarp;
+  constexpr int kMmaWarp = Wp::kMmaWarp;
+  constexpr int kWgCols = Wp::kCols;
   extern __shared__ uint8_t pf_raw[];
   const uint32_t raw = smem_u32(pf_raw);
   uint8_t* smem = pf_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -277,6 +304,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       tma_load_4d(smem, rmap, 0, w.res_row, 0, w.res_head, res_full);
       bool ok = true;
       int issued = 0;
+      ItemIter it;
+      if (kCols) it.start(w, 0);
       for (int i = 0; i < w.n; ++i) {
         const int s = i % S;
         if (i >= S && !mbar_wait(empty + s, ((i / S) - 1) & 1)) {
@@ -285,9 +314,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
         }
         int row, head;
         if (kCols) {
-          int h;
-          cols_item(p, w, i, h, row);
-          head = w.b * p.num_heads + h;
+          row = it.qt * kTileRows;
+          head = w.b * p.num_heads + w.kvh * p.groups + it.hh;
+          it.next(w);
         } else {
           row = i * kTileRows;
           head = w.b * p.kv_heads + w.kvh;
@@ -334,35 +363,42 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     __syncwarp();
   } else {
     // ---- epilogue: thread t owns resident row t % 128 (its TMEM lane) in
-    // the accumulator columns [cb, cb + 64) of its warpgroup
+    // the accumulator columns [cb, cb + kWgCols) of its warpgroup
     const int t = threadIdx.x;
     const int row = t & (kTileRows - 1);
-    const int cb = (t >> 7) * kHalfCols;
+    const int wg = t >> 7;
+    const int cb = wg * kWgCols;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const float c = p.scaling * kLog2eP;
     bool ok = true;
     if (kCols) {
       const int key = w.k0 + row;
       float sum[4] = {0.f, 0.f, 0.f, 0.f};
-      int h, q0;
-      cols_item(p, w, 0, h, q0);
-      // each warp stages the LSEs of its 64 query columns in its own ring (lane
-      // l: columns l and l + 32 of the half), prefetched one item ahead, so no
-      // barrier spans more than the warp
-      float* ring = lse_s + warp * 2 * kHalfCols;
-      float ln0 = lse2_of(p, w.b, h, q0 + cb + lane);
-      float ln1 = lse2_of(p, w.b, h, q0 + cb + 32 + lane);
+      ItemIter cur, nxt;
+      cur.start(w, 0);
+      nxt = cur;
+      nxt.next(w);
+      const int hbase = w.kvh * p.groups;
+      // each warp stages the LSEs of its kWgCols query columns in its own ring
+      // (lane l: columns l, l + 32, ... of its share), prefetched one item
+      // ahead, so no barrier spans more than the warp
+      float* ring = lse_s + warp * 2 * kWgCols;
+      float ln[Wp::kChunks];
+#pragma unroll
+      for (int c2 = 0; c2 < Wp::kChunks; ++c2)
+        ln[c2] = lse2_of(p, w.b, hbase + cur.hh, cur.qt * kTileRows + cb + 32 * c2 + lane);
       for (int i = 0; i < w.n; ++i) {
-        float* ls = ring + (i & 1) * kHalfCols;
-        ls[lane] = ln0;
-        ls[32 + lane] = ln1;
-        cols_item(p, w, i, h, q0);
+        float* ls = ring + (i & 1) * kWgCols;
+#pragma unroll
+        for (int c2 = 0; c2 < Wp::kChunks; ++c2) ls[32 * c2 + lane] = ln[c2];
+        const int q0 = cur.qt * kTileRows;
         if (i + 1 < w.n) {
-          int h1, q1;
-          cols_item(p, w, i + 1, h1, q1);
-          ln0 = lse2_of(p, w.b, h1, q1 + cb + lane);
-          ln1 = lse2_of(p, w.b, h1, q1 + cb + 32 + lane);
+#pragma unroll
+          for (int c2 = 0; c2 < Wp::kChunks; ++c2)
+            ln[c2] = lse2_of(p, w.b, hbase + nxt.hh, nxt.qt * kTileRows + cb + 32 * c2 + lane);
         }
+        cur = nxt;
+        nxt.next(w);
         __syncwarp();
         const int acc = i & 1;
         // after a timeout the loop keeps its shape (no waits), so whole warps
@@ -373,12 +409,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
         // causal: query column j sees this row's key iff j >= key - q_offset - q0
         const bool diag = p.causal && q0 + p.q_offset < w.k0 + kTileRows - 1;
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
+        for (int c2 = 0; c2 < Wp::kChunks; ++c2) {
           uint32_t v[32];
           const int col0 = cb + 32 * c2;
           tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + col0), v);
           tmem_wait_ld_into(v);
-          if (c2 == 1) {
+          if (c2 == Wp::kChunks - 1) {
             tc_fence_before();
             mbar_arrive(tempty + acc);
           }
@@ -402,12 +438,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
             k0 + kTileRows > p.tk || (p.causal && k0 + kTileRows - 1 > w.q0 + p.q_offset);
         const int jmax = (p.causal ? min(p.tk, qpos + 1) : p.tk) - k0;  // columns j < jmax count
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
+        for (int c2 = 0; c2 < Wp::kChunks; ++c2) {
           uint32_t v[32];
           const int col0 = cb + 32 * c2;
           tmem_ld32(lane_base + (uint32_t)(acc * kTileRows + col0), v);
           tmem_wait_ld_into(v);
-          if (c2 == 1) {
+          if (c2 == Wp::kChunks - 1) {
             tc_fence_before();
             mbar_arrive(tempty + acc);
           }
@@ -415,17 +451,24 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
           else lse_chunk<false>(v, c, 0, m, l);
         }
       }
-      // merge the two warpgroups' halves of each row
-      float* mrg = lse_s;  // [128][2]
-      if (cb != 0) {
-        mrg[2 * row] = m;
-        mrg[2 * row + 1] = l;
+      // merge the warpgroups' shares of each row
+      float* mrg = lse_s;  // [WG - 1][128][2]
+      if (wg != 0) {
+        mrg[((wg - 1) * kTileRows + row) * 2] = m;
+        mrg[((wg - 1) * kTileRows + row) * 2 + 1] = l;
       }
-      named_barrier(1, kEpiThreads);
-      if (cb == 0 && ok && q < p.tq) {
-        const float m1 = mrg[2 * row], l1 = mrg[2 * row + 1];
-        const float mm = fmaxf(m, m1);
-        const float ls = mm == -INFINITY ? 0.f : l * ex2(m - mm) + l1 * ex2(m1 - mm);
+      if (WG > 1) named_barrier(1, kEpiThreads);
+      if (wg == 0 && ok && q < p.tq) {
+        float mm = m;
+#pragma unroll
+        for (int o = 1; o < WG; ++o) mm = fmaxf(mm, mrg[((o - 1) * kTileRows + row) * 2]);
+        float ls = 0.f;
+        if (mm != -INFINITY) {
+          ls = l * ex2(m - mm);
+#pragma unroll
+          for (int o = 1; o < WG; ++o)
+            ls += mrg[((o - 1) * kTileRows + row) * 2 + 1] * ex2(mrg[((o - 1) * kTileRows + row) * 2] - mm);
+        }
         const float kLn2 = 0.6931471805599453f;
         p.lse[(size_t)w.res_head * p.tq + q] = ls > 0.f ? (mm + lg2(ls)) * kLn2 : -INFINITY;
       }
@@ -461,14 +504,16 @@ cudaError_t prefill_error_word(uint32_t** out) {
 template <int D, bool kCols>
 static cudaError_t launch_umma(PrefillParams p, const CUtensorMap maps[2], long long grid,
                                cudaStream_t stream) {
+  constexpr int WG = kCols ? TKV_PF_WG_COLS : TKV_PF_WG_LSE;
+  using L = PfLayout<D, WG>;
   if (grid <= 0 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   cudaError_t e = prefill_error_word(&p.err);
   if (e != cudaSuccess) return e;
-  auto kern = umma_pass_kernel<D, kCols>;
+  auto kern = umma_pass_kernel<D, kCols, WG>;
   // the shared-memory opt-in is per function and device; it is idempotent
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PfLayout<D>::kBytes);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
   if (e != cudaSuccess) return e;
-  kern<<<(unsigned)grid, kUmmaThreads, PfLayout<D>::kBytes, stream>>>(p, maps[0], maps[1]);
+  kern<<<(unsigned)grid, PfWarps<WG>::kThreads, L::kBytes, stream>>>(p, maps[0], maps[1]);
   return cudaGetLastError();
 }
 
