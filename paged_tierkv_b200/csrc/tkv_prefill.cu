@@ -49,7 +49,7 @@ constexpr int kTileRows = 128;       // M of every MMA and the rows (N) of every
 // The epilogue is WG warpgroups: warp w < 4 WG reads TMEM lanes 32 (w % 4) ..
 // (its lane quarter) in the accumulator columns [128 / WG * (w / 4), + 128 /
 // WG) of its warpgroup; warp 4 WG is the TMA producer, warp 4 WG + 1 the MMA
-// issuer.  Warpgroups per pass (build-time): more of them keep more exp2
+// issuer, warp 4 WG + 2 (column pass) stages the query LSEs of each item.  Warpgroups per pass (build-time): more of them keep more exp2
 // streams in flight per SM, at fewer registers per thread.
 #ifndef TKV_PF_WG_LSE
 #define TKV_PF_WG_LSE 2
@@ -63,7 +63,8 @@ struct PfWarps {
   static constexpr int kEpiThreads = 128 * WG;
   static constexpr int kProdWarp = 4 * WG;
   static constexpr int kMmaWarp = 4 * WG + 1;
-  static constexpr int kThreads = kEpiThreads + 64;
+  static constexpr int kLseWarp = 4 * WG + 2;
+  static constexpr int kThreads = kEpiThreads + 96;
   static constexpr int kCols = kTileRows / WG;   // accumulator columns per warpgroup
   static constexpr int kChunks = kCols / 32;     // 32-column TMEM loads per item
 };
@@ -75,12 +76,12 @@ struct PfLayout {
   static constexpr int kTile = kTileRows * D * 2;  // [D/64][128 rows][64] fp16, 128B-swizzled
   static constexpr int kStages = D == 128 ? 2 : 4;
   static constexpr int kBarOff = kTile * (1 + kStages);
-  // full[S], empty[S], resident, tfull[2], tempty[2], done
-  static constexpr int kNumBars = 2 * kStages + 6;
+  // full[S], empty[S], resident, tfull[2], tempty[2], done, lfull[4], lempty[4]
+  static constexpr int kNumBars = 2 * kStages + 14;
   static constexpr int kLseOff = kBarOff + kNumBars * 8;
-  // column pass: per epilogue warp a ring of 2 x kCols LSEs (4 KB in all);
-  // LSE pass: the other warpgroups' (max, sum) per row, [WG - 1][128][2]
-  static constexpr int kTaddrOff = kLseOff + 4 * WG * 2 * PfWarps<WG>::kCols * 4;
+  // column pass: a ring of 4 items' 128 query LSEs (2 KB); LSE pass: the
+  // other warpgroups' (max, sum) per row, [WG - 1][128][2] (<= 3 KB)
+  static constexpr int kTaddrOff = kLseOff + 4096;
   static constexpr int kBytes = kTaddrOff + 16 + 1024;  // + slack to align the base to 1024
 };
 
@@ -155,12 +156,6 @@ struct ItemIter {
     }
   }
 };
-
-// log2-domain LSE of query row q of head h (+inf for rows past the end, whose
-// exponentials then vanish).
-__device__ __forceinline__ float lse2_of(const PrefillParams& p, int b, int h, int q) {
-  return q < p.tq ? __ldg(p.lse + ((size_t)b * p.num_heads + h) * p.tq + q) * kLog2eP : INFINITY;
-}
 
 __device__ __forceinline__ void tmem_wait_ld_into(uint32_t (&v)[32]) {
   // the wait "rewrites" the registers, so no use of them moves above it
@@ -267,6 +262,8 @@ __global__ void __launch_bounds__(PfWarps<WG>::kThreads, 2)
   uint64_t* tfull = res_full + 1;
   uint64_t* tempty = res_full + 3;
   uint64_t* done = res_full + 5;
+  uint64_t* lfull = done + 1;   // column pass: LSE ring slot written
+  uint64_t* lempty = done + 5;  // column pass: LSE ring slot read by every epilogue warp
   float* lse_s = reinterpret_cast<float*>(smem + L::kLseOff);
   uint32_t* taddr_s = reinterpret_cast<uint32_t*>(smem + L::kTaddrOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -285,6 +282,10 @@ __global__ void __launch_bounds__(PfWarps<WG>::kThreads, 2)
     mbar_init(tempty, kEpiThreads);
     mbar_init(tempty + 1, kEpiThreads);
     mbar_init(done, 1);
+    for (int k = 0; k < 4; ++k) {
+      mbar_init(lfull + k, 32);
+      mbar_init(lempty + k, kEpiThreads / 32);
+    }
     fence_mbar_init();
   }
   if (warp == kProdWarp) tmem_alloc(taddr_s, kTmemCols);
@@ -331,6 +332,31 @@ __global__ void __launch_bounds__(PfWarps<WG>::kThreads, 2)
       if (!ok) atomicOr(p.err, TKV_DEVERR_TIMEOUT);
     }
     __syncwarp();
+  } else if (warp == Wp::kLseWarp) {
+    // ---- column pass: the query LSEs of item i (log2 domain, +inf past the
+    // last query row) into ring slot i % 4, up to four items ahead
+    if (kCols) {
+      ItemIter it;
+      it.start(w, 0);
+      const int hbase = w.kvh * p.groups;
+      bool ok = true;
+      for (int i = 0; i < w.n; ++i) {
+        const int slot = i & 3;
+        if (i >= 4 && ok && !mbar_wait(lempty + slot, ((i >> 2) - 1) & 1)) ok = false;
+        __syncwarp();
+        const int q0 = it.qt * kTileRows;
+        const float* src = p.lse + ((size_t)w.b * p.num_heads + hbase + it.hh) * p.tq;
+#pragma unroll
+        for (int k = 0; k < kTileRows / 32; ++k) {
+          const int q = q0 + 32 * k + lane;
+          lse_s[slot * kTileRows + 32 * k + lane] = q < p.tq ? __ldg(src + q) * kLog2eP : INFINITY;
+        }
+        mbar_arrive(lfull + slot);
+        it.next(w);
+      }
+      if (!ok && lane == 0) atomicOr(p.err, TKV_DEVERR_TIMEOUT);
+    }
+    __syncwarp();
   } else if (warp == kMmaWarp) {
     // ---- MMA issuer: S^T tile (kCols) or S tile = resident (A) x streamed (B)^T
     if (lane == 0) {
@@ -374,35 +400,17 @@ __global__ void __launch_bounds__(PfWarps<WG>::kThreads, 2)
     if (kCols) {
       const int key = w.k0 + row;
       float sum[4] = {0.f, 0.f, 0.f, 0.f};
-      ItemIter cur, nxt;
+      ItemIter cur;
       cur.start(w, 0);
-      nxt = cur;
-      nxt.next(w);
-      const int hbase = w.kvh * p.groups;
-      // each warp stages the LSEs of its kWgCols query columns in its own ring
-      // (lane l: columns l, l + 32, ... of its share), prefetched one item
-      // ahead, so no barrier spans more than the warp
-      float* ring = lse_s + warp * 2 * kWgCols;
-      float ln[Wp::kChunks];
-#pragma unroll
-      for (int c2 = 0; c2 < Wp::kChunks; ++c2)
-        ln[c2] = lse2_of(p, w.b, hbase + cur.hh, cur.qt * kTileRows + cb + 32 * c2 + lane);
       for (int i = 0; i < w.n; ++i) {
-        float* ls = ring + (i & 1) * kWgCols;
-#pragma unroll
-        for (int c2 = 0; c2 < Wp::kChunks; ++c2) ls[32 * c2 + lane] = ln[c2];
-        const int q0 = cur.qt * kTileRows;
-        if (i + 1 < w.n) {
-#pragma unroll
-          for (int c2 = 0; c2 < Wp::kChunks; ++c2)
-            ln[c2] = lse2_of(p, w.b, hbase + nxt.hh, nxt.qt * kTileRows + cb + 32 * c2 + lane);
-        }
-        cur = nxt;
-        nxt.next(w);
-        __syncwarp();
-        const int acc = i & 1;
+        const int slot = i & 3;
         // after a timeout the loop keeps its shape (no waits), so whole warps
         // run tcgen05.ld and every thread meets the final barriers
+        if (ok && !mbar_wait(lfull + slot, (i >> 2) & 1)) ok = false;
+        const float* ls = lse_s + slot * kTileRows + cb;
+        const int q0 = cur.qt * kTileRows;
+        cur.next(w);
+        const int acc = i & 1;
         if (ok && !mbar_wait(tfull + acc, (i >> 1) & 1)) ok = false;
         __syncwarp();
         tc_fence_after();
@@ -421,6 +429,8 @@ __global__ void __launch_bounds__(PfWarps<WG>::kThreads, 2)
           if (diag) cols_chunk<true>(v, ls + 32 * c2, c, col0 - (key - p.q_offset - q0), sum);
           else cols_chunk<false>(v, ls + 32 * c2, c, 0, sum);
         }
+        __syncwarp();  // the warp's reads of the ring slot are done
+        if (lane == 0) mbar_arrive(lempty + slot);
       }
       if (ok && key < p.tk) atomicAdd(p.token_mass + key, (sum[0] + sum[1]) + (sum[2] + sum[3]));
     } else {
