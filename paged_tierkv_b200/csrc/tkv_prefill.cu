@@ -171,12 +171,12 @@ __device__ __forceinline__ void tmem_wait_ld_into(uint32_t (&v)[32]) {
 }
 
 // Logits per 32 whose exp2 runs on the FMA pipe (ex2_fma) instead of MUFU.
-// MUFU retires 16 exp2 per SM clock; in the LSE pass it is the busiest pipe
-// while the FMA and ALU pipes idle, so a share of its exps moves over.  The
-// column pass gains nothing from it (it does not saturate MUFU) and keeps all
-// its exps on MUFU.
+// MUFU retires 16 exp2 per SM clock and is the busiest pipe of both passes
+// while the FMA and ALU pipes idle, so a share of the exps moves over (the
+// shares measured best on B200: 4 / 32 in the LSE pass, 2 / 32 in the column
+// pass, whose epilogue spends more issue slots per logit).
 constexpr int kLseFmaExps = 4;
-constexpr int kColsFmaExps = 0;
+constexpr int kColsFmaExps = 2;
 
 // Logit j of a 32-chunk takes the FMA-pipe exp2 when kFma of 32 do (every
 // (32 / kFma)-th logit).
