@@ -972,8 +972,8 @@ def run_prefill(a, rank, device):
                          "peak": round(exp_peak / 1e12, 3), "unit": "Texp2/s",
                          "frac": round(exps / (ms_full * 1e-3) / exp_peak, 4),
                          "note": "peak = 16 MUFU exp2 per SM clock x 148 SMs at the 1965 MHz "
-                                 "max clock (nominal); 1/8 of the LSE pass's exps run on the "
-                                 "FMA pipe instead"},
+                                 "max clock (nominal); 1/8 of the LSE pass's and 1/16 of the column "
+                                 "pass's exps run on the FMA pipe instead"},
         "gpu_launches": steps * 3,
     }
     print(json.dumps(line), flush=True)
