@@ -330,6 +330,52 @@ int32_t tkv_decode_plan(const tkv_pools* pools, const tkv_decode_args* args,
   return TKV_OK;
 }
 
+// The four TMA descriptors of a pool set.  Serving loops decode against the
+// same pools layer after layer, and encoding costs host time on every call,
+// so the last few sets of this thread are kept, keyed by every input of the
+// encoding.
+static bool pool_maps(const tkv_pools* pools, CUtensorMap maps[4]) {
+  struct Entry {
+    const void* ptr[4];
+    int64_t hot_rows, warm_rows;
+    int d, bs, valid;
+    CUtensorMap maps[4];
+  };
+  thread_local Entry cache[4] = {};
+  thread_local int next = 0;
+  const int bs = pools->block_size, d = pools->head_dim, hkv = pools->kv_heads;
+  const int64_t hot_rows = pools->hot_slots * hkv * bs;
+  const int64_t warm_rows = pools->warm_slots * hkv * bs;
+  const void* ptr[4] = {pools->hot_k, pools->hot_v, pools->warm_k, pools->warm_v};
+  for (Entry& e : cache) {
+    if (e.valid && e.hot_rows == hot_rows && e.warm_rows == warm_rows && e.d == d && e.bs == bs &&
+        e.ptr[0] == ptr[0] && e.ptr[1] == ptr[1] && e.ptr[2] == ptr[2] && e.ptr[3] == ptr[3]) {
+      std::memcpy(maps, e.maps, sizeof(e.maps));
+      return true;
+    }
+  }
+#if TKV_HOT_3D
+  const bool hot_ok = encode_hot_map_3d(&maps[0], pools->hot_k, hot_rows, d, bs) &&
+                      encode_hot_map_3d(&maps[1], pools->hot_v, hot_rows, d, bs);
+#else
+  const bool hot_ok = encode_pool_map(&maps[0], pools->hot_k, true, hot_rows, d, 64, bs) &&
+                      encode_pool_map(&maps[1], pools->hot_v, true, hot_rows, d, 64, bs);
+#endif
+  if (!hot_ok || !encode_pool_map(&maps[2], pools->warm_k, false, warm_rows, d, d, bs) ||
+      !encode_pool_map(&maps[3], pools->warm_v, false, warm_rows, d, d, bs))
+    return false;
+  Entry& e = cache[next];
+  next = (next + 1) % 4;
+  for (int i = 0; i < 4; ++i) e.ptr[i] = ptr[i];
+  e.hot_rows = hot_rows;
+  e.warm_rows = warm_rows;
+  e.d = d;
+  e.bs = bs;
+  e.valid = 1;
+  std::memcpy(e.maps, maps, sizeof(e.maps));
+  return true;
+}
+
 static int32_t decode_impl(const tkv_pools* pools, const tkv_decode_args* a,
                            const tkv_exchange* xc, void* stream) {
   Plan plan;
@@ -348,20 +394,8 @@ static int32_t decode_impl(const tkv_pools* pools, const tkv_decode_args* a,
   if (st != TKV_OK) return st;
 
   CUtensorMap maps[4];
+  if (!pool_maps(pools, maps)) return TKV_ERR_CUDA;
   const int bs = pools->block_size, d = pools->head_dim, hkv = pools->kv_heads;
-  const int64_t hot_rows = pools->hot_slots * hkv * bs;
-  const int64_t warm_rows = pools->warm_slots * hkv * bs;
-#if TKV_HOT_3D
-  const bool hot_ok = encode_hot_map_3d(&maps[0], pools->hot_k, hot_rows, d, bs) &&
-                      encode_hot_map_3d(&maps[1], pools->hot_v, hot_rows, d, bs);
-#else
-  const bool hot_ok = encode_pool_map(&maps[0], pools->hot_k, true, hot_rows, d, 64, bs) &&
-                      encode_pool_map(&maps[1], pools->hot_v, true, hot_rows, d, 64, bs);
-#endif
-  if (!hot_ok ||
-      !encode_pool_map(&maps[2], pools->warm_k, false, warm_rows, d, d, bs) ||
-      !encode_pool_map(&maps[3], pools->warm_v, false, warm_rows, d, d, bs))
-    return TKV_ERR_CUDA;
 
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   DecodeParams p;

@@ -30,8 +30,16 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def _stream(stream) -> ctypes.c_void_p:
+# torch's raw current-stream accessor (what its own kernel launchers use);
+# building a torch.cuda.Stream object per call costs microseconds
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream(stream, device_index: int | None = None) -> ctypes.c_void_p:
     if stream is None:
+        if _RAW_STREAM is not None:
+            idx = torch.cuda.current_device() if device_index is None else device_index
+            return ctypes.c_void_p(_RAW_STREAM(idx))
         stream = torch.cuda.current_stream()
     return ctypes.c_void_p(stream.cuda_stream)
 
@@ -141,6 +149,20 @@ class TieredPools:
             if t is None or t.dtype != mdt or t.numel() != n_meta or not t.is_contiguous():
                 raise ValueError(f"{name} must be a contiguous {mdt} tensor with {n_meta} elements.")
 
+    def struct(self) -> N.TkvPools:
+        """validate() and as_struct() for repeated calls: the struct is rebuilt
+        only when a tensor object or its data pointer changes."""
+        key = self._key() + tuple(t.data_ptr() if t is not None else 0 for t in (
+            self.hot_k, self.hot_v, self.warm_k, self.warm_v, self.k_scale, self.k_zero,
+            self.v_scale, self.v_zero))
+        cached = getattr(self, "_struct_cache", None)
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        self.validate()
+        st = self.as_struct()
+        object.__setattr__(self, "_struct_cache", (key, st))
+        return st
+
     def as_struct(self) -> N.TkvPools:
         return N.TkvPools(
             _ptr(self.hot_k), _ptr(self.hot_v), _ptr(self.warm_k), _ptr(self.warm_v),
@@ -212,15 +234,17 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
     query = query.contiguous()
     if query.data_ptr() % 16:  # the kernel reads the query in 16-byte vectors
         query = query.clone()
-    pools.validate()
+    pstruct = pools.struct()
     batch, num_heads, head_dim = query.shape
     if head_dim != pools.head_dim:
         raise ValueError("query head_dim does not match the pools.")
     table = _as_table(block_table, batch, "block_table")
     states = _as_table(block_states, batch, "block_states")
     lengths = _as_table(block_lengths, batch, "block_lengths")
-    if not (_row_stride(table) == _row_stride(states) == _row_stride(lengths)):
+    row_stride = _row_stride(table)
+    if not (row_stride == _row_stride(states) == _row_stride(lengths)):
         table, states, lengths = table.contiguous(), states.contiguous(), lengths.contiguous()
+        row_stride = _row_stride(table)
     max_blocks = int(table.shape[1])
     nb_dev = None
     if isinstance(num_blocks, torch.Tensor):
@@ -243,27 +267,35 @@ def decode_attention(query: torch.Tensor, block_table: torch.Tensor, block_state
         lse = (torch.empty((batch, num_heads), dtype=torch.float32, device=query.device)
                if return_lse else None)
     lib = N.load()
-    st = _stream(stream)
-    pstruct = pools.as_struct()
+    dev_index = query.device.index
+    st = _stream(stream, dev_index)
     args = N.TkvDecodeArgs(
         _ptr(query), _DTYPE[query.dtype], _DTYPE[odt], batch, num_heads, int(num_key_value_groups),
-        max_blocks, _ptr(table), _ptr(states), _ptr(lengths), _row_stride(table), _ptr(nb_dev),
+        max_blocks, _ptr(table), _ptr(states), _ptr(lengths), row_stride, _ptr(nb_dev),
         nb_uniform, float(scaling), _ptr(out), _ptr(lse), _ptr(scores), int(num_splits),
         int(chunk_blocks), None, 0)
-    splits = ctypes.c_int32()
-    nbytes = ctypes.c_size_t()
-    N.check(lib.tkv_decode_plan(ctypes.byref(pstruct), ctypes.byref(args), ctypes.byref(splits),
-                                ctypes.byref(nbytes)), "tkv_decode_plan")
-    ws = workspace_for(query.device, st.value or 0, nbytes.value)
-    args.workspace = ws.data_ptr()
-    args.workspace_bytes = ws.numel()
-    if exchange is not None:
-        N.check(lib.tkv_decode_attention_exchange(ctypes.byref(pstruct), ctypes.byref(args),
-                                                  ctypes.byref(exchange), st),
-                "tkv_decode_attention_exchange")
-    else:
-        N.check(lib.tkv_decode_attention(ctypes.byref(pstruct), ctypes.byref(args), st),
-                "tkv_decode_attention")
+    # The stream's workspace usually fits already; the plan (and a larger
+    # workspace) is only needed when the library reports that it does not.
+    ws = _WORKSPACES.get((dev_index, st.value or 0))
+    for attempt in range(2):
+        if ws is None or attempt:
+            splits = ctypes.c_int32()
+            nbytes = ctypes.c_size_t()
+            N.check(lib.tkv_decode_plan(ctypes.byref(pstruct), ctypes.byref(args),
+                                        ctypes.byref(splits), ctypes.byref(nbytes)), "tkv_decode_plan")
+            ws = workspace_for(query.device, st.value or 0, nbytes.value)
+        args.workspace = ws.data_ptr()
+        args.workspace_bytes = ws.numel()
+        if exchange is not None:
+            status = lib.tkv_decode_attention_exchange(ctypes.byref(pstruct), ctypes.byref(args),
+                                                       ctypes.byref(exchange), st)
+            what = "tkv_decode_attention_exchange"
+        else:
+            status = lib.tkv_decode_attention(ctypes.byref(pstruct), ctypes.byref(args), st)
+            what = "tkv_decode_attention"
+        if status != N.TKV_ERR_WORKSPACE or attempt:
+            break
+    N.check(status, what)
     return out, scores, lse
 
 
