@@ -32,6 +32,26 @@ def _require_backend():
             "`python -m paged_tierkv_b200.build` or use TIERKV_ATTENTION_BACKEND=eager.") from exc
 
 
+# The pool sets of the last two calls.  A runtime passes the same pool tensors
+# layer after layer, so their checks and their C struct are reused; the
+# bound keeps pools the runtime has replaced (grown) from staying alive.
+_POOLS_CACHE: list = []
+
+
+def _pools_of(tensors) -> TieredPools:
+    key = tuple(id(t) for t in tensors) + tuple(0 if t is None else t.data_ptr() for t in tensors)
+    for k, pools in _POOLS_CACHE:
+        if k == key:
+            return pools
+    hk, hv, wk, wv, ks, kz, vs, vz = tensors
+    pools = TieredPools(hk.contiguous(), hv.contiguous(), wk.contiguous(), wv.contiguous(),
+                        ks.contiguous(), kz.contiguous(), vs.contiguous(),
+                        kz.new_empty(0) if vz is None else vz.contiguous(), FORMAT_R)
+    _POOLS_CACHE.insert(0, (key, pools))
+    del _POOLS_CACHE[2:]
+    return pools
+
+
 def tierkv_decode_attention(
     query_states: torch.Tensor,
     block_table: torch.Tensor,
@@ -72,10 +92,8 @@ def tierkv_decode_attention(
     if int(num_blocks) > block_table.shape[0]:
         raise ValueError("num_blocks exceeds the provided block table length.")
 
-    pools = TieredPools(hot_k_pool.contiguous(), hot_v_pool.contiguous(), warm_k_pool.contiguous(),
-                        warm_v_pool.contiguous(), k_scale.contiguous(), k_zero.contiguous(),
-                        v_scale.contiguous(), k_zero.new_empty(0) if v_zero is None else v_zero.contiguous(),
-                        FORMAT_R)
+    pools = _pools_of((hot_k_pool, hot_v_pool, warm_k_pool, warm_v_pool, k_scale, k_zero, v_scale,
+                       v_zero))
     _, num_heads, _, head_dim = query_states.shape
     out, scores, _ = decode_attention(
         query_states, block_table.reshape(1, -1), block_states.reshape(1, -1),

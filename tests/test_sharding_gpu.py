@@ -1,7 +1,8 @@
-"""Context-sharded decode over NCCL on 2 GPUs (skipped with fewer): each rank
-runs the sm_100a kernel on its block range, the packed partials are
-all-gathered and merged by the LSE-merge kernel; the result must match the
-unsharded oracle."""
+"""Context-sharded decode on 2, 4 and 8 GPUs (each world size skipped with
+fewer GPUs): each rank runs the sm_100a kernel on its block range; the packed
+partials are all-gathered over NCCL and merged by the LSE-merge kernel, or
+exchanged over CUDA IPC peer memory inside the decode launch; the result must
+match the unsharded oracle on every rank."""
 
 import os
 import socket
@@ -52,13 +53,13 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_context_sharded_decode_nccl():
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_context_sharded_decode_nccl(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     from oracle import tierkv_oracle as orc
     from tierkv_cases import make_case
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -122,15 +123,15 @@ def _worker_p2p(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_context_sharded_decode_peer_exchange():
-    """Two processes, one GPU each: the exchange of partials over CUDA IPC
-    peer memory inside the decode launch (no collective on the data path)."""
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_context_sharded_decode_peer_exchange(world):
+    """One process per GPU: the exchange of partials over CUDA IPC peer memory
+    inside the decode launch (no collective on the data path)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     from oracle import tierkv_oracle as orc  # noqa: F401
     from tierkv_cases import make_case, oracle_decode
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
