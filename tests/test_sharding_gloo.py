@@ -87,10 +87,10 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-def test_context_sharded_decode_two_ranks():
+@pytest.mark.parametrize("world", [2, 4])
+def test_context_sharded_decode_over_ranks(world):
     from oracle import tierkv_oracle as orc
     from tierkv_cases import make_case
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
