@@ -47,6 +47,10 @@ def parse():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--ctx", type=int, default=32768)
     ap.add_argument("--hot-frac", type=float, default=0.25)
+    ap.add_argument("--warm-frac", type=float, default=None,
+                    help="WARM share of the blocks (default: the non-HOT blocks split 2:1 "
+                         "WARM:COLD, configuration 5); 0.6 with --hot-frac 0.2 is configuration "
+                         "3's 20/60/20 mix")
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--sweep", action="store_true",
                     help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
@@ -152,14 +156,16 @@ def ncu_traffic(key: str):
 
 
 def workload_key(a) -> str:
-    return f"c5_b{a.batch}_ctx{a.ctx}_h{a.hot_frac:g}_bs{a.block_size}"
+    w = "" if getattr(a, "warm_frac", None) is None else f"_w{a.warm_frac:g}"
+    return f"c5_b{a.batch}_ctx{a.ctx}_h{a.hot_frac:g}{w}_bs{a.block_size}"
 
 
 def build_workload(a, seed, device):
     from paged_tierkv_b200 import workloads
     return workloads.make_workload(batch=a.batch, q_heads=32, kv_heads=8, head_dim=128,
                                    block_size=a.block_size, ctx_tokens=a.ctx,
-                                   hot_frac=a.hot_frac, seed=seed, device=device)
+                                   hot_frac=a.hot_frac, warm_frac=getattr(a, "warm_frac", None),
+                                   seed=seed, device=device)
 
 
 def time_device(wl, steps, warmup, dist_on):
