@@ -569,11 +569,14 @@ def _prefill_kv(pool, key_states: torch.Tensor, value_states: torch.Tensor):
     return key_states.contiguous(), value_states.contiguous()
 
 
-def _hot_block(pool, plan: SyncPlan, physical_idx: int, key, length: int) -> int:
+def _hot_block(pool, plan: SyncPlan, physical_idx: int, key, length: int,
+               ensure: bool = True) -> int:
     """write_hot_tokens(physical_idx, 0, chunk) (tierkv_policy.py:934-967)
-    without its tensor work; returns the slot."""
+    without its tensor work; returns the slot.  ``ensure=False`` skips the
+    geometry check of an input it has already passed."""
     physical_idx = pool._check_physical_idx(physical_idx)
-    pool._ensure_metadata(key)
+    if ensure:
+        pool._ensure_metadata(key)
     current_state = pool.get_physical_state(physical_idx)
     if current_state == COLD_STATE:
         raise KeyError(f"Physical block {physical_idx} is COLD and cannot be promoted.")
@@ -589,11 +592,13 @@ def _hot_block(pool, plan: SyncPlan, physical_idx: int, key, length: int) -> int
     return int(slot_idx)
 
 
-def _warm_block(pool, plan: SyncPlan, physical_idx: int, key, length: int) -> int:
+def _warm_block(pool, plan: SyncPlan, physical_idx: int, key, length: int,
+                ensure: bool = True) -> int:
     """write_warm_block (tierkv_policy.py:969-1002) without its tensor work;
     returns the slot."""
     physical_idx = pool._check_physical_idx(physical_idx)
-    pool._ensure_metadata(key)
+    if ensure:
+        pool._ensure_metadata(key)
     current_state = pool.get_physical_state(physical_idx)
     if current_state == HOT_STATE:
         pool._free_hot_slot(pool.physical_slots.get(physical_idx, -1))
@@ -646,10 +651,19 @@ def plan_prefill(self, seq_id: int, key_states: torch.Tensor, value_states: torc
     desired_states = self._desired_prefill_states(num_blocks, block_scores)
     out = out if out is not None else PrefillPlan(SyncPlan(int(seq_id)))
     plan = out.plan
+    allocate = self.block_manager.allocate_block
+    update_state = self.block_manager.update_block_state
+    add_entry = out.entries.append
+    locations, slots_of, lengths_of = pool.physical_locations, pool.physical_slots, pool.physical_lengths
+    cell_physical, cell_states, cell_slots, cell_lengths = (plan.physical, plan.states, plan.slots,
+                                                            plan.lengths)
+    layer = int(seq_id)
+    key3 = None   # the layer's K as [1, kv_heads, tokens, head_dim] once checked
+    checked = False  # the pool has accepted key3's geometry (_ensure_metadata)
     for logical_idx, desired_state in enumerate(desired_states):
-        physical_idx = self.block_manager.allocate_block(seq_id)
+        physical_idx = allocate(seq_id)
         if desired_state != HOT_STATE:
-            self.block_manager.update_block_state(seq_id, logical_idx, desired_state)
+            update_state(seq_id, logical_idx, desired_state)
         start = logical_idx * block_size
         length = min(start + block_size, total_tokens) - start
         if desired_state in (HOT_STATE, WARM_STATE) or (desired_state == COLD_STATE
@@ -658,22 +672,42 @@ def plan_prefill(self, seq_id: int, key_states: torch.Tensor, value_states: torc
                 pool._check_physical_idx(physical_idx)
                 key, value = _prefill_kv(pool, key_states, value_states)
                 out.key, out.value = key[0], value[0]
+            if key3 is None:
+                key3 = out.key[None]
         if desired_state == HOT_STATE:
-            slot = _hot_block(pool, plan, physical_idx, out.key[None], length)
-            out.entries.append((HOT_STATE, slot, start, length))
+            slot = _hot_block(pool, plan, physical_idx, key3, length, ensure=not checked)
+            checked = True
+            add_entry((HOT_STATE, slot, start, length))
         elif desired_state == WARM_STATE:
-            slot = _warm_block(pool, plan, physical_idx, out.key[None], length)
-            out.entries.append((WARM_STATE, slot, start, length))
+            slot = _warm_block(pool, plan, physical_idx, key3, length, ensure=not checked)
+            checked = True
+            add_entry((WARM_STATE, slot, start, length))
         elif desired_state == COLD_STATE:
             if not pool.is_allocated():
-                slot = _hot_block(pool, plan, physical_idx, out.key[None], length)
-                out.entries.append((HOT_STATE, slot, start, length))
+                slot = _hot_block(pool, plan, physical_idx, key3, length, ensure=not checked)
+                checked = True
+                add_entry((HOT_STATE, slot, start, length))
                 _demote_to_cold(pool, plan, physical_idx)
             else:
                 _cold_block(pool, plan, physical_idx, length)
         else:
             raise ValueError(f"Unsupported desired state: {desired_state}")
-        _set_block_entry(pool, plan, seq_id, logical_idx, physical_idx, desired_state)
+        # set_block_entry (tierkv_policy.py:1016-1035); the physical index has
+        # passed its range check in the write above
+        if not pool.is_allocated():
+            raise RuntimeError("CompactTieredKVTensorPool has not been allocated yet.")
+        if layer < 0 or layer >= pool.num_layers:
+            raise ValueError("layer_idx is out of range.")
+        if logical_idx >= pool.max_blocks_per_layer:
+            raise RuntimeError(
+                f"Logical block {logical_idx} exceeds max_blocks_per_layer={pool.max_blocks_per_layer}.")
+        physical_idx = int(physical_idx)
+        cell = (layer, logical_idx)
+        locations[physical_idx] = cell
+        cell_physical[cell] = physical_idx
+        cell_states[cell] = int(desired_state)
+        cell_slots[cell] = int(slots_of.get(physical_idx, -1))
+        cell_lengths[cell] = int(lengths_of.get(physical_idx, 0))
     layer_state.num_blocks = num_blocks
     layer_state.open_physical_idx = None
     layer_state.open_token_count = 0
