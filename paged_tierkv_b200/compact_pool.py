@@ -88,7 +88,11 @@ class CompactPool:
             raise ValueError("KV tensors must have shape [1, kv_heads, tokens, head_dim].")
         if key_states.shape[-2] > self.block_size:
             raise ValueError("A single stored block cannot exceed block_size tokens.")
-        return (key_states.to(torch.float16).contiguous(), value_states.to(torch.float16).contiguous())
+        if key_states.dtype != torch.float16:
+            key_states = key_states.to(torch.float16)
+        if value_states.dtype != torch.float16:
+            value_states = value_states.to(torch.float16)
+        return key_states.contiguous(), value_states.contiguous()
 
     def _ensure_metadata(self, key_states) -> None:
         if (key_states.device != self.device or int(key_states.shape[1]) != self.kv_heads

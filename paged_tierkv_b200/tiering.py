@@ -478,8 +478,11 @@ def plan_append(self, seq_id: int, key_states: torch.Tensor, value_states: torch
             _promote_to_hot(pool, plan, physical_idx)
         remaining_capacity = self.block_size - layer_state.open_token_count
         take = min(remaining_capacity, total_tokens - offset)
-        k_chunk = key_states[:, :, offset:offset + take, :].contiguous()
-        v_chunk = value_states[:, :, offset:offset + take, :].contiguous()
+        if offset == 0 and take == total_tokens:  # the whole input (one decode token)
+            k_chunk, v_chunk = key_states.contiguous(), value_states.contiguous()
+        else:
+            k_chunk = key_states[:, :, offset:offset + take, :].contiguous()
+            v_chunk = value_states[:, :, offset:offset + take, :].contiguous()
         start = layer_state.open_token_count
         slot, k_chunk, v_chunk = _write_hot_tokens(pool, plan, physical_idx, start, k_chunk, v_chunk)
         if new_logical_idx is not None:
@@ -494,11 +497,32 @@ def plan_append(self, seq_id: int, key_states: torch.Tensor, value_states: torch
     return steps, allocated_new_block
 
 
+# HOT-only pool structs of recent appends, keyed by the pool tensors' pointers
+# and shape (a decode loop appends to the same pools token after token)
+_HOT_STRUCTS: dict = {}
+
+
+def _hot_struct(pool):
+    from . import _native as N
+    hk, hv = pool.hot_k_pool, pool.hot_v_pool
+    key = (hk.data_ptr(), hv.data_ptr(), tuple(hk.shape))
+    st = _HOT_STRUCTS.get(key)
+    if st is None:
+        st = N.TkvPools(hk.data_ptr(), hv.data_ptr(), None, None, None, None, None, None,
+                        int(hk.shape[0]), 0, int(hk.shape[1]), int(hk.shape[2]), int(hk.shape[3]),
+                        ops.FORMAT_R)
+        if len(_HOT_STRUCTS) >= 8:
+            _HOT_STRUCTS.clear()
+        _HOT_STRUCTS[key] = st
+    return st
+
+
 def apply_append(pool, steps, stream=None) -> int:
     """One fused launch per step (after its promotion, if any); returns the
     number of launches."""
     from . import _native as N
     import ctypes
+    lib = N.load()
     launches = 0
     for step in steps:
         if step.plan.promotions:
@@ -511,19 +535,17 @@ def apply_append(pool, steps, stream=None) -> int:
         value = step.value if step.value.data_ptr() % 16 == 0 else step.value.clone()
         cells = []
         for table, recorded in _table_groups(pool, step.plan):
-            width = int(table.shape[1])
-            for (layer, logical), v in recorded.items():
-                cells.append(N.TkvTableCell(table.data_ptr(), layer * width + logical, int(v), 0))
+            if recorded:
+                width, base = int(table.shape[1]), table.data_ptr()
+                cells.extend((base, layer * width + logical, int(v), 0)
+                             for (layer, logical), v in recorded.items())
         if len(cells) > N.TKV_APPEND_MAX_CELLS:
             raise RuntimeError("append step records more table cells than one launch carries.")
         arr = (N.TkvTableCell * max(1, len(cells)))(*cells)
-        hk, hv = pool.hot_k_pool, pool.hot_v_pool  # the append touches the HOT pool only
-        ps = N.TkvPools(hk.data_ptr(), hv.data_ptr(), None, None, None, None, None, None,
-                        int(hk.shape[0]), 0, int(hk.shape[1]), int(hk.shape[2]), int(hk.shape[3]),
-                        ops.FORMAT_R)
-        N.check(N.load().tkv_append_hot_tokens(ctypes.byref(ps), step.slot, step.start,
-                                                int(key.shape[-2]), key.data_ptr(), value.data_ptr(),
-                                                arr, len(cells), ops._stream(stream)),
+        ps = _hot_struct(pool)  # the append touches the HOT pool only
+        N.check(lib.tkv_append_hot_tokens(ctypes.byref(ps), step.slot, step.start,
+                                          int(key.shape[-2]), key.data_ptr(), value.data_ptr(),
+                                          arr, len(cells), ops._stream(stream, key.device.index)),
                 "tkv_append_hot_tokens")
         launches += 1
     return launches
