@@ -154,6 +154,19 @@ def _promote_to_hot(pool, plan: SyncPlan, physical_idx: int) -> None:
     _metadata(pool, plan, physical_idx, HOT_STATE, hot_slot, length)
 
 
+def _int_array(values) -> np.ndarray:
+    """int(x) for every x, as int64.  A 1-D integer sequence or array converts
+    in one numpy call; anything else (floats, bools, tensors of other kinds)
+    goes through int() one element at a time."""
+    try:
+        arr = np.asarray(values)
+    except (TypeError, ValueError):
+        arr = None
+    if arr is not None and arr.ndim == 1 and arr.dtype.kind in "iu":
+        return arr.astype(np.int64, copy=False)
+    return np.asarray([int(x) for x in values], dtype=np.int64)
+
+
 def plan_sync(pool, layer_idx: int, physical_indices, states) -> SyncPlan:
     """The loop of sync_storage_states (tierkv_policy.py:1849-1867), recording
     moves and table cells instead of performing them.  Updates the pool's
@@ -161,8 +174,8 @@ def plan_sync(pool, layer_idx: int, physical_indices, states) -> SyncPlan:
     the reference does, and may grow its tensors through the pool's own slot
     allocators."""
     plan = SyncPlan(int(layer_idx))
-    physical = [int(x) for x in physical_indices]
-    target = np.asarray([int(x) for x in states], dtype=np.int64)
+    physical = _int_array(physical_indices).tolist()
+    target = _int_array(states)
     if len(physical) != len(target):
         # zip() semantics of the reference loop
         n = min(len(physical), len(target))
