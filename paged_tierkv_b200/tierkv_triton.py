@@ -34,7 +34,11 @@ def _require_backend():
 
 # The pool sets of the last two calls.  A runtime passes the same pool tensors
 # layer after layer, so their checks and their C struct are reused; the
-# bound keeps pools the runtime has replaced (grown) from staying alive.
+# bound keeps pools the runtime has replaced (grown) from staying alive.  Only
+# sets of contiguous tensors are kept: the cached entry then holds the caller's
+# own tensor objects, so their ids cannot be reused while it lives, and a
+# non-contiguous pool, which is copied on every call, is never served from a
+# stale copy.
 _POOLS_CACHE: list = []
 
 
@@ -47,8 +51,11 @@ def _pools_of(tensors) -> TieredPools:
     pools = TieredPools(hk.contiguous(), hv.contiguous(), wk.contiguous(), wv.contiguous(),
                         ks.contiguous(), kz.contiguous(), vs.contiguous(),
                         kz.new_empty(0) if vz is None else vz.contiguous(), FORMAT_R)
-    _POOLS_CACHE.insert(0, (key, pools))
-    del _POOLS_CACHE[2:]
+    held = (pools.hot_k, pools.hot_v, pools.warm_k, pools.warm_v, pools.k_scale, pools.k_zero,
+            pools.v_scale, pools.v_zero)
+    if all(a is b for a, b in zip(held, tensors) if b is not None):
+        _POOLS_CACHE.insert(0, (key, pools))
+        del _POOLS_CACHE[2:]
     return pools
 
 
