@@ -231,13 +231,15 @@ __device__ __forceinline__ float* x_lse(const DecodeParams& p, int q, uint32_t e
 // partial slot dj of rows with stride dstride.  All NT threads take part;
 // wsl is shared scratch of kMaxGroups * (cnt + 2) floats.  One warp per
 // head: a lane owns 4 dims (a float4 of every part's row) and, for head_dim
-// 64, every other part; the loop keeps 8 independent 16-byte loads in flight.
+// 64, every other part; each round keeps kMergeDepth independent 16-byte
+// loads in flight, and the LSEs come in rounds of kMergeLseDepth per thread.
 // Partial rows each lane loads per round of the split merge (the merge is
 // latency-bound: one round trip per round).
 #ifndef TKV_MERGE_DEPTH
 #define TKV_MERGE_DEPTH 16
 #endif
 constexpr int kMergeDepth = TKV_MERGE_DEPTH;
+constexpr int kMergeLseDepth = 4;
 
 template <int D, int NT>
 __device__ __forceinline__ void merge_parts(const float* po, const float* plse, int rstride,
@@ -247,9 +249,17 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
                                             uint32_t epoch = 0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* hm = wsl + kMaxGroups * cnt;  // [G] max, [G] sum
-  for (int e = threadIdx.x; e < G * cnt; e += NT) {
-    const int h = e / cnt;
-    wsl[e] = __ldcg(plse + (row0 + h) * rstride + j0 + (e - h * cnt));
+  for (int e0 = threadIdx.x; e0 < G * cnt; e0 += NT * kMergeLseDepth) {
+    float v[kMergeLseDepth];
+#pragma unroll
+    for (int k = 0; k < kMergeLseDepth; ++k) {
+      const int e = e0 + k * NT;
+      const int h = e / cnt;
+      v[k] = e < G * cnt ? __ldcg(plse + (row0 + h) * rstride + j0 + (e - h * cnt)) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < kMergeLseDepth; ++k)
+      if (e0 + k * NT < G * cnt) wsl[e0 + k * NT] = v[k];
   }
   __syncthreads();
   for (int h = warp; h < G; h += NT / 32) {
@@ -295,10 +305,21 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
         o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
       }
     }
-    for (; sp < cnt; sp += kSplitLanes) {
-      const float4 x = __ldcg(src + (size_t)sp * kVecs);
-      const float w = wsl[h * cnt + sp];
-      o.x += w * x.x; o.y += w * x.y; o.z += w * x.z; o.w += w * x.w;
+    if (sp < cnt) {
+      // the rest (fewer than kMergeDepth rows per lane) in one predicated
+      // round, so it costs one round trip instead of one per row
+      float4 x[kMergeDepth];
+#pragma unroll
+      for (int k = 0; k < kMergeDepth; ++k) {
+        const int s = sp + k * kSplitLanes;
+        x[k] = s < cnt ? __ldcg(src + (size_t)s * kVecs) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < kMergeDepth; ++k) {
+        const int s = sp + k * kSplitLanes;
+        const float w = s < cnt ? wsl[h * cnt + s] : 0.f;
+        o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
+      }
     }
 #pragma unroll
     for (int off = kLanesPerRow; off < 32; off <<= 1) {
