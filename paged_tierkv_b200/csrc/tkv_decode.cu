@@ -240,6 +240,11 @@ __device__ __forceinline__ float* x_lse(const DecodeParams& p, int q, uint32_t e
 #endif
 constexpr int kMergeDepth = TKV_MERGE_DEPTH;
 constexpr int kMergeLseDepth = 4;
+// WARM tiles a consumer warp takes between two removals of the V offset sum
+#ifndef TKV_VCORR_FLUSH
+#define TKV_VCORR_FLUSH 8
+#endif
+constexpr int kVcorrFlush = TKV_VCORR_FLUSH;
 
 template <int D, int NT>
 __device__ __forceinline__ void merge_parts(const float* po, const float* plse, int rstride,
@@ -694,9 +699,13 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
   // WARM V enters the tensor cores as exact fp16 (1024 + code), so acc also
   // collects sum_t w_t (1024 + zero_t) per head (w = P * V scale as the MMA
-  // sees it, fp16); this lane's share of that sum, heads 2t, 2t+1, is
-  // subtracted once before the merge
+  // sees it, fp16); vcorr is this lane's share of that sum, heads 2t, 2t+1.
+  // It is taken out of acc every kVcorrFlush WARM tiles and once more before
+  // the merge.  Left in until the end, the offset (about 1024 x the weights)
+  // grows with the tokens a warp walks, and the fp32 rounding of acc costs the
+  // result bits in proportion.
   float vcorr[2] = {0.f, 0.f};
+  int warm_run = 0;  // WARM tiles since vcorr was last taken out of acc
 
   const int g = lane >> 2;
   const int t = lane & 3;
@@ -995,6 +1004,22 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
               mma_16816(acc[4 * kk + i], a0, a1, a2, a3, pb0, pb1);
             }
           }
+        }
+        if (++warm_run == kVcorrFlush) {
+          warm_run = 0;
+          float vc0 = vcorr[0], vc1 = vcorr[1];
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) {
+            vc0 += __shfl_xor_sync(0xffffffffu, vc0, off);
+            vc1 += __shfl_xor_sync(0xffffffffu, vc1, off);
+          }
+#pragma unroll
+          for (int i = 0; i < Cfg::kKS; ++i) {
+            acc[i][0] -= vc0; acc[i][1] -= vc1;
+            acc[i][2] -= vc0; acc[i][3] -= vc1;
+          }
+          vcorr[0] = 0.f;
+          vcorr[1] = 0.f;
         }
       }
 #if !TKV_EARLY_RELEASE
