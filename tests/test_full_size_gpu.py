@@ -1,7 +1,8 @@
 """Decode attention at the benchmark's full sizes (GPU).
 
 Configuration 5 (32 sequences x 32768 tokens, 32 q / 8 kv heads, head_dim 128,
-block 16, 25 % HOT / 50 % WARM / 25 % COLD, Format R) and configuration 4 (one
+block 16, 25 % HOT / 50 % WARM / 25 % COLD; Format R with fp16 and bf16
+queries, and Format S) and configuration 4 (one
 131072-token context, 10 % / 60 % / 30 %), built as ``bench.py`` builds them,
 decoded through the public API and checked three ways:
 
@@ -24,6 +25,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 from oracle import tierkv_oracle as orc  # noqa: E402
+from paged_tierkv_b200 import ops  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -54,7 +56,7 @@ def _host_sequence(wl, s):
         sel = np.nonzero(states == state)[0]
         remap[sel] = [lut[int(x)] for x in table[sel]]
     p = wl.pools
-    g = lambda t, i: t.index_select(0, picks[i]).cpu().numpy()  # noqa: E731
+    g = lambda t, i: None if t is None else t.index_select(0, picks[i]).cpu().numpy()  # noqa: E731
     return dict(query=wl.query[s:s + 1].float().cpu().numpy(), table=remap[None], states=states[None],
                 lengths=lengths[None], hot_k=g(p.hot_k, 0), hot_v=g(p.hot_v, 0),
                 warm_k=g(p.warm_k, 1), warm_v=g(p.warm_v, 1), k_scale=g(p.k_scale, 1),
@@ -66,7 +68,8 @@ def _oracle(wl, s):
     return orc.decode_attention(h["query"], h["table"], h["states"], h["lengths"], wl.num_blocks,
                                 h["hot_k"], h["hot_v"], h["warm_k"], h["warm_v"], h["k_scale"],
                                 h["k_zero"], h["v_scale"], h["v_zero"], wl.groups, wl.scaling,
-                                fmt="R", dtype=np.float64)
+                                fmt="R" if wl.pools.fmt == ops.FORMAT_R else "S",
+                                dtype=np.float64)
 
 
 def _decode(wl, **kw):
@@ -96,11 +99,15 @@ def _check(wl, sampled):
         torch.testing.assert_close(other.float(), out.float(), atol=SCALE_FRAC * scale, rtol=0)
 
 
-def test_configuration_5_full_size():
+@pytest.mark.parametrize("fmt,qdtype", [("R", torch.float16), ("S", torch.float16),
+                                         ("R", torch.bfloat16)])
+def test_configuration_5_full_size(fmt, qdtype):
     from paged_tierkv_b200 import workloads
     wl = workloads.make_workload(batch=32, q_heads=32, kv_heads=8, head_dim=128, block_size=16,
-                                 ctx_tokens=32768, hot_frac=0.25, seed=0, device="cuda")
+                                 ctx_tokens=32768, hot_frac=0.25, seed=0, device="cuda",
+                                 fmt=ops.FORMAT_R if fmt == "R" else ops.FORMAT_S)
     assert (wl.n_hot, wl.n_warm, wl.n_cold) == (512, 1024, 512)
+    wl.query = wl.query.to(qdtype)
     _check(wl, sampled=(0, 31))
 
 
