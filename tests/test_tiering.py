@@ -67,6 +67,33 @@ def test_transition_walk_equals_block_by_block_loop(path):
         np.testing.assert_array_equal(_apply_cells(fx, plan_f)[name], _apply_cells(fx, plan_s)[name])
 
 
+@pytest.mark.parametrize("kind", ["list", "int32", "uint8", "tensor", "float", "numpy_scalars"])
+def test_plan_input_types_give_the_same_plan(kind):
+    """plan_sync takes the block and state sequences the reference's loop
+    would (lists, arrays, tensors, floats that int() truncates) and plans
+    the same moves and cells for each."""
+    path = FIXTURES[0]
+    fx = _load(path)
+    ref_pool = CompactPoolStub(fx, "cpu")
+    meta = ref_pool.meta
+    phys, want = list(meta["physical_indices"]), list(meta["desired"])
+    ref = tiering.plan_sync(ref_pool, meta["layer"], phys, want)
+    conv = {
+        "list": lambda x: [int(v) for v in x],
+        "int32": lambda x: np.asarray(x, dtype=np.int32),
+        "uint8": lambda x: np.asarray(x, dtype=np.uint8) if max(x) < 256 else np.asarray(x),
+        "tensor": lambda x: torch.tensor([int(v) for v in x], dtype=torch.int64),
+        "float": lambda x: [float(v) + 0.25 for v in x],
+        "numpy_scalars": lambda x: [np.int16(v) for v in x],
+    }[kind]
+    pool = CompactPoolStub(fx, "cpu")
+    plan = tiering.plan_sync(pool, meta["layer"], conv(phys), conv(want))
+    assert pool.bookkeeping() == ref_pool.bookkeeping()
+    assert plan.demotions == ref.demotions and plan.promotions == ref.promotions
+    np.testing.assert_array_equal(plan.state_row, ref.state_row)
+    assert (plan.states, plan.slots, plan.lengths) == (ref.states, ref.slots, ref.lengths)
+
+
 def test_fixtures_cover_slot_reuse_and_growth():
     """The scenarios exercise what the staging and growth paths are for."""
     staged_dem = staged_pro = grown = 0
