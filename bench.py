@@ -292,8 +292,15 @@ def run_reference(a, rank):
         return
     wl = build_workload(a, seed=1234, device="cuda")
     from oracle import tierkv_oracle as orc
+    # One step = one (sequence, kv head) unit over the full context (its G
+    # query heads), about 1/8 of a sequence, so that the default 2000 steps
+    # end in about a minute; bytes are the unit's share of the workload.
     s = host_sample(wl, 1)
-    bytes_per_step = wl.algorithmic_bytes() / wl.batch
+    g = wl.groups
+    s = {k: (v[:, :g] if k == "query" else v[:, :1] if k not in ("table", "states", "lengths")
+             else v) for k, v in s.items()}
+    kv_heads = int(wl.pools.kv_heads)
+    bytes_per_step = wl.algorithmic_bytes() / wl.batch / kv_heads
 
     def once():
         orc.decode_attention(s["query"], s["table"], s["states"], s["lengths"], wl.num_blocks,
@@ -313,9 +320,11 @@ def run_reference(a, rank):
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(el / a.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded N(0,1) K/V/query)", "impl": "reference",
-        "config": {"workload": workload_key(a), **wl.info, "sample": "1 sequence per step"},
+        "config": {"workload": workload_key(a), **wl.info,
+                   "sample": "1 (sequence, kv head) unit per step"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": "1 of 32 sequences per step, all 8 kv heads, full 32k context"},
+                         "sample": f"1 (sequence, kv head) unit per step: {g} query heads over "
+                                   f"the full {wl.info['ctx_tokens']}-token context"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
