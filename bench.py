@@ -198,23 +198,29 @@ def time_device(wl, steps, warmup, dist_on):
 
 def time_e2e(wl, steps, warmup):
     """Same metric through the public API with host buffers: per step the query
-    and the three block tables go host->device from pinned memory and the output
-    comes back device->host, all inside the timed region."""
+    and the three block tables go host->device from pinned memory (one packed
+    copy) and the output comes back device->host, all inside the timed region."""
     from paged_tierkv_b200 import ops
     stream = torch.cuda.current_stream()
-    h_q = wl.query.cpu().pin_memory()
-    h_t = wl.block_table.cpu().pin_memory()
-    h_s = wl.block_states.cpu().pin_memory()
-    h_l = wl.block_lengths.cpu().pin_memory()
+    # the step's inputs (query, block table, states, lengths) sit back to back
+    # in one pinned host buffer and go up in one copy
+    srcs = [wl.query, wl.block_table, wl.block_states, wl.block_lengths]
+    sizes = [x.numel() * x.element_size() for x in srcs]
+    offs = [0]
+    for n in sizes:
+        offs.append(offs[-1] + (n + 255) // 256 * 256)
+    h_pack = torch.zeros(offs[-1], dtype=torch.uint8).pin_memory()
+    d_pack = torch.empty(offs[-1], dtype=torch.uint8, device=wl.query.device)
+    views = []
+    for x, o, n in zip(srcs, offs, sizes):
+        h_pack[o:o + n].view(x.dtype).view(x.shape).copy_(x.cpu())
+        views.append(d_pack[o:o + n].view(x.dtype).view(x.shape))
+    d_q, d_t, d_s, d_l = views
     h_out = torch.empty(wl.query.shape, dtype=torch.float16).pin_memory()
-    d_q, d_t, d_s, d_l = (torch.empty_like(x, device=wl.query.device) for x in (h_q, h_t, h_s, h_l))
     d_out = torch.empty(wl.query.shape, dtype=torch.float16, device=wl.query.device)
 
     def step():
-        d_q.copy_(h_q, non_blocking=True)
-        d_t.copy_(h_t, non_blocking=True)
-        d_s.copy_(h_s, non_blocking=True)
-        d_l.copy_(h_l, non_blocking=True)
+        d_pack.copy_(h_pack, non_blocking=True)
         ops.decode_attention(d_q, d_t, d_s, d_l, wl.pools, wl.num_blocks, wl.groups, wl.scaling,
                              out=d_out)
         h_out.copy_(d_out, non_blocking=True)
@@ -229,7 +235,7 @@ def time_e2e(wl, steps, warmup):
         step()
     e1.record(stream)
     torch.cuda.synchronize()
-    h2d = sum(x.numel() * x.element_size() for x in (h_q, h_t, h_s, h_l))
+    h2d = h_pack.numel()
     d2h = h_out.numel() * h_out.element_size()
     return e0.elapsed_time(e1), h2d, d2h
 
