@@ -337,19 +337,38 @@ int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream
  * with no device-allocation binding of its own.  Same arguments and results as
  * tkv_decode_attention, except that args->workspace / workspace_bytes are
  * ignored: the scratch (split partials, split tickets, chunk counters, score
- * scratch) lives in a library-owned device array of TKV_NOALLOC_SCRATCH_BYTES
- * that every GPU loading the library holds until the process exits.  The call
- * itself allocates nothing (no cudaMalloc/cudaFree, no allocating library
- * routine); it clears the counters it needs on `stream` before the launch.
- * Calls whose tkv_decode_plan() workspace exceeds the array return
- * TKV_ERR_SCRATCH_LIMIT.  The first call on each device looks up the array's
- * device address with cudaGetSymbolAddress while that device is current; make
- * that first call before any stream capture.  All calls on a device share the
- * one array, so calls that overlap on the GPU (different streams, or different
- * host threads) race and must be serialised by the caller.
+ * scratch, the device error word) lives in a library-owned device array of
+ * TKV_NOALLOC_SCRATCH_BYTES that every GPU where the library's module is
+ * loaded holds until the process exits.  The call itself allocates nothing
+ * (no cudaMalloc/cudaFree, no allocating library routine); it clears the
+ * counters it needs on `stream` before the launch.  Calls whose
+ * tkv_decode_plan() workspace exceeds the array return TKV_ERR_SCRATCH_LIMIT.
+ * The first call on a device looks up the array's device address with
+ * cudaGetSymbolAddress while that device is current (see
+ * tkv_noalloc_prepare); make that first call before any stream capture.  All
+ * calls on a device share the one array, so calls that overlap on the GPU
+ * (different streams, or different host threads) race and must be serialised
+ * by the caller.  Device errors (TKV_DEVERR_*) accumulate in the array's error
+ * word until tkv_noalloc_read_device_errors reads and clears them.
  * No counterpart in the reference (its wrapper allocates with torch). */
 int32_t tkv_decode_attention_noalloc(const tkv_pools* pools, const tkv_decode_args* args,
                                      void* stream);
+
+/* Resolves the no-alloc scratch array on `device` (< 0: the current device)
+ * ahead of the first tkv_decode_attention_noalloc call.  Under lazy module
+ * loading (CUDA_MODULE_LOADING=LAZY, the default of recent CUDA runtimes) the
+ * array's TKV_NOALLOC_SCRATCH_BYTES are committed on a device when the
+ * library's module is first loaded there, which this call does: call it at
+ * start-up, before the runtime hands HBM to its own pools and before any
+ * stream capture.  Idempotent; restores the current device.
+ * No counterpart in the reference. */
+int32_t tkv_noalloc_prepare(int32_t device);
+
+/* Reads and clears the device error bits (TKV_DEVERR_*) that no-alloc decode
+ * calls on the current device have recorded in the library's array (the
+ * counterpart of tkv_read_device_errors for a caller workspace).
+ * Synchronizes the stream.  No counterpart in the reference. */
+int32_t tkv_noalloc_read_device_errors(uint32_t* bits_out, void* stream);
 
 #ifdef __cplusplus
 }

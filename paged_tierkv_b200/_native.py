@@ -42,6 +42,8 @@ EXPORTED_SYMBOLS = (
     "tkv_promote_to_hot",
     "tkv_read_device_errors",
     "tkv_decode_attention_noalloc",
+    "tkv_noalloc_prepare",
+    "tkv_noalloc_read_device_errors",
     "tkv_append_hot_tokens",
     "tkv_exchange_bytes",
     "tkv_exchange_alloc",
@@ -166,6 +168,8 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
         "tkv_read_device_errors": ([vp, ctypes.POINTER(ctypes.c_uint32), vp], i32),
         "tkv_decode_attention_noalloc": ([ctypes.POINTER(TkvPools), ctypes.POINTER(TkvDecodeArgs),
                                           vp], i32),
+        "tkv_noalloc_prepare": ([i32], i32),
+        "tkv_noalloc_read_device_errors": ([ctypes.POINTER(ctypes.c_uint32), vp], i32),
         "tkv_append_hot_tokens": ([ctypes.POINTER(TkvPools), i32, i32, i32, vp, vp,
                                    ctypes.POINTER(TkvTableCell), i32, vp], i32),
         "tkv_exchange_bytes": ([i32, i32, i32, i32], ctypes.c_size_t),

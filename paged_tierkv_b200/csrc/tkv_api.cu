@@ -819,22 +819,31 @@ int32_t tkv_read_device_errors(void* workspace, uint32_t* bits_out, void* stream
 // allocations, or a host that reaches this library only through the C ABI with
 // no device-allocation binding.  For them the split partials, split tickets,
 // chunk counters and score scratch live in this fixed array instead.  Every
-// GPU that loads the library holds TKV_NOALLOC_SCRATCH_BYTES of it until the
-// process exits.  Host code must not use `g_tkv_noalloc_scratch` as a device
-// address (on the host the name is only a stand-in); its device address is
-// looked up per device with cudaGetSymbolAddress.
+// GPU that loads the library's module holds TKV_NOALLOC_SCRATCH_BYTES of it
+// until the process exits.  Host code must not use `g_tkv_noalloc_scratch` as
+// a device address (on the host the name is only a stand-in); its device
+// address is looked up per device with cudaGetSymbolAddress.
+//
+// Under lazy module loading (CUDA_MODULE_LOADING=LAZY, the default of recent
+// CUDA runtimes) the array is committed on a device only when this module is
+// first loaded there, which the first cudaGetSymbolAddress does.
+// tkv_noalloc_prepare() does that up front, before the caller hands HBM to its
+// pools; otherwise the first no-alloc call on the device does it.
+//
+// Layout: the workspace layout of tkv_decode_attention over the whole array --
+// [0, 256) the device error word (sticky: set by the kernels, cleared only by
+// tkv_noalloc_read_device_errors), then the counters, then the data regions.
 // ---------------------------------------------------------------------------
 namespace {
 
 __device__ __align__(256) uint8_t g_tkv_noalloc_scratch[TKV_NOALLOC_SCRATCH_BYTES];
 
-// Device address of the scratch array on the current device, resolved on the
-// first call made while that device is current.
-int32_t noalloc_scratch(void** out) {
+// Device address of the scratch array on device `dev`, which must be current;
+// resolved on the first request for that device and kept.
+int32_t noalloc_scratch_on(int dev, void** out) {
   static std::mutex mu;
   static void* addr[kMaxDevices] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TKV_ERR_NO_DEVICE;
+  if (dev < 0 || dev >= kMaxDevices) return TKV_ERR_NO_DEVICE;
   std::lock_guard<std::mutex> lock(mu);
   if (addr[dev] == nullptr) {
     void* p = nullptr;
@@ -846,7 +855,34 @@ int32_t noalloc_scratch(void** out) {
   return TKV_OK;
 }
 
+int32_t noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TKV_ERR_NO_DEVICE;
+  return noalloc_scratch_on(dev, out);
+}
+
 }  // namespace
+
+extern "C" int32_t tkv_noalloc_prepare(int32_t device) {
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return TKV_ERR_NO_DEVICE;
+  const int dev = device < 0 ? cur : device;
+  if (dev != cur && cudaSetDevice(dev) != cudaSuccess) return TKV_ERR_NO_DEVICE;
+  int sms = 0;
+  int32_t st = current_device_sms(&sms);  // rejects devices that are not sm_100
+  void* scratch = nullptr;
+  if (st == TKV_OK) st = noalloc_scratch_on(dev, &scratch);
+  if (dev != cur && cudaSetDevice(cur) != cudaSuccess && st == TKV_OK) st = TKV_ERR_CUDA;
+  return st;
+}
+
+extern "C" int32_t tkv_noalloc_read_device_errors(uint32_t* bits_out, void* stream) {
+  if (!bits_out) return TKV_ERR_INVALID;
+  void* scratch = nullptr;
+  const int32_t st = noalloc_scratch(&scratch);
+  if (st != TKV_OK) return st;
+  return tkv_read_device_errors(scratch, bits_out, stream);
+}
 
 extern "C" int32_t tkv_decode_attention_noalloc(const tkv_pools* pools,
                                                 const tkv_decode_args* args, void* stream) {
@@ -861,11 +897,13 @@ extern "C" int32_t tkv_decode_attention_noalloc(const tkv_pools* pools,
   void* scratch = nullptr;
   st = noalloc_scratch(&scratch);
   if (st != TKV_OK) return st;
-  // The array keeps whatever the previous call left; the error word, split
-  // tickets and chunk counters must start at zero, so clear them first.
-  const size_t counters_end = kAlign + plan.counters_bytes;
-  if (cudaMemsetAsync(scratch, 0, counters_end, reinterpret_cast<cudaStream_t>(stream)) !=
-      cudaSuccess)
+  // The array keeps whatever the previous call left.  The split tickets and
+  // chunk counters must start at zero (a call cut short by a timeout can
+  // leave them set), so they are cleared first; the error word at offset 0
+  // is left alone so that errors stay readable until
+  // tkv_noalloc_read_device_errors clears them.
+  if (cudaMemsetAsync(reinterpret_cast<uint8_t*>(scratch) + kAlign, 0, plan.counters_bytes,
+                      reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
     return TKV_ERR_CUDA;
   tkv_decode_args a = *args;
   a.workspace = scratch;
