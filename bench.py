@@ -160,10 +160,88 @@ def workload_key(a) -> str:
     return f"c5_b{a.batch}_ctx{a.ctx}_h{a.hot_frac:g}{w}_bs{a.block_size}"
 
 
+# The headline workload's shape: Llama-3-8B attention heads, seeded.
+Q_HEADS, KV_HEADS, HEAD_DIM, SEED = 32, 8, 128, 1234
+
+
+def host_tier_counts(num_blocks: int, hot_frac: float, warm_frac: float | None = None):
+    """(n_hot, n_warm, n_cold) of one sequence, computed on the host without
+    importing the package: the same rule as workloads.tier_counts (a CPU test
+    checks that they agree)."""
+    n_hot = min(num_blocks, max(1, int(round(hot_frac * num_blocks))))
+    rest = num_blocks - n_hot
+    n_warm = int(round(rest * 2.0 / 3.0)) if warm_frac is None else \
+        min(rest, int(round(warm_frac * num_blocks)))
+    return n_hot, n_warm, rest - n_warm
+
+
+def host_first_states(num_blocks: int, n_hot: int, n_warm: int, seed: int) -> np.ndarray:
+    """Tier states of sequence 0 drawn exactly as workloads.assign_tiers draws
+    them (the same CPU generator and permutation), on the host."""
+    gen = torch.Generator().manual_seed(seed)
+    states = np.full(num_blocks, 2, np.int32)
+    states[0] = 0
+    if n_hot > 1:
+        states[num_blocks - (n_hot - 1):] = 0
+    middle = np.arange(1, num_blocks - (n_hot - 1))
+    pick = torch.randperm(middle.size, generator=gen)[:n_warm].numpy()
+    states[middle[pick]] = 1
+    return states
+
+
+def host_bytes_per_step(batch, nb, n_hot, n_warm, bs, d, hkv, hq) -> int:
+    """Algorithmic HBM bytes of one decode call (Workload.algorithmic_bytes on the host)."""
+    per_seq_head = n_hot * bs * 4 * d + n_warm * (bs * 2 * d + 8 * bs)
+    return batch * (hkv * per_seq_head + 12 * nb + 2 * hq * d * 2)
+
+
+def bench_config(a, world: int) -> dict:
+    """The `config` of the headline line, identical for both arms (it depends
+    on the arguments and the world size only)."""
+    nb = -(-a.ctx // a.block_size)
+    n_hot, n_warm, n_cold = host_tier_counts(nb, a.hot_frac, getattr(a, "warm_frac", None))
+    return {"workload": workload_key(a), "batch": a.batch, "q_heads": Q_HEADS,
+            "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "block_size": a.block_size,
+            "ctx_tokens": a.ctx, "hot_frac": a.hot_frac, "blocks_per_seq": nb,
+            "hot_blocks": n_hot, "warm_blocks": n_warm, "cold_blocks": n_cold, "seed": SEED,
+            "warm_format": "R (uint8 + fp16 scale/zero)",
+            "parallelism": f"dp{world} (independent batches, no collective)",
+            "l2": "inputs >> 126 MB L2; no flush needed",
+            "bytes_per_step_per_gpu": host_bytes_per_step(a.batch, nb, n_hot, n_warm, a.block_size,
+                                                          HEAD_DIM, KV_HEADS, Q_HEADS)}
+
+
+def host_unit_sample(a, seed: int):
+    """One (sequence, kv head) unit of the headline workload built on the host:
+    sequence 0's tier layout (same seed and draws as our arm), N(0, 1) fp16
+    K/V and query from a host generator, WARM blocks quantized by the oracle's
+    restatement of quantize_fp16_to_int8 (bit-exact with the reference).
+    Nothing here touches a GPU or this package."""
+    from oracle import tierkv_oracle as orc
+    bs, d, g = a.block_size, HEAD_DIM, Q_HEADS // KV_HEADS
+    nb = -(-a.ctx // bs)
+    n_hot, n_warm, _ = host_tier_counts(nb, a.hot_frac, getattr(a, "warm_frac", None))
+    states = host_first_states(nb, n_hot, n_warm, seed)
+    lengths = np.full(nb, bs, np.int32)
+    lengths[-1] = a.ctx - (nb - 1) * bs
+    rng = np.random.default_rng(seed)
+    table = np.full(nb, -1, np.int32)
+    hot_idx, warm_idx = np.nonzero(states == 0)[0], np.nonzero(states == 1)[0]
+    table[hot_idx] = rng.permutation(hot_idx.size)
+    table[warm_idx] = rng.permutation(warm_idx.size)
+    f16 = lambda *shape: rng.standard_normal(shape, dtype=np.float32).astype(np.float16)  # noqa: E731
+    hot_k, hot_v = f16(max(1, hot_idx.size), 1, bs, d), f16(max(1, hot_idx.size), 1, bs, d)
+    wk, ks, kz = orc.quantize_rows_r(f16(max(1, warm_idx.size), 1, bs, d))
+    wv, vs, vz = orc.quantize_rows_r(f16(max(1, warm_idx.size), 1, bs, d))
+    return dict(query=f16(1, g, d), table=table[None], states=states[None], lengths=lengths[None],
+                num_blocks=nb, hot_k=hot_k, hot_v=hot_v, warm_k=wk, warm_v=wv, k_scale=ks,
+                k_zero=kz, v_scale=vs, v_zero=vz, groups=g, scaling=d ** -0.5)
+
+
 def build_workload(a, seed, device):
     from paged_tierkv_b200 import workloads
-    return workloads.make_workload(batch=a.batch, q_heads=32, kv_heads=8, head_dim=128,
-                                   block_size=a.block_size, ctx_tokens=a.ctx,
+    return workloads.make_workload(batch=a.batch, q_heads=Q_HEADS, kv_heads=KV_HEADS,
+                                   head_dim=HEAD_DIM, block_size=a.block_size, ctx_tokens=a.ctx,
                                    hot_frac=a.hot_frac, warm_frac=getattr(a, "warm_frac", None),
                                    seed=seed, device=device)
 
@@ -291,27 +369,26 @@ def blas_threads() -> int:
 
 
 # --------------------------------------------------------------------------- arms
-def run_reference(a, rank):
+def run_reference(a, rank, world):
     """The reference arm: the CPU restatement of the reference's PyTorch tiered
-    path (the reference itself is Python and cannot travel), on host cores."""
+    path (tierkv_triton.py:708-820; the reference itself is Python, has no
+    packaging and cannot travel to the GPU box), on the host cores.  Its
+    inputs are built on the host (host_unit_sample); it imports nothing of
+    this package and never touches a GPU."""
     if rank != 0:
         return
-    wl = build_workload(a, seed=1234, device="cuda")
     from oracle import tierkv_oracle as orc
     # One step = one (sequence, kv head) unit over the full context (its G
-    # query heads), about 1/8 of a sequence, so that the default 2000 steps
-    # end in about a minute; bytes are the unit's share of the workload.
-    s = host_sample(wl, 1)
-    g = wl.groups
-    s = {k: (v[:, :g] if k == "query" else v[:, :1] if k not in ("table", "states", "lengths")
-             else v) for k, v in s.items()}
-    kv_heads = int(wl.pools.kv_heads)
-    bytes_per_step = wl.algorithmic_bytes() / wl.batch / kv_heads
+    # query heads), 1/8 of a sequence, so that the default 2000 steps end in
+    # about a minute; its bytes are the unit's share of the workload's.
+    s = host_unit_sample(a, SEED)
+    cfg = bench_config(a, world)
+    bytes_per_step = cfg["bytes_per_step_per_gpu"] / a.batch / KV_HEADS
 
     def once():
-        orc.decode_attention(s["query"], s["table"], s["states"], s["lengths"], wl.num_blocks,
+        orc.decode_attention(s["query"], s["table"], s["states"], s["lengths"], s["num_blocks"],
                              s["hot_k"], s["hot_v"], s["warm_k"], s["warm_v"], s["k_scale"],
-                             s["k_zero"], s["v_scale"], s["v_zero"], wl.groups, wl.scaling,
+                             s["k_zero"], s["v_scale"], s["v_zero"], s["groups"], s["scaling"],
                              dtype=np.float32)
     for _ in range(a.warmup):
         once()
@@ -321,16 +398,18 @@ def run_reference(a, rank):
     el = time.perf_counter() - t0
     gbs = bytes_per_step * a.steps / el / 1e9
     cores = blas_threads()
+    sample = (f"1 (sequence, kv head) unit per step: {s['groups']} query heads over the full "
+              f"{a.ctx}-token context of sequence 0 (its tier layout drawn with our arm's seed; "
+              "N(0,1) K/V drawn on the host, WARM blocks quantized by the oracle's "
+              "quantize_fp16_to_int8); GB/s = the unit's share of the step's bytes / time")
     line = {
-        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": a.gpus,
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(el / a.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded N(0,1) K/V/query)", "impl": "reference",
-        "config": {"workload": workload_key(a), **wl.info,
-                   "sample": "1 (sequence, kv head) unit per step"},
+        "config": cfg,
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"1 (sequence, kv head) unit per step: {g} query heads over "
-                                   f"the full {wl.info['ctx_tokens']}-token context"},
+                         "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -384,15 +463,16 @@ def run_ours(a, rank, world, dist_on, device):
                "sample": f"1 of {wl.batch} sequences (8 kv heads, full context), {reps} reps, "
                          f"{sec_per:.2f} s each"}
     tr = ncu_traffic(workload_key(a))
+    cfg = bench_config(a, world)
+    if cfg["bytes_per_step_per_gpu"] != bytes_step:
+        raise RuntimeError("host byte count disagrees with the workload's")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(total_ms / a.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic (seeded N(0,1) K/V/query; WARM blocks demoted on device)",
-        "config": {"workload": workload_key(a), **wl.info, "warm_format": "R (uint8 + fp16 scale/zero)",
-                   "parallelism": f"dp{world} (independent batches, no collective)",
-                   "splits": splits, "l2": "inputs >> 126 MB L2; no flush needed",
-                   "bytes_per_step_per_gpu": bytes_step},
+        "config": cfg,
+        "splits": splits,
         "tokens_per_s": round(wl.batch * world / (32 * total_ms / a.steps * 1e-3), 1),
         "tokens_per_s_note": "attention-only decode tokens/s for a 32-layer model (batch / (32 x step))",
         "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -400,7 +480,11 @@ def run_ours(a, rank, world, dist_on, device):
         "gpu_launches": a.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": tr, "kernel": "tkv::decode_kernel<128,16,R,f16>",
+                     "traffic": tr,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                        "batch-4 launch of this mix, x 8 to batch 32 "
+                                        "(profiles/decode_c5_h025_bs16.md)") if tr else None,
+                     "kernel": "tkv::decode_kernel<128,16,R,f16>",
                      "kernel_ms": round(kernel_ms, 4)},
         "cpu_baseline": cpu,
         "clocks": clocks,
@@ -597,12 +681,24 @@ def run_demote(a, rank, world, dist_on, device):
     }), flush=True)
 
 
+def _compact_pool_stand_in():
+    """The test suite's stand-in for the reference's compact pool and block
+    manager (tests/compact_pool.py): the reference's own classes are not
+    installed on the GPU box."""
+    tests = os.path.join(ROOT, "tests")
+    if tests not in sys.path:
+        sys.path.insert(0, tests)
+    import compact_pool
+    return compact_pool
+
+
 def _tiering_layer(device, blocks=2048, n_hot=512, n_warm=1024, seed=17):
     """One layer of configuration 5's sequence shape in a CompactPool: 2048
     blocks appended through the fused append, then tiered by one tick into
     512 HOT (sink + recent) / 1024 WARM / 512 COLD."""
     import types
-    from paged_tierkv_b200 import compact_pool, tiering
+    from paged_tierkv_b200 import tiering
+    compact_pool = _compact_pool_stand_in()
     bs, hkv, d = 16, 8, 128
     pool = compact_pool.CompactPool(num_layers=1, block_size=bs, kv_heads=hkv, head_dim=d,
                                     max_blocks_per_layer=blocks + 64, max_hot_slots=blocks + 64,
@@ -782,7 +878,8 @@ def run_prefill_store(a, rank, device):
     tensor work (row copies and tail fills for HOT blocks, the torch
     quantizer's ops for WARM blocks, one element write per table cell)."""
     import types
-    from paged_tierkv_b200 import _native, compact_pool, ops, tiering
+    from paged_tierkv_b200 import _native, ops, tiering
+    compact_pool = _compact_pool_stand_in()
     _native.load(build_if_missing=True)
     if rank != 0:
         return
@@ -1032,7 +1129,7 @@ def main():
     a.gpus = world
     try:
         if a.impl == "reference":
-            run_reference(a, rank)
+            run_reference(a, rank, world)
         elif a.config == "c4":
             run_c4(a, rank, world, dist_on, device)
         elif a.config == "demote":

@@ -1,13 +1,16 @@
-"""A compact tiered pool for the batched tick and the fused append.
+"""Test and benchmark stand-in for the reference's compact pool.
 
-The reference's ``CompactTieredKVTensorPool`` (tierkv_policy.py:701-1365) is
-the pool a runtime normally hands to ``tiering``; this class carries the same
-attributes and slot-allocation behaviour -- LIFO free lists, growth by chunks
-of slots (``_alloc_*_slot`` / ``_free_*_slot`` 897-915, ``_grow_*_slots``
-857-895), the per-physical-block dictionaries and storage sets, the
-[num_layers, max_blocks_per_layer] int32 block tables -- so the batched paths
-can run (and be measured) where the reference is not installed.  It holds no
-policy and moves no data itself.
+Not part of the product: the reference's ``CompactTieredKVTensorPool``
+(tierkv_policy.py:701-1365) and its ``BlockManager`` (csrc/block_manager.cpp)
+stay as they are and are what a runtime hands to ``paged_tierkv_b200.tiering``.
+This class carries the same attributes and slot-allocation behaviour -- LIFO
+free lists, growth by chunks of slots (``_alloc_*_slot`` / ``_free_*_slot``
+897-915, ``_grow_*_slots`` 857-895), the per-physical-block dictionaries and
+storage sets, the [num_layers, max_blocks_per_layer] int32 block tables -- so
+the batched paths can be tested against the reference-made fixtures and
+measured (``bench.py --config tick / append / prefill_store``) on the GPU box,
+where the reference is not installed.  It holds no policy and moves no data
+itself.
 """
 
 from __future__ import annotations

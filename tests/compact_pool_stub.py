@@ -2,7 +2,7 @@
 
 Test infrastructure only.  The fixtures (tests/golden/make_tiering_golden.py)
 are made by the reference's own ``CompactTieredKVTensorPool``, so their
-"after" states pin both ``paged_tierkv_b200.compact_pool`` and the code under
+"after" states pin both the ``compact_pool`` stand-in and the code under
 test.
 """
 
@@ -13,7 +13,7 @@ import json
 import numpy as np
 import torch
 
-from paged_tierkv_b200.compact_pool import BlockAllocator, CompactPool, LayerState  # noqa: F401
+from compact_pool import BlockAllocator, CompactPool, LayerState  # noqa: F401
 
 
 def CompactPoolStub(fixture, device="cpu") -> CompactPool:
