@@ -314,6 +314,92 @@ def plan_splits(pools: TieredPools, batch: int, num_heads: int, num_key_value_gr
     return int(splits.value)
 
 
+def workspace_error_word(device_index: int | None = None, stream=None) -> torch.Tensor:
+    """The device error word (int32 [1]) of the workspace that decode calls on
+    ``stream`` (default: the current stream) of ``device_index`` use."""
+    dev = torch.cuda.current_device() if device_index is None else int(device_index)
+    st = _stream(stream, dev)
+    ws = workspace_for(torch.device("cuda", dev), st.value or 0, 1 << 16)
+    return ws[:4].view(torch.int32)
+
+
+class TierKVDeviceError(N.TierKVError):
+    """Error bits (TKV_DEVERR_*) that a decode launch recorded on the device:
+    ``bits & TKV_DEVERR_BAD_SLOT`` -- a HOT/WARM table entry outside its pool
+    (read as zeros); ``bits & TKV_DEVERR_TIMEOUT`` -- a bounded wait gave up
+    (a peer that never published its partials, or a stalled pipeline), so the
+    output of that call is not valid."""
+
+    def __init__(self, bits: int, call: int, what: str = "decode"):
+        self.bits = int(bits)
+        self.call = int(call)
+        names = [n for b, n in ((N.TKV_DEVERR_BAD_SLOT, "out-of-pool slot"),
+                                (N.TKV_DEVERR_TIMEOUT, "bounded wait timed out")) if self.bits & b]
+        super().__init__(f"{what} call {self.call} recorded device error 0x{self.bits:x} "
+                         f"({', '.join(names) or 'unknown'})")
+
+
+class DeviceErrorWatch:
+    """Reports the device error bits of decode calls without synchronizing.
+
+    ``record(word)`` enqueues, on the current stream, a 4-byte copy of the
+    call's error word into pinned host memory and an event behind it (every
+    ``period``-th call; none while a CUDA graph is being captured).
+    ``poll()`` reads the copies whose events have completed, never waiting,
+    and raises :class:`TierKVDeviceError` for the first one that holds error
+    bits; it then clears the error word on the device (the bits are sticky
+    there) and drops the copies made before.  Polling before each call thus
+    reports an error one call (or a few, while the GPU runs behind) after the
+    call that recorded it.  ``check()`` waits for every outstanding copy, so
+    it reports everything recorded so far; call it after the last call.
+    While a CUDA graph is being captured nothing is recorded or polled, so
+    calls replayed from a graph are not watched: after replays, read the
+    word itself (``read_device_errors``)."""
+
+    def __init__(self, depth: int = 8, period: int = 1, what: str = "decode"):
+        self.depth = int(depth)
+        self.period = max(1, int(period))
+        self.what = what
+        self._host = None
+        self._slots: list = []      # (event, slot index, call number, error word)
+        self._next_slot = 0
+        self.calls = 0
+
+    def record(self, word: torch.Tensor) -> None:
+        self.calls += 1
+        if self.calls % self.period or torch.cuda.is_current_stream_capturing():
+            return
+        if self._host is None:
+            self._host = torch.zeros(self.depth, dtype=torch.int32).pin_memory()
+        if len(self._slots) >= self.depth:   # the GPU is `depth` recorded calls behind
+            self._slots[0][0].synchronize()
+            self.poll()
+            if len(self._slots) >= self.depth:
+                self._slots.pop(0)
+        slot = self._next_slot
+        self._next_slot = (slot + 1) % self.depth
+        self._host[slot:slot + 1].copy_(word, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._slots.append((ev, slot, self.calls, word))
+
+    def poll(self) -> None:
+        if not self._slots or torch.cuda.is_current_stream_capturing():
+            return  # event queries are not permitted while a graph is captured
+        while self._slots and self._slots[0][0].query():
+            _, slot, call, word = self._slots.pop(0)
+            bits = int(self._host[slot])
+            if bits:
+                word.zero_()
+                self._slots.clear()
+                raise TierKVDeviceError(bits, call, self.what)
+
+    def check(self) -> None:
+        if self._slots and not torch.cuda.is_current_stream_capturing():
+            self._slots[-1][0].synchronize()
+        self.poll()
+
+
 def read_device_errors(device=None, stream=None) -> int:
     """Read and clear the device error bits of the current stream's workspace."""
     st = _stream(stream)

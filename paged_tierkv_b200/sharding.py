@@ -82,6 +82,14 @@ class ContextShardedDecode:
         self.local_fn = local_fn or _local_cuda
         self.merge_fn = merge_fn or _merge_cuda
         self._bufs: dict = {}
+        # device errors of the local decode launches (an out-of-pool slot),
+        # reported one call behind without synchronizing
+        self.watch = ops.DeviceErrorWatch(what="context-sharded decode")
+
+    def check(self) -> None:
+        """Raise ``ops.TierKVDeviceError`` for device errors recorded by any
+        call so far (waits for the outstanding error-word copies)."""
+        self.watch.check()
 
     def _buffers(self, rows: int, d: int, world: int, device):
         key = (rows, d, world, str(device))
@@ -102,11 +110,16 @@ class ContextShardedDecode:
         world = dist.get_world_size(self.group)
         b, hq, d = query.shape
         rows = b * hq
+        watched = query.is_cuda and self.local_fn is _local_cuda
+        if watched:
+            self.watch.poll()
         local, gathered = self._buffers(rows, d, world, query.device)
         o_local = local[:rows * d].view(b, hq, d)
         lse_local = local[rows * d:].view(b, hq)
         scores = self.local_fn(query, block_table, block_states, block_lengths, pools, num_blocks,
                                num_key_value_groups, scaling, o_local, lse_local, return_scores)
+        if watched:
+            self.watch.record(ops.workspace_error_word(query.device.index))
         if world > 1:
             dist.all_gather_into_tensor(gathered, local, group=self.group)
             parts = gathered.view(world, rows * (d + 1))
@@ -151,7 +164,8 @@ class PeerExchange:
         self._mapped = []
         # device_epoch: the epoch lives in device memory and every launch
         # advances it, so CUDA graph replays see a new epoch every call
-        self.epoch_t = (torch.ones(1, dtype=torch.int32, device=torch.cuda.current_device())
+        self.epoch_device = torch.device("cuda", torch.cuda.current_device())
+        self.epoch_t = (torch.ones(1, dtype=torch.int32, device=self.epoch_device)
                         if device_epoch else None)
         if inboxes is not None:
             # caller-provided inbox addresses (e.g. several inboxes in one process)
@@ -199,6 +213,39 @@ class PeerExchange:
             x.inbox[q] = ptr
         return x
 
+    def resync(self) -> None:
+        """Bring the ranks' epochs back into step after a timed-out exchange.
+
+        Collective: every rank of the group calls it, between calls, once any
+        rank has raised a timeout (the application agrees on that, e.g. with
+        its own all-reduce of an error flag).  Waits for this rank's GPU work,
+        meets the other ranks, and moves every rank to one epoch beyond the
+        largest epoch any rank has used, so no flag in any inbox (all of them
+        stamped with older epochs) can satisfy the next call's wait before its
+        peer has published for it."""
+        torch.cuda.synchronize()
+        if self.epoch_t is not None:
+            cur = int(self.epoch_t.item())
+        else:
+            cur = int(self.epoch)
+        nxt = cur + 2
+        if self._own is not None:  # a process group: agree on the largest epoch
+            import torch.distributed as dist
+            t = torch.tensor([nxt], dtype=torch.int64, device=self.epoch_device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            nxt = int(t.item())
+        nxt &= 0xFFFFFFFF
+        if nxt == 0:
+            nxt = 1
+        if self.epoch_t is not None:
+            self.epoch_t.fill_(nxt)
+        else:
+            self.epoch = nxt - 1  # next() hands out nxt
+        if self._own is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+
     def close(self) -> None:
         lib = self._N.load()
         if self._own is not None:
@@ -221,15 +268,30 @@ class P2PContextDecode:
 
     def __init__(self, exchange: PeerExchange):
         self.exchange = exchange
+        # device errors of the launches (a peer that did not publish within
+        # the exchange's timeout, an out-of-pool slot), reported one call
+        # behind without synchronizing
+        self.watch = ops.DeviceErrorWatch(what="exchange decode")
+
+    def check(self) -> None:
+        """Raise ``ops.TierKVDeviceError`` for device errors recorded by any
+        eager call so far (waits for the outstanding error-word copies).
+        Calls replayed from a CUDA graph are not watched: after replays, read
+        the stream's error word with ``ops.read_device_errors``."""
+        self.watch.check()
 
     def __call__(self, query: torch.Tensor, block_table: torch.Tensor, block_states: torch.Tensor,
                  block_lengths: torch.Tensor, pools, num_blocks, num_key_value_groups: int,
                  scaling: float, *, out_dtype=torch.float16, return_scores: bool = False,
                  out: torch.Tensor | None = None) -> ShardResult:
-        from . import ops
+        """Raises ``ops.TierKVDeviceError`` before launching when an earlier
+        call's launch recorded a device error; after a timeout every rank must
+        call ``exchange.resync()`` before the next call."""
+        self.watch.poll()
         o, scores, lse = ops.decode_attention(query, block_table, block_states, block_lengths, pools,
                                               num_blocks, num_key_value_groups, scaling,
                                               return_scores=return_scores, return_lse=True,
                                               out=out, out_dtype=out_dtype,
                                               exchange=self.exchange.next())
+        self.watch.record(ops.workspace_error_word(query.device.index))
         return ShardResult(o, lse, scores)

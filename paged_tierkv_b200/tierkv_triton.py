@@ -20,7 +20,7 @@ from __future__ import annotations
 import torch
 
 from . import _native
-from .ops import FORMAT_R, TieredPools, decode_attention
+from .ops import FORMAT_R, DeviceErrorWatch, TieredPools, decode_attention, workspace_error_word
 
 
 def _require_backend():
@@ -38,12 +38,29 @@ def _require_backend():
 # sets of contiguous tensors are kept: the cached entry then holds the caller's
 # own tensor objects, so their ids cannot be reused while it lives, and a
 # non-contiguous pool, which is copied on every call, is never served from a
-# stale copy.
+# stale copy.  The key holds each tensor's address, shape and strides, so a
+# tensor changed in place (resize_ / set_ that keep its address) is checked
+# and described anew.
 _POOLS_CACHE: list = []
+
+# Device errors of the kernel (a HOT/WARM table entry outside its pool, read
+# as zeros -- undefined behaviour in the reference's kernel) are raised as
+# ops.TierKVDeviceError without synchronizing: every ERROR_CHECK_PERIOD-th
+# call copies the error word to pinned memory behind the launch, and a later
+# call raises once that copy has landed.  check_device_errors() waits for it.
+ERROR_CHECK_PERIOD = 16
+_WATCH = DeviceErrorWatch(period=ERROR_CHECK_PERIOD, what="tierkv_decode_attention")
+
+
+def check_device_errors() -> None:
+    """Raise ops.TierKVDeviceError for device errors recorded so far by the
+    calls this module has checked (waits for the outstanding copies)."""
+    _WATCH.check()
 
 
 def _pools_of(tensors) -> TieredPools:
-    key = tuple(id(t) for t in tensors) + tuple(0 if t is None else t.data_ptr() for t in tensors)
+    key = tuple((id(t), t.data_ptr(), t.shape, t.stride()) if t is not None else None
+                for t in tensors)
     for k, pools in _POOLS_CACHE:
         if k == key:
             return pools
@@ -102,10 +119,15 @@ def tierkv_decode_attention(
     pools = _pools_of((hot_k_pool, hot_v_pool, warm_k_pool, warm_v_pool, k_scale, k_zero, v_scale,
                        v_zero))
     _, num_heads, _, head_dim = query_states.shape
+    _WATCH.poll()
     out, scores, _ = decode_attention(
         query_states, block_table.reshape(1, -1), block_states.reshape(1, -1),
         block_lengths.reshape(1, -1), pools, int(num_blocks), int(num_key_value_groups),
         float(scaling), return_scores=bool(return_scores))
+    if (_WATCH.calls + 1) % _WATCH.period == 0:
+        _WATCH.record(workspace_error_word(query_states.device.index))
+    else:
+        _WATCH.calls += 1
     out = out.view(1, 1, num_heads, head_dim)
     if return_scores:
         return out, scores[0]

@@ -131,7 +131,14 @@ def test_per_sequence_block_counts():
     _close(out, ref)
 
 
-def test_bf16_query_and_outputs():
+@pytest.mark.parametrize("splits", [0, 1])
+def test_bf16_query_and_outputs(splits):
+    """bf16 queries: the attention itself (fp32 output) is checked at the
+    north star's 2e-3 / 1e-2 against the float64 oracle of the bf16-rounded
+    query; the bf16 output is then checked separately as a rounding of that
+    fp32 result -- bit-identical for one split (the same launch math), and
+    within one bf16 ulp (2^-8 relative, plus the fp32 run-to-run spread of
+    dynamic chunk claiming) for the planned split count."""
     from paged_tierkv_b200 import ops
     case = make_case(seed=13, batch=2, q_heads=32, kv_heads=8, head_dim=128, num_blocks=30)
     case["query"] = (case["query"].astype(np.float32) * 3.0).astype(np.float16)
@@ -141,14 +148,19 @@ def test_bf16_query_and_outputs():
     # the oracle sees the bf16-rounded query
     case_b = dict(case, query=q.float().cpu().numpy())
     ref_b, _, _ = oracle_decode(case_b)
-    out, _, _ = ops.decode_attention(q, d["block_table"], d["block_states"], d["block_lengths"],
-                                     d["pools"], d["num_blocks"], case["groups"], case["scaling"])
+    args = (d["block_table"], d["block_states"], d["block_lengths"], d["pools"], d["num_blocks"],
+            case["groups"], case["scaling"])
+    out32_b, _, _ = ops.decode_attention(q, *args, out_dtype=torch.float32, num_splits=splits)
+    out, _, _ = ops.decode_attention(q, *args, num_splits=splits)
     torch.cuda.synchronize()
     assert out.dtype == torch.bfloat16
-    _close(out, ref_b, atol=4e-3, rtol=1.6e-2)  # + bf16 output rounding (2^-9)
-    out32, _, _ = ops.decode_attention(d["query"], d["block_table"], d["block_states"],
-                                       d["block_lengths"], d["pools"], d["num_blocks"],
-                                       case["groups"], case["scaling"], out_dtype=torch.float32)
+    _close(out32_b, ref_b)  # the attention: 2e-3 abs / 1e-2 rel
+    rounded = out32_b.to(torch.bfloat16)
+    if splits == 1:
+        assert torch.equal(out.view(torch.int16), rounded.view(torch.int16))
+    else:
+        torch.testing.assert_close(out.float(), out32_b, atol=1e-5, rtol=2.0 ** -8)
+    out32, _, _ = ops.decode_attention(d["query"], *args, out_dtype=torch.float32)
     torch.cuda.synchronize()
     _close(out32, ref, atol=1e-3, rtol=5e-3)
 
@@ -174,6 +186,32 @@ def test_out_of_pool_slot_reads_as_zero_and_is_reported():
     out, _, _ = _run(dict(case, block_table=bad))
     _close(out, ref)
     assert ops.read_device_errors() & 0x1
+
+
+def test_out_of_pool_slot_raises_through_the_shim():
+    """The drop-in shim raises ops.TierKVDeviceError for an out-of-pool slot
+    without synchronizing the calls (a later call, or check_device_errors)."""
+    from paged_tierkv_b200 import ops
+    from paged_tierkv_b200 import tierkv_triton as shim
+    case = make_case(seed=21, batch=1, q_heads=8, kv_heads=2, head_dim=64, num_blocks=6,
+                     states=[0, 1, 0, 0, 1, 0])
+    d = to_device(case)
+    p = d["pools"]
+    bad = d["block_table"].clone()
+    bad[0, 3] = p.hot_k.shape[0] + 7
+    q = d["query"][:, :, None, :]
+    shim.check_device_errors()
+    ops.read_device_errors()  # clear
+    with pytest.raises(ops.TierKVDeviceError) as err:
+        for _ in range(4 * shim.ERROR_CHECK_PERIOD):
+            shim.tierkv_decode_attention(q, bad[0], d["block_states"][0], d["block_lengths"][0],
+                                         p.hot_k, p.hot_v, p.warm_k, p.warm_v, p.k_scale, p.k_zero,
+                                         p.v_scale, p.v_zero, num_blocks=6, num_key_value_groups=4,
+                                         scaling=case["scaling"])
+        shim.check_device_errors()
+    assert err.value.bits & 0x1
+    shim.check_device_errors()
+    assert ops.read_device_errors() == 0
 
 
 DECODE_CASES = sorted(os.path.basename(p)[7:-4] for p in glob.glob(os.path.join(GOLDEN, "decode_*.npz")))

@@ -132,6 +132,57 @@ def test_peer_that_never_publishes_times_out():
     assert ops.read_device_errors() & N.TKV_DEVERR_TIMEOUT
 
 
+def test_timeout_raises_from_the_sharding_api_and_resync_recovers():
+    """A peer that never publishes: the call comes back (bounded wait), the
+    next call raises TierKVDeviceError with the timeout bit before it
+    launches, and after resync() the exchange works again with the peer's
+    partials published for the new epoch."""
+    from paged_tierkv_b200 import _native as N
+    from paged_tierkv_b200 import ops, sharding
+    nb, cut, D = 40, 17, 128
+    case = make_case(seed=93, batch=1, q_heads=32, kv_heads=8, head_dim=D, num_blocks=nb,
+                     max_blocks=nb)
+    ref, _, _ = oracle_decode(case)
+    shards = []
+    for sl in (slice(0, cut), slice(cut, nb)):
+        shards.append(dict(case, block_table=np.ascontiguousarray(case["block_table"][:, sl]),
+                           block_states=np.ascontiguousarray(case["block_states"][:, sl]),
+                           block_lengths=np.ascontiguousarray(case["block_lengths"][:, sl])))
+    d0, d1 = to_device(shards[0]), to_device(shards[1])
+    rows, units, world = 32, 8, 2
+    box0, box1 = _inbox(world, rows, units, D), _inbox(world, rows, units, D)
+    ex = sharding.PeerExchange(rows_cap=rows, units_cap=units, head_dim=D,
+                               inboxes=[box0.data_ptr(), box1.data_ptr()], rank=0,
+                               timeout_ns=20_000_000)
+    dec = sharding.P2PContextDecode(ex)
+    ops.read_device_errors()  # clear
+    args = lambda dd: (dd["query"], dd["block_table"], dd["block_states"],  # noqa: E731
+                       dd["block_lengths"], dd["pools"], cut, case["groups"], case["scaling"])
+    dec(*args(d0))  # nothing publishes rank 1's partials: the wait runs out
+    with pytest.raises(ops.TierKVDeviceError) as err:
+        dec.check()
+    assert err.value.bits & N.TKV_DEVERR_TIMEOUT and err.value.call == 1
+    dec.check()  # reported once; the device word was cleared
+    ex.resync()
+    x_epoch = ex.epoch + 1  # the epoch the next call uses
+    assert x_epoch >= 3
+    flags_b, lse_off = _layout(world, rows, units, D)
+    o1 = torch.empty((1, 32, D), dtype=torch.float32, device="cuda")
+    from paged_tierkv_b200 import ops as o
+    _, _, l1 = o.decode_attention(d1["query"], d1["block_table"], d1["block_states"],
+                                  d1["block_lengths"], d1["pools"], nb - cut, case["groups"],
+                                  case["scaling"], out=o1, out_dtype=torch.float32, return_lse=True)
+    par = x_epoch & 1
+    box0[flags_b:lse_off].view(torch.float32).view(2, rows, world, D)[par, :, 1, :] = o1.view(rows, D)
+    box0[lse_off:lse_off + 2 * rows * world * 4].view(torch.float32).view(2, rows, world)[par, :, 1] = \
+        l1.view(rows)
+    torch.cuda.synchronize()
+    box0[:flags_b].view(torch.int32)[units:2 * units] = x_epoch
+    res = dec(*args(d0))
+    dec.check()
+    np.testing.assert_allclose(res.out.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+
+
 def test_exchange_argument_checks():
     from paged_tierkv_b200 import sharding
     case = make_case(seed=91, batch=2, q_heads=8, kv_heads=2, head_dim=64, num_blocks=6)
