@@ -1,9 +1,12 @@
 """Decode attention at the benchmark's full sizes (GPU).
 
-Configuration 5 (32 sequences x 32768 tokens, 32 q / 8 kv heads, head_dim 128,
-block 16, 25 % HOT / 50 % WARM / 25 % COLD; Format R with fp16 and bf16
-queries, and Format S) and configuration 4 (one
-131072-token context, 10 % / 60 % / 30 %), built as ``bench.py`` builds them,
+Configuration 5 (32 sequences x 32768 tokens, 32 q / 8 kv heads, head_dim 128;
+block 16 at 25 % HOT / 50 % WARM / 25 % COLD with Format R for fp16 and bf16
+queries and with Format S; the rest of its sweep -- hot fractions 1.0, 0.5,
+0.1 at block 16 and all four at block 32, the non-HOT blocks split 2:1
+WARM:COLD), configuration 3's attention shape (64 sequences x 8192 tokens,
+20 % / 60 % / 20 %) and configuration 4 (one 131072-token context,
+10 % / 60 % / 30 %), built as ``bench.py`` builds them,
 decoded through the public API and checked three ways:
 
 * against the float64 oracle on sampled sequences (the oracle finishes one
@@ -109,6 +112,27 @@ def test_configuration_5_full_size(fmt, qdtype):
     assert (wl.n_hot, wl.n_warm, wl.n_cold) == (512, 1024, 512)
     wl.query = wl.query.to(qdtype)
     _check(wl, sampled=(0, 31))
+
+
+@pytest.mark.parametrize("block_size,hot_frac", [(16, 1.0), (16, 0.5), (16, 0.1), (32, 1.0),
+                                                 (32, 0.5), (32, 0.25), (32, 0.1)])
+def test_configuration_5_sweep_full_size(block_size, hot_frac):
+    from paged_tierkv_b200 import workloads
+    wl = workloads.make_workload(batch=32, q_heads=32, kv_heads=8, head_dim=128,
+                                 block_size=block_size, ctx_tokens=32768, hot_frac=hot_frac,
+                                 seed=int(hot_frac * 100) + block_size, device="cuda")
+    nb = 32768 // block_size
+    assert (wl.n_hot, wl.n_warm, wl.n_cold) == workloads.tier_counts(nb, hot_frac)
+    _check(wl, sampled=(5,))
+
+
+def test_configuration_3_attention_full_size():
+    from paged_tierkv_b200 import workloads
+    wl = workloads.make_workload(batch=64, q_heads=32, kv_heads=8, head_dim=128, block_size=16,
+                                 ctx_tokens=8192, hot_frac=0.2, warm_frac=0.6, seed=33,
+                                 device="cuda")
+    assert (wl.n_hot, wl.n_warm, wl.n_cold) == (102, 307, 103)
+    _check(wl, sampled=(0, 63))
 
 
 def test_configuration_4_full_context():
