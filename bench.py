@@ -13,6 +13,17 @@ far larger than the 126 MB L2, so no flush is needed between steps.
 For N > 1 the script runs under torchrun: each rank owns its own batch of 32
 sequences (data-parallel, no collective on the data path; weak scaling) and
 `value` is the bytes of all ranks over the slowest rank's device time.
+
+The same line carries two strong-scaling objects (fixed total work split over
+the N ranks, each replayed from a CUDA graph, max over ranks):
+  c4 -- configuration 4, one 131072-token context over 32 layers, each layer's
+        blocks split into byte-balanced contiguous ranges; ms per step with
+        the partials exchanged inside the decode launch over peer memory,
+        the NCCL all-gather + merge variant beside it, the local shard decode
+        alone, and layer-0 parity against the unsharded one-rank output;
+  c3 -- configuration 3's attention, 64 sequences x 8192 tokens (20/60/20)
+        split data-parallel; aggregate tokens/s and per-GPU GB/s.
+(`--no-scaling-extras` leaves them out.)
 """
 
 from __future__ import annotations
@@ -71,6 +82,10 @@ def parse():
                          "decode launch (p2p) or NCCL all-gather + merge launch (nccl)")
     ap.add_argument("--no-graph", action="store_true",
                     help="c4: launch every layer from Python instead of replaying a CUDA graph")
+    ap.add_argument("--no-scaling-extras", action="store_true",
+                    help="leave out the c4 (one 131072-token context sharded over the GPUs) and "
+                         "c3 (64 x 8192-token sequences split over the GPUs) strong-scaling "
+                         "objects of the headline line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -342,16 +357,16 @@ def host_sample(wl, seqs):
                 v_scale=g(p.v_scale, wi), v_zero=g(p.v_zero, wi))
 
 
-def cpu_oracle_rate(wl, seconds, seqs=1):
-    """GB/s of the CPU restatement of the reference path on a bounded sample."""
+def cpu_oracle_rate(s, seconds):
+    """GB/s of the CPU restatement of the reference path on a bounded sample
+    (``host_sample`` of the workload plus its byte count and geometry)."""
     from oracle import tierkv_oracle as orc
-    s = host_sample(wl, seqs)
-    bytes_per_call = wl.algorithmic_bytes() * seqs / wl.batch
+    bytes_per_call = s["bytes"]
     reps, t0 = 0, time.perf_counter()
     while True:
-        orc.decode_attention(s["query"], s["table"], s["states"], s["lengths"], wl.num_blocks,
+        orc.decode_attention(s["query"], s["table"], s["states"], s["lengths"], s["num_blocks"],
                              s["hot_k"], s["hot_v"], s["warm_k"], s["warm_v"], s["k_scale"],
-                             s["k_zero"], s["v_scale"], s["v_zero"], wl.groups, wl.scaling,
+                             s["k_zero"], s["v_scale"], s["v_zero"], s["groups"], s["scaling"],
                              dtype=np.float32)
         reps += 1
         el = time.perf_counter() - t0
@@ -437,6 +452,18 @@ def run_ours(a, rank, world, dist_on, device):
     all_bytes = bytes_step * world * a.steps
     value = all_bytes / (total_ms * 1e-3) / 1e9
     e2e_val = all_bytes / (e2e_ms * 1e-3) / 1e9
+    batch = wl.batch
+    cpu_sample = None
+    if rank == 0 and not a.no_cpu_baseline:
+        cpu_sample = dict(host_sample(wl, 1), bytes=bytes_step / batch, num_blocks=wl.num_blocks,
+                          groups=wl.groups, scaling=wl.scaling)
+    del wl
+    torch.cuda.empty_cache()
+    extras = {}
+    if not a.no_scaling_extras:
+        # the two strong-scaling curves: fixed total work split over the ranks
+        extras["c4"] = c4_object(a, rank, world, dist_on, device)
+        extras["c3"] = c3_object(a, rank, world, dist_on, device)
     sweep = None
     if a.sweep:
         sweep = []
@@ -457,10 +484,10 @@ def run_ours(a, rank, world, dist_on, device):
     kernel_ms = statistics.mean(per)
     achieved = bytes_step / (kernel_ms * 1e-3) / 1e9
     cpu = None
-    if not a.no_cpu_baseline:
-        gbs, sec_per, reps = cpu_oracle_rate(wl, a.cpu_seconds)
+    if cpu_sample is not None:
+        gbs, sec_per, reps = cpu_oracle_rate(cpu_sample, a.cpu_seconds)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": blas_threads(), "kind": "port",
-               "sample": f"1 of {wl.batch} sequences (8 kv heads, full context), {reps} reps, "
+               "sample": f"1 of {batch} sequences (8 kv heads, full context), {reps} reps, "
                          f"{sec_per:.2f} s each"}
     tr = ncu_traffic(workload_key(a))
     cfg = bench_config(a, world)
@@ -473,7 +500,7 @@ def run_ours(a, rank, world, dist_on, device):
         "data": "synthetic (seeded N(0,1) K/V/query; WARM blocks demoted on device)",
         "config": cfg,
         "splits": splits,
-        "tokens_per_s": round(wl.batch * world / (32 * total_ms / a.steps * 1e-3), 1),
+        "tokens_per_s": round(batch * world / (32 * total_ms / a.steps * 1e-3), 1),
         "tokens_per_s_note": "attention-only decode tokens/s for a 32-layer model (batch / (32 x step))",
         "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
@@ -489,70 +516,31 @@ def run_ours(a, rank, world, dist_on, device):
         "cpu_baseline": cpu,
         "clocks": clocks,
     }
+    line.update(extras)
     if sweep is not None:
         line["sweep"] = sweep
     print(json.dumps(line), flush=True)
 
 
-def run_c4(a, rank, world, dist_on, device):
-    """Configuration 4: batch 1, 131072 tokens, 32 layers, 10 % HOT / 60 % WARM /
-    30 % COLD; every layer's blocks are split into byte-balanced contiguous
-    ranges, one per GPU; per layer one decode launch, one all-gather of the
-    packed (o, LSE) partials and one merge launch.  Strong scaling."""
-    from paged_tierkv_b200 import _native, sharding, workloads
-    _native.load(build_if_missing=True)
-    ctx, bs, d, hkv, hq = 131072, a.block_size, 128, 8, 32
-    nb = ctx // bs
-    n_hot, n_warm, _ = workloads.tier_counts(nb, 0.10, 0.60)
-    layers = []
-    total_bytes = 0
-    for layer in range(a.layers):
-        states = workloads.assign_tiers(1, nb, n_hot, n_warm, seed=5000 + layer)
-        lengths = torch.full((1, nb), bs, dtype=torch.int32)
-        ranges = workloads.balanced_block_ranges(states, world, bs, d)
-        s, e = ranges[rank]
-        wl = workloads.materialize(states[:, s:e].contiguous(), lengths[:, s:e].contiguous(),
-                                   q_heads=hq, kv_heads=hkv, head_dim=d, block_size=bs,
-                                   seed=7000 + 97 * layer + rank, device=device)
-        layers.append(wl)
-        total_bytes += wl.algorithmic_bytes()
-    ex = None
-    if world > 1 and a.exchange == "p2p":
-        ex = sharding.PeerExchange(rows_cap=hq, units_cap=hkv, head_dim=d, device_epoch=True)
-        dec = sharding.P2PContextDecode(ex)
-    else:
-        dec = sharding.ContextShardedDecode()
-    out = torch.empty((1, hq, d), dtype=torch.float16, device=device)
-
-    def step():
-        for wl in layers:
-            if world == 1:
-                workloads.decode(wl, out=out)
-            elif ex is not None:
-                dec(wl.query, wl.block_table, wl.block_states, wl.block_lengths, wl.pools,
-                    wl.num_blocks, wl.groups, wl.scaling, out=out)
-            else:
-                dec(wl.query, wl.block_table, wl.block_states, wl.block_lengths, wl.pools,
-                    wl.num_blocks, wl.groups, wl.scaling)
-
-    # The whole 32-layer step (decode launches, all-gathers, merges) is captured
-    # once in a CUDA graph on a dedicated stream and replayed; warm-up runs on
-    # that stream first so no allocation happens during capture.
-    side = torch.cuda.Stream(device=device)
+def _timed_graph(step, steps, warmup, dist_on, device, graph=True, side=None):
+    """Device ms per call of `step`, captured once in a CUDA graph on a side
+    stream (warm-up first, so nothing is allocated during capture) and
+    replayed; max over ranks.  Every rank makes the same collective calls."""
+    side = side or torch.cuda.Stream(device=device)
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
-        for _ in range(max(1, a.warmup)):
+        for _ in range(max(1, warmup)):
             step()
     torch.cuda.synchronize()
-    graph = None
-    if not a.no_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
             step()
         torch.cuda.synchronize()
-    run = graph.replay if graph is not None else step
+    run = g.replay if g is not None else step
     with torch.cuda.stream(side):
-        for _ in range(a.warmup):
+        for _ in range(warmup):
             run()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
@@ -560,22 +548,194 @@ def run_c4(a, rank, world, dist_on, device):
             torch.distributed.barrier()
         torch.cuda.synchronize()
         e0.record(side)
-        for _ in range(a.steps):
+        for _ in range(steps):
             run()
         e1.record(side)
         torch.cuda.synchronize()
     if dist_on:
         torch.distributed.barrier()
-    del graph
+    del g
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=device)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t[0])
+
+
+def c4_layers(a, rank, world, device, layers):
+    """Configuration 4's per-rank shards: for each layer, the byte-balanced
+    contiguous block range of this rank, materialized as its own pools."""
+    from paged_tierkv_b200 import workloads
+    ctx, bs, d, hkv, hq = 131072, a.block_size, HEAD_DIM, KV_HEADS, Q_HEADS
+    nb = ctx // bs
+    n_hot, n_warm, _ = workloads.tier_counts(nb, 0.10, 0.60)
+    out, total = [], 0
+    for layer in range(layers):
+        states = workloads.assign_tiers(1, nb, n_hot, n_warm, seed=5000 + layer)
+        lengths = torch.full((1, nb), bs, dtype=torch.int32)
+        s, e = workloads.balanced_block_ranges(states, world, bs, d)[rank]
+        wl = workloads.materialize(states[:, s:e].contiguous(), lengths[:, s:e].contiguous(),
+                                   q_heads=hq, kv_heads=hkv, head_dim=d, block_size=bs,
+                                   seed=7000 + 97 * layer + rank, device=device)
+        out.append(wl)
+        total += wl.algorithmic_bytes()
+    return out, total, (ctx, bs, nb, n_hot, n_warm)
+
+
+def c4_parity(a, rank, world, device):
+    """Layer-0 parity of the sharded decode against one rank: every rank
+    builds the whole 131072-token layer from the same seed and decodes its
+    byte-balanced block range with the exchange (or, for one rank, the whole
+    range); rank 0 also decodes the unsharded layer.  Returns the largest
+    difference relative to the output's scale (rank 0), and whether any rank
+    recorded a device error."""
+    from paged_tierkv_b200 import ops, sharding, workloads
+    bs, d = a.block_size, HEAD_DIM
+    wl = workloads.make_workload(batch=1, q_heads=Q_HEADS, kv_heads=KV_HEADS, head_dim=d,
+                                 block_size=bs, ctx_tokens=131072, hot_frac=0.10, warm_frac=0.60,
+                                 seed=5000, device=device)
+    s, e = workloads.balanced_block_ranges(wl.block_states.cpu(), world, bs, d)[rank]
+    ex = None
+    if world > 1:
+        ex = sharding.PeerExchange(rows_cap=Q_HEADS, units_cap=KV_HEADS, head_dim=d)
+        res = sharding.P2PContextDecode(ex)(
+            wl.query, wl.block_table[:, s:e], wl.block_states[:, s:e], wl.block_lengths[:, s:e],
+            wl.pools, e - s, wl.groups, wl.scaling, out_dtype=torch.float32)
+        out = res.out
+    else:
+        out, _, _ = workloads.decode(wl, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    err = ops.read_device_errors()
     if ex is not None:
         ex.close()
-    t = torch.tensor([e0.elapsed_time(e1), float(total_bytes)], dtype=torch.float64, device=device)
-    if dist_on:
-        tb = t.clone()
+    rel = 0.0
+    if rank == 0:
+        full, _, _ = workloads.decode(wl, out_dtype=torch.float32, num_splits=1)
+        torch.cuda.synchronize()
+        rel = float((out - full).abs().max() / full.abs().max())
+    t = torch.tensor([rel, float(err)], dtype=torch.float64, device=device)
+    if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        torch.distributed.all_reduce(tb, op=torch.distributed.ReduceOp.SUM)
-        t[1] = tb[1]
-    ms = float(t[0]) / a.steps
+    del wl
+    torch.cuda.empty_cache()
+    return float(t[0]), int(t[1])
+
+
+def c4_measure(a, rank, world, dist_on, device, steps, warmup, exchanges):
+    """Configuration 4 (batch 1, 131072 tokens, 32 layers, 10 % HOT / 60 % WARM
+    / 30 % COLD; block-range sharded over the ranks): ms per 32-layer step,
+    replayed from a CUDA graph, for the local shard decode alone and for each
+    exchange variant ("p2p": partials exchanged over peer memory inside the
+    decode launch; "nccl": all-gather of the packed (o, LSE) + merge launch)."""
+    from paged_tierkv_b200 import ops, sharding, workloads
+    layers, total_bytes, (ctx, bs, nb, n_hot, n_warm) = c4_layers(a, rank, world, device, a.layers)
+    out16 = torch.empty((1, Q_HEADS, HEAD_DIM), dtype=torch.float16, device=device)
+    out32 = torch.empty((1, Q_HEADS, HEAD_DIM), dtype=torch.float32, device=device)
+    lse = torch.empty((1, Q_HEADS), dtype=torch.float32, device=device)
+
+    def local():
+        for wl in layers:
+            workloads.decode(wl, out=out32 if world > 1 else out16,
+                             out_dtype=torch.float32 if world > 1 else None,
+                             return_lse=lse if world > 1 else False)
+
+    res = {"local_ms": _timed_graph(local, steps, warmup, dist_on, device, not a.no_graph)}
+    for kind in (exchanges if world > 1 else ()):
+        ex = None
+        if kind == "p2p":
+            ex = sharding.PeerExchange(rows_cap=Q_HEADS, units_cap=KV_HEADS, head_dim=HEAD_DIM,
+                                       device_epoch=True)
+            dec = sharding.P2PContextDecode(ex)
+        else:
+            dec = sharding.ContextShardedDecode()
+
+        def step(dec=dec, ex=ex):
+            for wl in layers:
+                args = (wl.query, wl.block_table, wl.block_states, wl.block_lengths, wl.pools,
+                        wl.num_blocks, wl.groups, wl.scaling)
+                if ex is not None:
+                    dec(*args, out=out16)
+                else:
+                    dec(*args)
+        side = torch.cuda.Stream(device=device)
+        ops.read_device_errors(stream=side)
+        res[f"{kind}_ms"] = _timed_graph(step, steps, warmup, dist_on, device, not a.no_graph,
+                                         side=side)
+        torch.cuda.synchronize()
+        res[f"{kind}_device_errors"] = ops.read_device_errors(stream=side)
+        if ex is not None:
+            ex.close()
+    t = torch.tensor([float(total_bytes)], dtype=torch.float64, device=device)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+    del layers
+    torch.cuda.empty_cache()
+    return res, float(t[0]), (ctx, bs, nb, n_hot, n_warm)
+
+
+def c4_object(a, rank, world, dist_on, device, steps=50, warmup=5):
+    """The configuration-4 strong-scaling entry of the headline line."""
+    res, all_bytes, (ctx, bs, nb, n_hot, n_warm) = c4_measure(
+        a, rank, world, dist_on, device, steps, warmup, ("p2p", "nccl"))
+    rel, perr = c4_parity(a, rank, world, device)
+    ms = res.get("p2p_ms", res["local_ms"])
+    obj = {"workload": f"c4_ctx{ctx}_bs{bs}_l{a.layers}", "hot_blocks": n_hot, "warm_blocks": n_warm,
+           "partition": "byte-balanced contiguous block ranges, one per rank",
+           "ms_per_step": round(ms, 4), "tokens_per_s": round(1000.0 / ms, 2),
+           "GBps_all_gpus": round(all_bytes / (ms * 1e-3) / 1e9, 1),
+           "local_decode_ms_per_step": round(res["local_ms"], 4),
+           "steps": steps, "cuda_graph": not a.no_graph,
+           "parity_layer0_max_rel_vs_1_rank": rel, "parity_device_errors": perr}
+    if world > 1:
+        obj.update({
+            "exchange": "p2p: peer-memory stores + epoch flags inside the decode launch",
+            "exchange_us_per_layer": round((res["p2p_ms"] - res["local_ms"]) * 1e3 / a.layers, 2),
+            "nccl_ms_per_step": round(res["nccl_ms"], 4),
+            "nccl_tokens_per_s": round(1000.0 / res["nccl_ms"], 2),
+            "nccl_us_per_layer_over_local": round((res["nccl_ms"] - res["local_ms"]) * 1e3 / a.layers, 2),
+            "device_errors": res["p2p_device_errors"] | res["nccl_device_errors"]})
+    return obj
+
+
+def c3_object(a, rank, world, dist_on, device, steps=20, warmup=5, distinct_layers=4):
+    """Configuration 3's attention at fixed total work: 64 sequences x 8192
+    tokens, 20 % HOT / 60 % WARM / 20 % COLD, split data-parallel over the
+    ranks (no collective); one step = 32 layer calls per rank (cycling through
+    `distinct_layers` separately materialized layers, so repeated calls do
+    not find their layer in L2), replayed from a CUDA graph; max over ranks."""
+    from paged_tierkv_b200 import sharding, workloads
+    sl = sharding.dp_slice(64, rank, world)
+    n = sl.stop - sl.start
+    wls = [workloads.make_workload(batch=n, q_heads=Q_HEADS, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+                                   block_size=16, ctx_tokens=8192, hot_frac=0.2, warm_frac=0.6,
+                                   seed=600 + 31 * rank + i, device=device)
+           for i in range(distinct_layers)]
+    outs = [torch.empty((n, Q_HEADS, HEAD_DIM), dtype=torch.float16, device=device) for _ in wls]
+
+    def step():
+        for layer in range(32):
+            k = layer % len(wls)
+            workloads.decode(wls[k], out=outs[k])
+    ms = _timed_graph(step, steps, warmup, dist_on, device, not a.no_graph)
+    per_rank_bytes = 32 * wls[0].algorithmic_bytes()
+    del wls, outs
+    torch.cuda.empty_cache()
+    return {"workload": "c3_b64_ctx8192_h0.2_w0.6_bs16_l32", "sequences_total": 64,
+            "sequences_per_gpu": n, "ms_per_step": round(ms, 4),
+            "tokens_per_s": round(64 / (ms * 1e-3), 1),
+            "GBps_per_gpu": round(per_rank_bytes / (ms * 1e-3) / 1e9, 1),
+            "steps": steps, "scaling": "strong", "distinct_layers": distinct_layers,
+            "cuda_graph": not a.no_graph,
+            "note": "attention only: the model's projections, MLP and weights are outside this path"}
+
+
+def run_c4(a, rank, world, dist_on, device):
+    """`--config c4`: configuration 4 as its own line (strong scaling)."""
+    from paged_tierkv_b200 import _native
+    _native.load(build_if_missing=True)
+    kinds = (a.exchange,)
+    res, all_bytes, (ctx, bs, nb, n_hot, n_warm) = c4_measure(
+        a, rank, world, dist_on, device, a.steps, a.warmup, kinds)
+    ms = res.get(f"{a.exchange}_ms", res["local_ms"])
     if rank != 0:
         return
     line = {
@@ -587,10 +747,12 @@ def run_c4(a, rank, world, dist_on, device):
                    "warm_blocks": n_warm, "partition": "byte-balanced contiguous block ranges",
                    "exchange": ("none" if world == 1 else
                                 "peer-memory stores + epoch flags inside the decode launch"
-                                if ex is not None else "NCCL all_gather of packed (o, lse) per layer"),
+                                if a.exchange == "p2p" else
+                                "NCCL all_gather of packed (o, lse) per layer"),
                    "cuda_graph": not a.no_graph},
-        "GBps_all_gpus": round(float(t[1]) / (ms * 1e-3) / 1e9, 1),
-        "gpu_launches": a.steps * a.layers * (1 if (world == 1 or ex is not None) else 2),
+        "local_decode_ms_per_step": round(res["local_ms"], 4),
+        "GBps_all_gpus": round(all_bytes / (ms * 1e-3) / 1e9, 1),
+        "gpu_launches": a.steps * a.layers * (1 if (world == 1 or a.exchange == "p2p") else 2),
     }
     print(json.dumps(line), flush=True)
 
