@@ -61,6 +61,10 @@ struct TileInfo {
 #ifndef TKV_EARLY_RELEASE
 #define TKV_EARLY_RELEASE 1
 #endif
+// Launch decode kernels with programmatic stream serialization (see launch_one).
+#ifndef TKV_PDL
+#define TKV_PDL 1
+#endif
 
 
 template <int D, int BS, int FMT, int QT>
@@ -464,6 +468,18 @@ __device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, siz
   }
 }
 
+// Chunk c of a (sequence, kv head) with nb blocks and chunks of cmax blocks:
+// blocks [base, base + cnt), front to back.  (Measured on B200 and rejected:
+// handing the chunks out back to front or alternately from both ends, which
+// makes every CTA stream HOT tiles at once and then WARM tiles at once
+// instead of a mix, +4 % on configuration 4; short chunks for the last part
+// of each context, -2 % on configuration 4 but +1 % on configuration 5 and
+// +9 % on configuration 3 at 8 sequences.)
+__device__ __forceinline__ void chunk_span(int c, int nb, int cmax, int& base, int& cnt) {
+  base = c * cmax;
+  cnt = max(0, min(cmax, nb - base));
+}
+
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent byte of 1024.0
 
 template <int D, int BS, int FMT, int QT>
@@ -496,6 +512,26 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   const int G = p.groups;
   const int Hq = p.num_heads;
 
+  // Set-up that reads no global memory (barriers, descriptor prefetch) runs
+  // before the dependency wait, so that under programmatic dependent launch it
+  // overlaps the previous kernel's tail; everything a previous kernel may have
+  // written -- tables, block counts, query, workspace counters, the exchange
+  // epoch -- is read after it.
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    fence_mbar_init();
+  } else if (threadIdx.x == 32) {
+    prefetch_tensormap(&tm_hk);
+    prefetch_tensormap(&tm_hv);
+    prefetch_tensormap(&tm_wk);
+    prefetch_tensormap(&tm_wv);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+
   int nb = p.nb_dev ? p.nb_dev[seq] : p.nb_uniform;
   nb = max(0, min(nb, p.max_blocks));
   // Work is handed out in chunks of p.chunk (8, 16 or 32) blocks, one block
@@ -514,12 +550,13 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   const int32_t* srow = p.states + (size_t)seq * p.table_stride;
   const int32_t* lrow = p.lengths + (size_t)seq * p.table_stride;
   // the table entries of the producer's first chunk are requested before the
-  // prologue; (nbase, ncnt) is the chunk whose entries are loading
-  int nbase = dynamic ? split * cmax : 0;
-  int ncnt = 0;
+  // prologue; chunk `nchunk` = blocks [nbase, nbase + ncnt) is the one whose
+  // entries are loading
+  int nchunk = dynamic ? split : 0;
+  int nbase = 0, ncnt = 0;
   int nslot = -1, nstate = 2, nlen = 0;
   if (warp == 0) {
-    ncnt = max(0, min(cmax, nb - nbase));
+    chunk_span(nchunk, nb, cmax, nbase, ncnt);
     if (lane < ncnt) {
       nslot = __ldg(trow + nbase + lane);
       nstate = __ldg(srow + nbase + lane);
@@ -528,10 +565,6 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   }
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < Cfg::kStages; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
-    }
     misc[0] = 0;
     misc[1] = 0;
     // the exchange epoch of this call (see x_o): a value, never an address,
@@ -539,18 +572,11 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     uint32_t epoch = p.x_epoch;
     if (p.x_world > 0 && p.x_epoch_dev != nullptr) epoch = __ldcg(p.x_epoch_dev);
     misc[2] = (int)epoch;
-    fence_mbar_init();
   }
   __syncthreads();  // barriers initialised; the consumers stage the query below
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tensormap(&tm_hk);
-      prefetch_tensormap(&tm_hv);
-      prefetch_tensormap(&tm_wk);
-      prefetch_tensormap(&tm_wv);
-    }
     int tile = 0;
     int cold = 0;
     bool fail = false;
@@ -567,12 +593,11 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
         // claims beyond the first chunks of all splits
         int c = 0;
         if (lane == 0) c = (int)atomicAdd(chunk_ctr, 1u);
-        nbase = (__shfl_sync(0xffffffffu, c, 0) + p.splits) * cmax;
-        ncnt = max(0, min(cmax, nb - nbase));
+        nchunk = __shfl_sync(0xffffffffu, c, 0) + p.splits;
       } else {
-        nbase = base + ncnt;
-        ncnt = max(0, min(cmax, nb - nbase));
+        ++nchunk;
       }
+      chunk_span(nchunk, nb, cmax, nbase, ncnt);
       nslot = -1;
       nstate = 2;
       nlen = 0;
@@ -733,8 +758,14 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       }
       const TileInfo ti = info[s];
       if (ti.state < 0) break;
-      const uint32_t kb = smem_u32(stages + s * Cfg::kStageBytes);
+      // every shared-memory fragment address of this tile depends on a token
+      // taken after the wait, so no load of the stage (or of the staged
+      // query) is scheduled before the data has landed
+      const uint32_t tok = wait_token();
+      const uint32_t kb = after(smem_u32(stages + s * Cfg::kStageBytes), tok);
       const uint32_t vb = kb + Cfg::kHotBytes;
+      const uint32_t sqh_t = after(sqh_u, tok);
+      const uint32_t sqw_t = after(sqw_u, tok);
       const __half* ms = reinterpret_cast<const __half*>(meta + s * Cfg::kMetaBytes);
       const bool hot = ti.state == 0;
 
@@ -750,7 +781,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
 #pragma unroll
           for (int m = 0; m < Cfg::kKS / 2; ++m) {
             uint32_t b00, b01, b10, b11;
-            load_qfrag<D>(sqh_u, lane, m, b00, b01, b10, b11);
+            load_qfrag<D>(sqh_t, lane, m, b00, b01, b10, b11);
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               const int ks = 2 * m + kk;
@@ -800,7 +831,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
 #pragma unroll
           for (int m = 0; m < Cfg::kKS / 2; ++m) {
             uint32_t bq[2][2];
-            load_qfrag<D>(sqw_u, lane, m, bq[0][0], bq[0][1], bq[1][0], bq[1][1]);
+            load_qfrag<D>(sqw_t, lane, m, bq[0][0], bq[0][1], bq[1][0], bq[1][1]);
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               const int ks = 2 * m + kk;
@@ -876,6 +907,18 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
         }
       }
 #if TKV_EARLY_RELEASE
+      // the stage's data must be in registers before the stage is handed
+      // back: the logits (K) and the V fragments are inputs of the release
+#pragma unroll
+      for (int u = 0; u < Cfg::kSub; ++u) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hold(x[u][j]);
+#pragma unroll
+        for (int kk = 0; kk < D / 64; ++kk)
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (hot || j < 8) hold(vf[u][kk][j]);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[s]);
 #endif
@@ -1190,8 +1233,21 @@ static cudaError_t launch_one(const DecodeParams& p, const CUtensorMap maps[4],
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit, std::memory_order_relaxed);
   }
-  dim3 grid(p.splits, p.kv_heads, p.batch);
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p, maps[0], maps[1], maps[2], maps[3]);
+  // Programmatic dependent launch: the kernel may start while the previous
+  // kernel of the stream finishes (it waits with griddepcontrol.wait before
+  // touching memory that kernel could have written).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, p.kv_heads, p.batch);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = TKV_PDL ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1], maps[2], maps[3]);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -48,6 +48,15 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// Programmatic dependent launch (sm_90+): let the next kernel of the stream
+// be scheduled now (its CTAs take SM slots as this grid's CTAs exit), and wait
+// until the previous kernel of the stream has completed and its memory is
+// visible.  Both are no-ops for a launch without the programmatic attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -126,45 +135,60 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 }
 
 // ---- shared-memory loads ------------------------------------------------------
+// These are plain (non-volatile) asm so the compiler may schedule them freely,
+// e.g. issue every fragment load of a tile before its first MMA instead of
+// in program order.  They declare no memory dependency, so a caller must tie
+// their addresses to whatever makes the data valid (see wait_token / after)
+// and keep their results alive across a stage release (see hold).
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                         uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
+  asm("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(addr));
 }
 
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   uint32_t v;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
 
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   uint2 v;
-  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
   return v;
 }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
+  asm("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "r"(addr));
   return v;
 }
+
+// An opaque zero produced in program order (volatile) after everything before
+// it, e.g. an mbarrier wait; `after(addr, token)` makes an address depend on
+// it, so loads through that address cannot be hoisted above the wait.
+__device__ __forceinline__ uint32_t wait_token() {
+  uint32_t t;
+  asm volatile("mov.u32 %0, 0;" : "=r"(t)::"memory");
+  return t;
+}
+__device__ __forceinline__ uint32_t after(uint32_t x, uint32_t token) {
+  asm("add.u32 %0, %0, %1;" : "+r"(x) : "r"(token));
+  return x;
+}
+// Keeps a register's producer (a load) ahead of the next volatile asm, e.g.
+// the mbarrier arrive that hands a stage back to the producer.
+__device__ __forceinline__ void hold(uint32_t x) { asm volatile("" ::"r"(x)); }
+__device__ __forceinline__ void hold(float x) { asm volatile("" ::"f"(x)); }
 
 // ---- tensor-core fragments ----------------------------------------------------
 // D[16x8] += A[16x16] (row) * B[16x8] (col), fp16 inputs, fp32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -174,7 +198,7 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
 // Transposes the 8x8 b16 matrix held one row-pair per thread.
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
