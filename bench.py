@@ -14,6 +14,12 @@ For N > 1 the script runs under torchrun: each rank owns its own batch of 32
 sequences (data-parallel, no collective on the data path; weak scaling) and
 `value` is the bytes of all ranks over the slowest rank's device time.
 
+On one GPU the line also carries `c1` (configuration 1, the parity op: us per
+call, eager and graph-replayed), `c2` (configuration 2's attention at the
+TinyLlama shape, 22 layers, L2 flushed per step), `demote` (2^20-tile
+HOT->WARM demotion and promotion) and `sweep` (configuration 5's hot
+fractions at block 16 and 32); `--no-single-extras` leaves them out.
+
 The same line carries two strong-scaling objects (fixed total work split over
 the N ranks, each replayed from a CUDA graph, max over ranks):
   c4 -- configuration 4, one 131072-token context over 32 layers, each layer's
@@ -64,7 +70,8 @@ def parse():
                          "3's 20/60/20 mix")
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--sweep", action="store_true",
-                    help="also time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32")
+                    help="time hot fractions 1.0/0.5/0.25/0.1 at block 16 and 32 also on several "
+                         "GPUs (one GPU: always, unless --no-single-extras)")
     ap.add_argument("--config", choices=["c5", "c4", "demote", "tick", "append", "prefill",
                                          "prefill_store"],
                     default="c5",
@@ -86,6 +93,9 @@ def parse():
                     help="leave out the c4 (one 131072-token context sharded over the GPUs) and "
                          "c3 (64 x 8192-token sequences split over the GPUs) strong-scaling "
                          "objects of the headline line")
+    ap.add_argument("--no-single-extras", action="store_true",
+                    help="one GPU: leave out the c1 (parity op), c2 (TinyLlama-shape attention), "
+                         "demote and sweep objects of the headline line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -464,20 +474,13 @@ def run_ours(a, rank, world, dist_on, device):
         # the two strong-scaling curves: fixed total work split over the ranks
         extras["c4"] = c4_object(a, rank, world, dist_on, device)
         extras["c3"] = c3_object(a, rank, world, dist_on, device)
-    sweep = None
-    if a.sweep:
-        sweep = []
-        for bs in (16, 32):
-            for h in (1.0, 0.5, 0.25, 0.1):
-                a2 = argparse.Namespace(**{**vars(a), "hot_frac": h, "block_size": bs})
-                w2 = build_workload(a2, seed=99 + rank, device=device)
-                tm, pl, _ = time_device(w2, a.steps, a.warmup, dist_on)
-                b2 = w2.algorithmic_bytes()
-                gbs = b2 / (statistics.mean(pl) * 1e-3) / 1e9
-                sweep.append({"block_size": bs, "hot_frac": h, "bytes_per_call": b2,
-                              "ms_per_call": round(statistics.mean(pl), 4), "GBps": round(gbs, 1)})
-                del w2
-                torch.cuda.empty_cache()
+    if world == 1 and not a.no_single_extras:
+        # the other single-GPU measurements of the benchmark configurations
+        extras["c1"] = c1_object(device)
+        extras["c2"] = c2_object(device)
+        extras["demote"] = demote_object(a, device)
+    if (world == 1 and not a.no_single_extras) or a.sweep:
+        extras["sweep"] = sweep_object(a, rank, dist_on, device)
     if rank != 0:
         return
     peak, peak_kind = hbm_peak()
@@ -517,8 +520,6 @@ def run_ours(a, rank, world, dist_on, device):
         "clocks": clocks,
     }
     line.update(extras)
-    if sweep is not None:
-        line["sweep"] = sweep
     print(json.dumps(line), flush=True)
 
 
@@ -728,6 +729,123 @@ def c3_object(a, rank, world, dist_on, device, steps=20, warmup=5, distinct_laye
             "note": "attention only: the model's projections, MLP and weights are outside this path"}
 
 
+def _flush_l2(buf):
+    buf.add_(1)  # a write larger than the 126 MB L2 evicts it
+
+
+def c1_object(device, calls=200):
+    """Configuration 1 (the parity op): 4 sequences x 2048 tokens, 32 q / 8 kv
+    heads, head_dim 128, block 16, 32 HOT / 64 WARM / 32 COLD blocks per
+    sequence.  us per call as eager Python calls through the public API and
+    as CUDA-graph replays of the same calls (the inputs, 17 MB, stay L2
+    resident, as they would for a model layer)."""
+    from paged_tierkv_b200 import workloads
+    wl = workloads.make_workload(batch=4, q_heads=Q_HEADS, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+                                 block_size=16, ctx_tokens=2048, hot_frac=0.25, warm_frac=0.5,
+                                 seed=1, device=device)
+    out = torch.empty(wl.query.shape, dtype=torch.float16, device=device)
+    for _ in range(10):
+        workloads.decode(wl, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(calls):
+        workloads.decode(wl, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    eager_us = e0.elapsed_time(e1) * 1e3 / calls
+
+    def many():
+        for _ in range(100):
+            workloads.decode(wl, out=out)
+    graph_ms = _timed_graph(many, 5, 2, False, device)
+    b = wl.algorithmic_bytes()
+    return {"workload": "c1_b4_ctx2048_bs16_32h_64w_32c", "bytes_per_call": b,
+            "us_per_call_eager": round(eager_us, 2), "us_per_call_graph": round(graph_ms * 10, 2),
+            "GBps_graph": round(b / (graph_ms * 1e-2 * 1e-3) / 1e9, 1),
+            "l2": "inputs (17 MB) L2-resident across calls"}
+
+
+def c2_object(device, steps=20):
+    """Configuration 2's attention (TinyLlama shape: 22 layers, 32 q / 4 kv
+    heads, head_dim 64, block 16, 25 % HOT / 50 % WARM / 25 % COLD) at its mid-
+    generation context, 8 sequences x 1152 tokens (1024-token prompt + 128 of
+    the 256 generated): ms per 22-layer step, each layer a separately
+    materialised pool set, replayed from a CUDA graph after an L2 flush (the
+    whole model's KV, 105 MB, would otherwise stay in L2, which the model's
+    2.2 GB of weights evict in a real step).  Attention only: the model's
+    other work is outside this path."""
+    from paged_tierkv_b200 import workloads
+    wls = [workloads.make_workload(batch=8, q_heads=32, kv_heads=4, head_dim=64, block_size=16,
+                                   ctx_tokens=1152, hot_frac=0.25, warm_frac=0.5, seed=200 + i,
+                                   device=device) for i in range(22)]
+    outs = [torch.empty(w.query.shape, dtype=torch.float16, device=device) for w in wls]
+
+    def step():
+        for w, o in zip(wls, outs):
+            workloads.decode(w, out=o)
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        step()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(steps)]
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            _flush_l2(flush)
+            g.replay()
+        for e0, e1 in pairs:
+            _flush_l2(flush)
+            e0.record(side)
+            g.replay()
+            e1.record(side)
+    torch.cuda.synchronize()
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in pairs)
+    b = sum(w.algorithmic_bytes() for w in wls)
+    del g, wls, outs, flush
+    torch.cuda.empty_cache()
+    return {"workload": "c2_b8_ctx1152_h0.25_w0.5_bs16_l22_kv4_d64", "ms_per_step": round(ms, 4),
+            "attention_tokens_per_s": round(8 / (ms * 1e-3), 1),
+            "GBps": round(b / (ms * 1e-3) / 1e9, 1), "bytes_per_step": b,
+            "l2": "flushed (256 MB write) before every timed step", "cuda_graph": True,
+            "note": "attention only: model-level tokens/s needs the reference's model code, "
+                    "which does not run on the GPU box"}
+
+
+def sweep_object(a, rank, dist_on, device):
+    """Configuration 5's sweep: hot fractions 1.0 / 0.5 / 0.25 / 0.1 (the rest
+    split 2:1 WARM:COLD) at block 16 and 32; per point the mean event time of
+    a decode launch and its GB/s against the measured copy peak."""
+    peak, _ = hbm_peak()
+    out = []
+    for bs in (16, 32):
+        for h in (1.0, 0.5, 0.25, 0.1):
+            a2 = argparse.Namespace(**{**vars(a), "hot_frac": h, "block_size": bs})
+            w2 = build_workload(a2, seed=99 + rank, device=device)
+            _, pl, _ = time_device(w2, max(20, min(a.steps, 200)), max(3, a.warmup), dist_on)
+            b2 = w2.algorithmic_bytes()
+            gbs = b2 / (statistics.mean(pl) * 1e-3) / 1e9
+            out.append({"block_size": bs, "hot_frac": h, "bytes_per_call": b2,
+                        "ms_per_call": round(statistics.mean(pl), 4), "GBps": round(gbs, 1),
+                        "frac": round(gbs / peak, 4)})
+            del w2
+            torch.cuda.empty_cache()
+    return out
+
+
+def demote_object(a, device):
+    """Configuration 5's demotion: 2^20 fp16 [16 x 128] N(0,1) tiles (65536
+    blocks x 8 kv heads x K/V) quantized bit-exactly into the WARM pool in one
+    launch, and promoted back; ms and GB/s against the measured copy peak."""
+    a2 = argparse.Namespace(**{**vars(a), "demote_blocks": 65536})
+    return _demote_measure(a2, 0, False, device)[0]
+
+
 def run_c4(a, rank, world, dist_on, device):
     """`--config c4`: configuration 4 as its own line (strong scaling)."""
     from paged_tierkv_b200 import _native
@@ -757,13 +875,10 @@ def run_c4(a, rank, world, dist_on, device):
     print(json.dumps(line), flush=True)
 
 
-def run_demote(a, rank, world, dist_on, device):
-    """Configuration 5's demotion benchmark: 2^20 tiles of [16 x 128] fp16 N(0,1)
-    (one tile = one (block, kv head) K or V), i.e. 65536 blocks x 8 kv heads x
-    {K, V}, quantized bit-exactly (Format R) into the WARM pool in one launch.
-    Bytes per launch: 4 GiB read, 2 GiB codes + 64 MiB scale/zero written."""
-    from paged_tierkv_b200 import _native, ops
-    _native.load(build_if_missing=True)
+def _demote_measure(a, rank, dist_on, device):
+    """Demotion of a.demote_blocks blocks x 8 kv heads x K/V tiles of [16 x 128]
+    fp16 N(0,1) in one launch, then promotion back: mean event ms per launch."""
+    from paged_tierkv_b200 import ops
     blocks, hkv, bs, d = a.demote_blocks, 8, 16, 128
     pools = ops.TieredPools.allocate(blocks, blocks, hkv, bs, d, device)
     gen = torch.Generator(device=device).manual_seed(11 + rank)
@@ -778,7 +893,7 @@ def run_demote(a, rank, world, dist_on, device):
     steps = max(1, min(a.steps, 50))
 
     def timed(fn):
-        for _ in range(a.warmup):
+        for _ in range(max(1, a.warmup)):
             fn()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -792,26 +907,44 @@ def run_demote(a, rank, world, dist_on, device):
         torch.cuda.synchronize()
         return statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
 
+    ms = timed(lambda: ops.demote_blocks_to_warm(pools, src, dst, lens))
+    ms_p = timed(lambda: ops.promote_blocks_to_hot(pools, dst, src, lens))
+    x = pools.hot_k[:128].cpu().numpy() if rank == 0 else None
+    del pools
+    torch.cuda.empty_cache()
+    peak, _ = hbm_peak()
+    return {"workload": f"demote_{tiles}_tiles", "tiles": tiles, "bytes_per_launch": bytes_per,
+            "steps": steps, "ms": round(ms, 4), "GBps": round(bytes_per / (ms * 1e-3) / 1e9, 1),
+            "frac": round(bytes_per / (ms * 1e-3) / 1e9 / peak, 4),
+            "promote_ms": round(ms_p, 4),
+            "promote_GBps": round(bytes_per / (ms_p * 1e-3) / 1e9, 1),
+            "promote_frac": round(bytes_per / (ms_p * 1e-3) / 1e9 / peak, 4)}, x
+
+
+def run_demote(a, rank, world, dist_on, device):
+    """Configuration 5's demotion benchmark: 2^20 tiles of [16 x 128] fp16 N(0,1)
+    (one tile = one (block, kv head) K or V), i.e. 65536 blocks x 8 kv heads x
+    {K, V}, quantized bit-exactly (Format R) into the WARM pool in one launch.
+    Bytes per launch: 4 GiB read, 2 GiB codes + 64 MiB scale/zero written."""
+    from paged_tierkv_b200 import _native
+    _native.load(build_if_missing=True)
     sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     if sampler:
         sampler.start()
-    ms = timed(lambda: ops.demote_blocks_to_warm(pools, src, dst, lens))
+    res, x = _demote_measure(a, rank, dist_on, device)
     clocks = sampler.stop() if sampler else None
-    # promotion of the WARM slots just written back into HOT slots 0..blocks-1
-    ms_p = timed(lambda: ops.promote_blocks_to_hot(pools, dst, src, lens))
-    t = torch.tensor([ms, ms_p], dtype=torch.float64, device=device)
+    t = torch.tensor([res["ms"], res["promote_ms"]], dtype=torch.float64, device=device)
     if dist_on:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms, ms_p = float(t[0]), float(t[1])
     if rank != 0:
         return
+    tiles, bytes_per = res["tiles"], res["bytes_per_launch"]
     cpu = None
     if world == 1 and not a.no_cpu_baseline:
         # the oracle's restatement of quantize_fp16_to_int8 on a 2048-tile slice
         from oracle import tierkv_oracle as orc
-        sample_blocks = min(blocks, 128)
-        x = pools.hot_k[:sample_blocks].cpu().numpy()
-        tiles_s = sample_blocks * hkv * 2
+        tiles_s = x.shape[0] * 8 * 2
         reps, t0 = 0, time.perf_counter()
         while True:
             orc.quantize_rows_r(x)
@@ -828,7 +961,7 @@ def run_demote(a, rank, world, dist_on, device):
     gbs_p = bytes_per / (ms_p * 1e-3) / 1e9
     print(json.dumps({
         "metric": f"HOT->WARM demotion GB/s ({tiles} fp16 [16 x 128] tiles, Format R)",
-        "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world, "steps": res["steps"],
         "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "dtype": "fp16->u8", "data": "synthetic N(0,1)",
         "config": {"workload": f"demote_{tiles}_tiles", "tiles": tiles,
@@ -839,7 +972,7 @@ def run_demote(a, rank, world, dist_on, device):
                     "frac": round(gbs_p / peak, 4)},
         "clocks": clocks,
         "cpu_baseline": cpu,
-        "gpu_launches": 2 * steps,
+        "gpu_launches": 2 * res["steps"],
     }), flush=True)
 
 
