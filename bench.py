@@ -300,46 +300,66 @@ def time_device(wl, steps, warmup, dist_on):
 
 
 def time_e2e(wl, steps, warmup):
-    """Same metric through the public API with host buffers: per step the query
-    and the three block tables go host->device from pinned memory (one packed
-    copy) and the output comes back device->host, all inside the timed region."""
+    """Same metric through the public API with host buffers: every step's
+    inputs (the query and the three block tables, packed back to back in
+    pinned host memory) go host->device in one copy and its output comes back
+    device->host, all inside the timed region.  The copies run on a second
+    stream, double-buffered as a serving loop would run them: step i+1's
+    inputs go up and step i-1's output comes down while step i computes;
+    events order every buffer's reuse."""
     from paged_tierkv_b200 import ops
-    stream = torch.cuda.current_stream()
-    # the step's inputs (query, block table, states, lengths) sit back to back
-    # in one pinned host buffer and go up in one copy
+    dev = wl.query.device
+    compute = torch.cuda.current_stream()
+    copy = torch.cuda.Stream(device=dev)
     srcs = [wl.query, wl.block_table, wl.block_states, wl.block_lengths]
     sizes = [x.numel() * x.element_size() for x in srcs]
     offs = [0]
     for n in sizes:
         offs.append(offs[-1] + (n + 255) // 256 * 256)
     h_pack = torch.zeros(offs[-1], dtype=torch.uint8).pin_memory()
-    d_pack = torch.empty(offs[-1], dtype=torch.uint8, device=wl.query.device)
-    views = []
     for x, o, n in zip(srcs, offs, sizes):
         h_pack[o:o + n].view(x.dtype).view(x.shape).copy_(x.cpu())
-        views.append(d_pack[o:o + n].view(x.dtype).view(x.shape))
-    d_q, d_t, d_s, d_l = views
-    h_out = torch.empty(wl.query.shape, dtype=torch.float16).pin_memory()
-    d_out = torch.empty(wl.query.shape, dtype=torch.float16, device=wl.query.device)
+    d_pack = [torch.empty(offs[-1], dtype=torch.uint8, device=dev) for _ in range(2)]
+    views = [[d[o:o + n].view(x.dtype).view(x.shape) for x, o, n in zip(srcs, offs, sizes)]
+             for d in d_pack]
+    h_out = [torch.empty(wl.query.shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    d_out = [torch.empty(wl.query.shape, dtype=torch.float16, device=dev) for _ in range(2)]
 
-    def step():
-        d_pack.copy_(h_pack, non_blocking=True)
-        ops.decode_attention(d_q, d_t, d_s, d_l, wl.pools, wl.num_blocks, wl.groups, wl.scaling,
-                             out=d_out)
-        h_out.copy_(d_out, non_blocking=True)
+    def run(n):
+        up = [torch.cuda.Event() for _ in range(n)]
+        done = [torch.cuda.Event() for _ in range(n)]
+        with torch.cuda.stream(copy):
+            d_pack[0].copy_(h_pack, non_blocking=True)
+            up[0].record(copy)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                with torch.cuda.stream(copy):
+                    if i >= 1:
+                        copy.wait_event(done[i - 1])  # buffer (i + 1) % 2 is free again
+                    d_pack[1 - b].copy_(h_pack, non_blocking=True)
+                    up[i + 1].record(copy)
+            compute.wait_event(up[i])
+            q, t, st, ln = views[b]
+            ops.decode_attention(q, t, st, ln, wl.pools, wl.num_blocks, wl.groups, wl.scaling,
+                                 out=d_out[b])
+            done[i].record(compute)
+            with torch.cuda.stream(copy):
+                copy.wait_event(done[i])
+                h_out[b].copy_(d_out[b], non_blocking=True)
+        compute.wait_stream(copy)  # the last output is on the host
 
-    for _ in range(warmup):
-        step()
+    run(max(2, warmup))
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        step()
-    e1.record(stream)
+    e0.record(compute)
+    copy.wait_event(e0)
+    run(steps)
+    e1.record(compute)
     torch.cuda.synchronize()
     h2d = h_pack.numel()
-    d2h = h_out.numel() * h_out.element_size()
+    d2h = h_out[0].numel() * h_out[0].element_size()
     return e0.elapsed_time(e1), h2d, d2h
 
 
