@@ -232,11 +232,15 @@ __device__ __forceinline__ float* x_lse(const DecodeParams& p, int q, uint32_t e
 // (sequence, kv head): part j of row r at po + ((r * rstride) + j0 + j) * D
 // and plse[r * rstride + j0 + j].  The result goes to the final output
 // (p.out / p.out_lse / p.lse_final) when dst_o is null, else to the fp32
-// partial slot dj of rows with stride dstride.  All NT threads take part;
-// wsl is shared scratch of kMaxGroups * (cnt + 2) floats.  One warp per
-// head: a lane owns 4 dims (a float4 of every part's row) and, for head_dim
-// 64, every other part; each round keeps kMergeDepth independent 16-byte
-// loads in flight, and the LSEs come in rounds of kMergeLseDepth per thread.
+// partial slot dj of rows with stride dstride.  wsl is shared scratch of
+// G * cnt floats.  One warp per head, no CTA barrier: a lane owns 4 dims (a
+// float4 of every part's row) and, for head_dim 64, every other part; each
+// round keeps kMergeDepth independent 16-byte loads in flight, the first
+// round together with the row's LSEs (kMergeLseDepth per lane per round).
+// (Measured on B200 against three CTA-wide phases -- LSEs, max and sum,
+// weights -- each behind a CTA barrier and a full fence around the ticket:
+// the 74-way merge of a 131072-token layer 5.3 -> 3.3 us, an 8-GPU shard's
+// launch 18.8 -> 17.3 us.)
 // Partial rows each lane loads per round of the split merge (the merge is
 // latency-bound: one round trip per round).
 #ifndef TKV_MERGE_DEPTH
@@ -250,6 +254,40 @@ constexpr int kMergeLseDepth = 4;
 #endif
 constexpr int kVcorrFlush = TKV_VCORR_FLUSH;
 
+// Stores the merged row (o: this lane's float4 of dims 4v..4v+3).
+template <int D>
+__device__ __forceinline__ void merged_row_out(const DecodeParams& p, size_t row, int v, bool lead,
+                                               int lane, float4 o, float lse, float* dst_o,
+                                               float* dst_lse, int dstride, int dj, bool xout,
+                                               uint32_t epoch) {
+  if (dst_o != nullptr) {
+    if (lead) reinterpret_cast<float4*>(dst_o + (row * dstride + dj) * D)[v] = o;
+    if (lane == 0) dst_lse[row * dstride + dj] = lse;
+  } else if (xout) {
+    // this rank's partial of the row into every rank's inbox
+    for (int q = 0; q < p.x_world; ++q) {
+      if (lead)
+        reinterpret_cast<float4*>(x_o<D>(p, q, epoch) + (row * p.x_world + p.x_rank) * D)[v] = o;
+      if (lane == 0) x_lse<D>(p, q, epoch)[row * p.x_world + p.x_rank] = lse;
+    }
+  } else {
+    if (lead) {
+      const size_t base = row * D + 4 * v;
+      store_out(p.out, p.out_dtype, base + 0, o.x);
+      store_out(p.out, p.out_dtype, base + 1, o.y);
+      store_out(p.out, p.out_dtype, base + 2, o.z);
+      store_out(p.out, p.out_dtype, base + 3, o.w);
+    }
+    if (lane == 0) {
+      if (p.out_lse) p.out_lse[row] = lse;
+      if (p.lse_final) p.lse_final[row] = lse;
+    }
+  }
+}
+
+// The warp of a head requests the first round of partial rows and the row's
+// LSEs together, reduces max and sum over its lanes and keeps the weights in
+// its own scratch row.
 template <int D, int NT>
 __device__ __forceinline__ void merge_parts(const float* po, const float* plse, int rstride,
                                             int j0, int cnt, size_t row0, int G, float* wsl,
@@ -257,77 +295,68 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
                                             int dstride, int dj, bool xout = false,
                                             uint32_t epoch = 0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* hm = wsl + kMaxGroups * cnt;  // [G] max, [G] sum
-  for (int e0 = threadIdx.x; e0 < G * cnt; e0 += NT * kMergeLseDepth) {
-    float v[kMergeLseDepth];
-#pragma unroll
-    for (int k = 0; k < kMergeLseDepth; ++k) {
-      const int e = e0 + k * NT;
-      const int h = e / cnt;
-      v[k] = e < G * cnt ? __ldcg(plse + (row0 + h) * rstride + j0 + (e - h * cnt)) : 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < kMergeLseDepth; ++k)
-      if (e0 + k * NT < G * cnt) wsl[e0 + k * NT] = v[k];
-  }
-  __syncthreads();
-  for (int h = warp; h < G; h += NT / 32) {
-    float M = -INFINITY;
-    for (int sp = lane; sp < cnt; sp += 32) M = fmaxf(M, wsl[h * cnt + sp]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float S = 0.f;
-    if (M != -INFINITY)
-      for (int sp = lane; sp < cnt; sp += 32) S += ex2((wsl[h * cnt + sp] - M) * kLog2e);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
-    if (lane == 0) {
-      hm[h] = M;
-      hm[kMaxGroups + h] = S;
-    }
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * cnt; e += NT) {
-    const int h = e / cnt;
-    const float M = hm[h], S = hm[kMaxGroups + h];
-    wsl[e] = (M != -INFINITY && S > 0.f) ? ex2((wsl[e] - M) * kLog2e) / S : 0.f;
-  }
-  __syncthreads();
   constexpr int kVecs = D / 4;                 // float4 per partial row
   constexpr int kLanesPerRow = kVecs < 32 ? kVecs : 32;
   constexpr int kSplitLanes = 32 / kLanesPerRow;
+  const int v = lane % kLanesPerRow;
+  const int sp0 = lane / kLanesPerRow;
   for (int h = warp; h < G; h += NT / 32) {
     const size_t row = row0 + h;
-    const int v = lane % kLanesPerRow;
-    const int sp0 = lane / kLanesPerRow;
+    float* wl = wsl + (size_t)h * cnt;
     const float4* src = reinterpret_cast<const float4*>(po + (row * rstride + j0) * D) + v;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    int sp = sp0;
-    for (; sp + (kMergeDepth - 1) * kSplitLanes < cnt; sp += kMergeDepth * kSplitLanes) {
-      float4 x[kMergeDepth];
+    const float* lsrc = plse + row * rstride + j0;
+    float4 x[kMergeDepth];
 #pragma unroll
-      for (int k = 0; k < kMergeDepth; ++k)
-        x[k] = __ldcg(src + (size_t)(sp + k * kSplitLanes) * kVecs);
+    for (int k = 0; k < kMergeDepth; ++k) {
+      const int sidx = sp0 + k * kSplitLanes;
+      x[k] = sidx < cnt ? __ldcg(src + (size_t)sidx * kVecs) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float M = -INFINITY;
+    for (int e0 = lane; e0 < cnt; e0 += 32 * kMergeLseDepth) {
+      float lv[kMergeLseDepth];
 #pragma unroll
-      for (int k = 0; k < kMergeDepth; ++k) {
-        const float w = wsl[h * cnt + sp + k * kSplitLanes];
-        o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
+      for (int k = 0; k < kMergeLseDepth; ++k) {
+        const int e = e0 + 32 * k;
+        lv[k] = e < cnt ? __ldcg(lsrc + e) : -INFINITY;
+      }
+#pragma unroll
+      for (int k = 0; k < kMergeLseDepth; ++k) {
+        const int e = e0 + 32 * k;
+        if (e < cnt) wl[e] = lv[k];
+        M = fmaxf(M, lv[k]);
       }
     }
-    if (sp < cnt) {
-      // the rest (fewer than kMergeDepth rows per lane) in one predicated
-      // round, so it costs one round trip instead of one per row
-      float4 x[kMergeDepth];
 #pragma unroll
-      for (int k = 0; k < kMergeDepth; ++k) {
-        const int s = sp + k * kSplitLanes;
-        x[k] = s < cnt ? __ldcg(src + (size_t)s * kVecs) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    // each lane turns its own LSEs into weights, then the warp reads them all
+    float S = 0.f;
+    if (M != -INFINITY) {
+      for (int e = lane; e < cnt; e += 32) {
+        const float w = ex2((wl[e] - M) * kLog2e);
+        wl[e] = w;
+        S += w;
       }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
+    const bool live = M != -INFINITY && S > 0.f;
+    for (int e = lane; e < cnt; e += 32) wl[e] = live ? wl[e] / S : 0.f;
+    __syncwarp();
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    int sp = sp0;
+    for (;;) {
 #pragma unroll
       for (int k = 0; k < kMergeDepth; ++k) {
-        const int s = sp + k * kSplitLanes;
-        const float w = s < cnt ? wsl[h * cnt + s] : 0.f;
+        const int sidx = sp + k * kSplitLanes;
+        const float w = sidx < cnt ? wl[sidx] : 0.f;
         o.x += w * x[k].x; o.y += w * x[k].y; o.z += w * x[k].z; o.w += w * x[k].w;
+      }
+      sp += kMergeDepth * kSplitLanes;
+      if (sp - sp0 >= cnt) break;
+#pragma unroll
+      for (int k = 0; k < kMergeDepth; ++k) {
+        const int sidx = sp + k * kSplitLanes;
+        x[k] = sidx < cnt ? __ldcg(src + (size_t)sidx * kVecs) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
@@ -337,32 +366,8 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
       o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
       o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
     }
-    const float M = hm[h], S = hm[kMaxGroups + h];
-    const float lse = (M != -INFINITY && S > 0.f) ? M + logf(S) : -INFINITY;
-    if (dst_o != nullptr) {
-      if (sp0 == 0)
-        reinterpret_cast<float4*>(dst_o + (row * dstride + dj) * D)[v] = o;
-      if (lane == 0) dst_lse[row * dstride + dj] = lse;
-    } else if (xout) {
-      // this rank's partial of the row into every rank's inbox
-      for (int q = 0; q < p.x_world; ++q) {
-        if (sp0 == 0)
-          reinterpret_cast<float4*>(x_o<D>(p, q, epoch) + (row * p.x_world + p.x_rank) * D)[v] = o;
-        if (lane == 0) x_lse<D>(p, q, epoch)[row * p.x_world + p.x_rank] = lse;
-      }
-    } else {
-      if (sp0 == 0) {
-        const size_t base = row * D + 4 * v;
-        store_out(p.out, p.out_dtype, base + 0, o.x);
-        store_out(p.out, p.out_dtype, base + 1, o.y);
-        store_out(p.out, p.out_dtype, base + 2, o.z);
-        store_out(p.out, p.out_dtype, base + 3, o.w);
-      }
-      if (lane == 0) {
-        if (p.out_lse) p.out_lse[row] = lse;
-        if (p.lse_final) p.lse_final[row] = lse;
-      }
-    }
+    const float lse = live ? M + logf(S) : -INFINITY;
+    merged_row_out<D>(p, row, v, sp0 == 0, lane, o, lse, dst_o, dst_lse, dstride, dj, xout, epoch);
   }
 }
 
@@ -1173,10 +1178,12 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   uint32_t* ticket = ngroups > 1 ? p.counters + 2 * (size_t)p.batch * p.kv_heads +
                                        unit * (size_t)ngroups + group
                                  : p.counters + unit;
-  __threadfence();
+  // thread 0's acquire-release increment publishes the CTA's partials (the
+  // barrier orders every thread's stores before it) and, for the last CTA,
+  // acquires everyone else's; the next barrier hands that on to the CTA
   __syncthreads();
   if (threadIdx.x == 0) {
-    const uint32_t prev = atomicAdd(ticket, 1u);
+    const uint32_t prev = atom_add_acq_rel_gpu(ticket, 1u);
     misc[1] = (prev == (uint32_t)(gcount - 1)) ? 1 : 0;
   }
   __syncthreads();
@@ -1186,7 +1193,6 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
       atomicExch(ticket, 0u);
       atomicExch(chunk_ctr, 0u);
     }
-    __threadfence();
     const uint32_t epoch = (uint32_t)misc[2];
     merge_parts<D, Cfg::kThreads>(p.part_o, p.part_lse, nsplit, 0, nsplit, row0, G, wsl, p,
                                   nullptr, nullptr, 0, 0, p.x_world > 0, epoch);
@@ -1194,13 +1200,11 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     return;
   }
   if (threadIdx.x == 0) atomicExch(ticket, 0u);
-  __threadfence();
   merge_parts<D, Cfg::kThreads>(p.part_o, p.part_lse, nsplit, gfirst, gcount, row0, G, wsl, p,
                                 p.gpart_o, p.gpart_lse, ngroups, group);
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const uint32_t prev = atomicAdd(p.counters + unit, 1u);
+    const uint32_t prev = atom_add_acq_rel_gpu(p.counters + unit, 1u);
     misc[1] = (prev == (uint32_t)(ngroups - 1)) ? 1 : 0;
   }
   __syncthreads();
@@ -1209,7 +1213,6 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     atomicExch(p.counters + unit, 0u);
     atomicExch(chunk_ctr, 0u);
   }
-  __threadfence();
   const uint32_t epoch = (uint32_t)misc[2];
   merge_parts<D, Cfg::kThreads>(p.gpart_o, p.gpart_lse, ngroups, 0, ngroups, row0, G, wsl, p,
                                 nullptr, nullptr, 0, 0, p.x_world > 0, epoch);

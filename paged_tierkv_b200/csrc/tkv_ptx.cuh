@@ -48,6 +48,18 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// GPU-scope fetch-and-add with acquire-release semantics (merge tickets):
+// the release covers the stores of the whole CTA when a CTA barrier precedes
+// it, the acquire covers every store released by earlier increments.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 // Programmatic dependent launch (sm_90+): let the next kernel of the stream
 // be scheduled now (its CTAs take SM slots as this grid's CTAs exit), and wait
 // until the previous kernel of the stream has completed and its memory is
