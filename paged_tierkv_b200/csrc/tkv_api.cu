@@ -438,6 +438,14 @@ static int32_t decode_impl(const tkv_pools* pools, const tkv_decode_args* a,
   p.splits = plan.splits;
   p.chunk = plan.chunk;
   p.group_size = plan.group_size;
+  {
+    // the first wave of CTAs (those resident at once) prefetches before its
+    // dependency wait; later waves start after the previous kernel is done
+    int ctas = 0;
+    if (!cached_occupancy(d, bs, pools->format, a->query_dtype, &ctas) || ctas <= 0)
+      return TKV_ERR_CUDA;
+    p.prefetch_ctas = sms * ctas;
+  }
   p.out_dtype = a->out_dtype;
   p.scale_log2 = a->scaling * kLog2e;
   if (xc) {

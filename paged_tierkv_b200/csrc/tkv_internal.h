@@ -68,6 +68,8 @@ struct DecodeParams {
   int32_t splits;
   int32_t chunk;              // blocks per claimed work chunk: 8, 16 or 32
   int32_t group_size;         // splits merged per group (= splits: one level)
+  int32_t prefetch_ctas;      // CTAs with a smaller linear index prefetch before the
+                              // dependency wait (the first wave)
   // context-sharded exchange (x_world > 0): inbox of rank q mapped at x_inbox[q];
   // layout: flags [world][units] u32 (256-byte padded), then o [2][rows][world][D]
   // and lse [2][rows][world] fp32 (double-buffered by epoch parity)
