@@ -105,7 +105,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// ---- TMA / bulk copies (no .multicast::cluster anywhere) ----------------------
+// ---- TMA / bulk copies (none multicast across a cluster) ----------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x,
                                             int32_t y, uint64_t* bar) {
   asm volatile(
