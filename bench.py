@@ -708,7 +708,7 @@ def c4_object(a, rank, world, dist_on, device, steps=50, warmup=5):
            "parity_layer0_max_rel_vs_1_rank": rel, "parity_device_errors": perr}
     if world > 1:
         obj.update({
-            "exchange": "p2p: peer-memory stores + epoch flags inside the decode launch",
+            "exchange": "p2p: epoch-tagged peer-memory stores inside the decode launch",
             "exchange_us_per_layer": round((res["p2p_ms"] - res["local_ms"]) * 1e3 / a.layers, 2),
             "nccl_ms_per_step": round(res["nccl_ms"], 4),
             "nccl_tokens_per_s": round(1000.0 / res["nccl_ms"], 2),
@@ -884,7 +884,7 @@ def run_c4(a, rank, world, dist_on, device):
         "config": {"workload": f"c4_ctx{ctx}_bs{bs}_l{a.layers}", "hot_blocks": n_hot,
                    "warm_blocks": n_warm, "partition": "byte-balanced contiguous block ranges",
                    "exchange": ("none" if world == 1 else
-                                "peer-memory stores + epoch flags inside the decode launch"
+                                "epoch-tagged peer-memory stores inside the decode launch"
                                 if a.exchange == "p2p" else
                                 "NCCL all_gather of packed (o, lse) per layer"),
                    "cuda_graph": not a.no_graph},

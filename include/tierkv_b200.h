@@ -262,14 +262,15 @@ int32_t tkv_store_prefill_blocks(const tkv_pools* pools, const void* key, const 
  * Each rank holds a contiguous block range of the same sequences; every rank
  * launches tkv_decode_attention_exchange with its own tables and pools and
  * the same epoch.  The last CTA of each (sequence, kv head) writes its
- * normalised partial (o, LSE) into every rank's inbox with plain stores
- * through CUDA IPC mappings (no multicast), publishes it with a release store
- * of the epoch into the receiving rank's flag for (sender, unit), waits
- * (acquire, bounded by timeout_ns; TKV_DEVERR_TIMEOUT when it runs out) for
- * the flags of all ranks in its own inbox, and merges the world partials into
- * args->out / out_lse (and the global LSE the score pass normalises with).
- * Partials are double-buffered by epoch parity, so a rank may run one call
- * ahead of the others.  Replaces the per-layer all-gather + merge. */
+ * normalised partial (o, LSE) into every rank's inbox through CUDA IPC
+ * mappings (no multicast) as 64-bit words, each the call's epoch (high half)
+ * and an fp32 value (low half) in one system-scope store; it then polls the
+ * words of all ranks in its own inbox until each carries the epoch (bounded
+ * by timeout_ns; TKV_DEVERR_TIMEOUT when it runs out, missing partials then
+ * count as empty) and merges the world partials into args->out / out_lse
+ * (and the global LSE the score pass normalises with).  Partials are
+ * double-buffered by epoch parity, so a rank may run one call ahead of the
+ * others.  Replaces the per-layer all-gather + merge. */
 #define TKV_EXCHANGE_MAX_RANKS 8
 
 typedef struct tkv_exchange {

@@ -217,25 +217,32 @@ __device__ __forceinline__ void load_qfrag(uint32_t sq, int lane, int m, uint32_
 }
 
 // ---------------------------------------------------------------- exchange
-// Rank q's inbox as mapped in this process: flags [world][units_cap], then
-// o [2][rows_cap][world][D] and lse [2][rows_cap][world] (epoch parity).
-// The epoch of the call is read once per CTA at kernel start (thread 0: the
-// value in the parameters, or a plain global load from x_epoch_dev, which
-// nothing writes while the launch runs) and handed to these helpers by value.
-__device__ __forceinline__ uint32_t* x_flags(const DecodeParams& p, int q) {
-  return reinterpret_cast<uint32_t*>(p.x_inbox[q]);
-}
+// Rank q's inbox as mapped in this process: o words [2][rows_cap][world][D]
+// and lse words [2][rows_cap][world] (epoch parity), each word the epoch of
+// the call that wrote it (high half) and an fp32 value (low half).  A word is
+// valid for a call when its epoch is the call's: the value and its epoch
+// travel in one single-copy-atomic 8-byte store, so no flag and no release
+// fence are needed, and a reader polls the words themselves.  The epoch of
+// the call is read once per CTA at kernel start (thread 0: the value in the
+// parameters, or a plain global load from x_epoch_dev, which nothing writes
+// while the launch runs) and handed to these helpers by value.
 template <int D>
-__device__ __forceinline__ float* x_o(const DecodeParams& p, int q, uint32_t epoch) {
-  return reinterpret_cast<float*>(p.x_inbox[q] + xchg_flags_bytes(p.x_world, p.x_units_cap)) +
+__device__ __forceinline__ uint64_t* x_o(const DecodeParams& p, int q, uint32_t epoch) {
+  return reinterpret_cast<uint64_t*>(p.x_inbox[q]) +
          (size_t)(epoch & 1u) * p.x_rows_cap * p.x_world * D;
 }
 template <int D>
-__device__ __forceinline__ float* x_lse(const DecodeParams& p, int q, uint32_t epoch) {
-  return reinterpret_cast<float*>(p.x_inbox[q] + xchg_flags_bytes(p.x_world, p.x_units_cap) +
-                                  xchg_o_bytes(p.x_world, p.x_rows_cap, D)) +
+__device__ __forceinline__ uint64_t* x_lse(const DecodeParams& p, int q, uint32_t epoch) {
+  return reinterpret_cast<uint64_t*>(p.x_inbox[q] + xchg_o_bytes(p.x_world, p.x_rows_cap, D)) +
          (size_t)(epoch & 1u) * p.x_rows_cap * p.x_world;
 }
+__device__ __forceinline__ uint64_t x_word(float v, uint32_t epoch) {
+  return ((uint64_t)epoch << 32) | (uint64_t)__float_as_uint(v);
+}
+__device__ __forceinline__ bool x_valid(uint64_t w, uint32_t epoch) {
+  return (uint32_t)(w >> 32) == epoch;
+}
+__device__ __forceinline__ float x_value(uint64_t w) { return __uint_as_float((uint32_t)w); }
 
 // Merges `cnt` normalised partials (o, LSE) of the G rows row0.. of a
 // (sequence, kv head): part j of row r at po + ((r * rstride) + j0 + j) * D
@@ -275,9 +282,12 @@ __device__ __forceinline__ void merged_row_out(const DecodeParams& p, size_t row
   } else if (xout) {
     // this rank's partial of the row into every rank's inbox
     for (int q = 0; q < p.x_world; ++q) {
-      if (lead)
-        reinterpret_cast<float4*>(x_o<D>(p, q, epoch) + (row * p.x_world + p.x_rank) * D)[v] = o;
-      if (lane == 0) x_lse<D>(p, q, epoch)[row * p.x_world + p.x_rank] = lse;
+      if (lead) {
+        uint64_t* dst = x_o<D>(p, q, epoch) + (row * p.x_world + p.x_rank) * D + 4 * v;
+        st_relaxed_sys_v2(dst, x_word(o.x, epoch), x_word(o.y, epoch));
+        st_relaxed_sys_v2(dst + 2, x_word(o.z, epoch), x_word(o.w, epoch));
+      }
+      if (lane == 0) st_relaxed_sys(x_lse<D>(p, q, epoch) + row * p.x_world + p.x_rank, x_word(lse, epoch));
     }
   } else {
     if (lead) {
@@ -381,8 +391,11 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
 }
 
 // The world partials of the G rows row0.. (this rank's inbox, epoch parity)
-// merged into the output: one warp per head, every lane loading the <= 8 LSEs
-// and its float4 of every partial in one round of loads.
+// merged into the output: one warp per head.  Lane q < world polls rank q's
+// LSE word, then every lane polls the words of its 4 dims of each rank's
+// partial and accumulates them.  All polls share one deadline (timeout_ns,
+// 2 s by default); past it they give up, record TKV_DEVERR_TIMEOUT and treat
+// the missing partials as empty.
 template <int D, int NT>
 __device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int G, uint32_t epoch) {
   constexpr int kVecs = D / 4;                 // float4 per row
@@ -390,32 +403,62 @@ __device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int 
   constexpr int kSplitLanes = 32 / kLanesPerRow;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int W = p.x_world;
-  const float* xo = x_o<D>(p, p.x_rank, epoch);
-  const float* xl = x_lse<D>(p, p.x_rank, epoch);
+  const uint64_t* xo = x_o<D>(p, p.x_rank, epoch);
+  const uint64_t* xl = x_lse<D>(p, p.x_rank, epoch);
   const int v = lane % kLanesPerRow;
   const int q0 = lane / kLanesPerRow;
+  const uint64_t limit = p.x_timeout_ns ? p.x_timeout_ns : 2000000000ull;
+  const uint64_t t0 = globaltimer();
+  bool late = false;  // this lane gave up on a word
   for (int h = warp; h < G; h += NT / 32) {
     const size_t row = row0 + h;
-    float lse[8];
-    float4 o[8];
+    float lq = -INFINITY;
+    if (lane < W) {
+      const uint64_t* src = xl + row * W + lane;
+      uint64_t w = ld_relaxed_sys(src);
+      while (!x_valid(w, epoch) && !late) {
+        if (globaltimer() - t0 > limit) {
+          late = true;
+        } else {
+          __nanosleep(32);
+          w = ld_relaxed_sys(src);
+        }
+      }
+      if (x_valid(w, epoch)) lq = x_value(w);
+    }
+    float M = lq;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float wq = (M != -INFINITY && lq != -INFINITY) ? ex2((lq - M) * kLog2e) : 0.f;
+    float S = wq;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) S += __shfl_xor_sync(0xffffffffu, S, off);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      lse[q] = q < W ? __ldcg(xl + row * W + q) : -INFINITY;
-      o[q] = (q < W && (q % kSplitLanes) == q0)
-                 ? __ldcg(reinterpret_cast<const float4*>(xo + (row * W + q) * D) + v)
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    float M = -INFINITY;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) M = fmaxf(M, lse[q]);
-    float S = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float w = ex2((lse[q] - M) * kLog2e);  // 0 for absent / empty partials
-        S += w;
-        acc.x += w * o[q].x; acc.y += w * o[q].y; acc.z += w * o[q].z; acc.w += w * o[q].w;
+      const float w = __shfl_sync(0xffffffffu, wq, q);  // 0 for absent / empty partials
+      if (q < W && (q % kSplitLanes) == q0 && w > 0.f) {
+        const uint64_t* src = xo + (row * W + q) * D + 4 * v;
+        uint64_t a0, a1, a2, a3;
+        ld_relaxed_sys_v2(src, a0, a1);
+        ld_relaxed_sys_v2(src + 2, a2, a3);
+        bool ok = x_valid(a0, epoch) && x_valid(a1, epoch) && x_valid(a2, epoch) &&
+                  x_valid(a3, epoch);
+        while (!ok && !late) {
+          if (globaltimer() - t0 > limit) {
+            late = true;
+          } else {
+            __nanosleep(32);
+            ld_relaxed_sys_v2(src, a0, a1);
+            ld_relaxed_sys_v2(src + 2, a2, a3);
+            ok = x_valid(a0, epoch) && x_valid(a1, epoch) && x_valid(a2, epoch) &&
+                 x_valid(a3, epoch);
+          }
+        }
+        if (ok) {
+          acc.x += w * x_value(a0); acc.y += w * x_value(a1);
+          acc.z += w * x_value(a2); acc.w += w * x_value(a3);
+        }
       }
     }
 #pragma unroll
@@ -439,35 +482,17 @@ __device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int 
       if (p.lse_final) p.lse_final[row] = total;
     }
   }
+  if (late) atomicOr(p.err, 0x2u);
 }
 
-// Publishes this unit's partials (already stored into every inbox) with a
-// release store of the epoch into each rank's flag (sender, unit), waits --
-// bounded -- for every rank's flag in this rank's inbox, and merges the world
-// partials into the output.  The CTA barrier orders every thread's partial
-// stores before the flag writer's system-scope release (happens-before is
-// transitive through bar.sync), which the reader's acquire pairs with.
+// Merges the world partials of this unit (its own partial is already stored
+// into every rank's inbox) and, with a device epoch, advances the epoch once
+// the launch's last unit is done.
 template <int D, int NT>
 __device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, size_t row0, int G,
                                          float* wsl, uint32_t epoch) {
-  __syncthreads();
-  const int world = p.x_world;
-  if ((int)threadIdx.x < world)
-    st_release_sys(x_flags(p, threadIdx.x) + (size_t)p.x_rank * p.x_units_cap + unit, epoch);
-  if ((int)threadIdx.x < world) {
-    const uint32_t* f = x_flags(p, p.x_rank) + (size_t)threadIdx.x * p.x_units_cap + unit;
-    const uint64_t limit = p.x_timeout_ns ? p.x_timeout_ns : 2000000000ull;
-    const uint64_t t0 = globaltimer();
-    // a peer may already be one call ahead: wait until the flag reaches the epoch
-    while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
-      if (globaltimer() - t0 > limit) {
-        atomicOr(p.err, 0x2u);
-        break;
-      }
-      __nanosleep(128);
-    }
-  }
-  __syncthreads();
+  (void)unit;
+  (void)wsl;
   x_merge<D, NT>(p, row0, G, epoch);
   // A device epoch advances when the last unit of the launch is done: every
   // CTA of the launch has read the epoch by then (at its start).
@@ -1195,8 +1220,9 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     if (nsplit == 1 && p.x_world > 0) {
       const uint32_t epoch = (uint32_t)misc[2];
       for (int q = 0; q < p.x_world; ++q) {
-        x_o<D>(p, q, epoch)[(row * p.x_world + p.x_rank) * D + d] = on;
-        if (d == 0) x_lse<D>(p, q, epoch)[row * p.x_world + p.x_rank] = lse;
+        st_relaxed_sys(x_o<D>(p, q, epoch) + (row * p.x_world + p.x_rank) * D + d, x_word(on, epoch));
+        if (d == 0)
+          st_relaxed_sys(x_lse<D>(p, q, epoch) + row * p.x_world + p.x_rank, x_word(lse, epoch));
       }
     } else if (nsplit == 1) {
       store_out(p.out, p.out_dtype, row * D + d, on);

@@ -71,8 +71,8 @@ struct DecodeParams {
   int32_t prefetch_ctas;      // CTAs with a smaller linear index prefetch before the
                               // dependency wait (the first wave)
   // context-sharded exchange (x_world > 0): inbox of rank q mapped at x_inbox[q];
-  // layout: flags [world][units] u32 (256-byte padded), then o [2][rows][world][D]
-  // and lse [2][rows][world] fp32 (double-buffered by epoch parity)
+  // layout: epoch-tagged 64-bit words, o [2][rows][world][D] then lse
+  // [2][rows][world] (double-buffered by epoch parity; see xchg_total_bytes)
   int32_t x_world;
   int32_t x_rank;
   uint32_t x_epoch;
@@ -168,16 +168,17 @@ struct AppendParams {
   int32_t cell_val[8];
 };
 
-// Inbox layout of the context-sharded exchange (see DecodeParams::x_inbox).
-__host__ __device__ inline size_t xchg_flags_bytes(int world, int units) {
-  return ((size_t)world * units * 4 + 255) / 256 * 256;
-}
+// Inbox layout of the context-sharded exchange (see DecodeParams::x_inbox):
+// o words [2][rows][world][D], then LSE words [2][rows][world], double-buffered
+// by epoch parity.  A word is 64 bits: the epoch of the call that wrote it in
+// the high half, the fp32 value in the low half.  (`units` does not enter the
+// layout.)
 __host__ __device__ inline size_t xchg_o_bytes(int world, int rows, int d) {
-  return (size_t)2 * rows * world * d * 4;
+  return (size_t)2 * rows * world * d * 8;
 }
 __host__ __device__ inline size_t xchg_total_bytes(int world, int rows, int units, int d) {
-  return xchg_flags_bytes(world, units) + xchg_o_bytes(world, rows, d) +
-         ((size_t)2 * rows * world * 4 + 255) / 256 * 256;
+  (void)units;
+  return xchg_o_bytes(world, rows, d) + ((size_t)2 * rows * world * 8 + 255) / 256 * 256;
 }
 
 struct PrefillParams {

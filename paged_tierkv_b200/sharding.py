@@ -12,8 +12,9 @@ the GPUs of one node:
   [o | LSE] buffer (NCCL over NVLink) and the LSE-merge kernel give every rank
   the full-context output (``ContextShardedDecode``).  ``P2PContextDecode``
   does the same inside the decode launch: partials are stored into every
-  rank's inbox over CUDA IPC peer memory, published with epoch flags and
-  merged by the same kernel.  Block scores need no second exchange:
+  rank's inbox over CUDA IPC peer memory as 64-bit words tagged with the
+  call's epoch, and merged by the same kernel once every word it needs
+  carries that epoch.  Block scores need no second exchange:
   p_global = p_local * exp(lse_local - lse_global).
 
 COLD blocks stay exact under sharding: each rank adds the analytic
@@ -220,7 +221,7 @@ class PeerExchange:
         rank has raised a timeout (the application agrees on that, e.g. with
         its own all-reduce of an error flag).  Waits for this rank's GPU work,
         meets the other ranks, and moves every rank to one epoch beyond the
-        largest epoch any rank has used, so no flag in any inbox (all of them
+        largest epoch any rank has used, so no word in any inbox (all of them
         stamped with older epochs) can satisfy the next call's wait before its
         peer has published for it."""
         torch.cuda.synchronize()

@@ -1,10 +1,10 @@
 """Context-sharded decode with the peer-memory exchange, on one GPU.
 
 No launch here waits for another launch: with one rank the kernel exchanges
-with itself; the two-rank case has the other rank's partials and flags
-written into the inbox by the host beforehand (what the peer's kernel would
-have stored), so the launch finds them published; the timeout case waits on a
-flag nothing sets and must come back with TKV_DEVERR_TIMEOUT.  The real
+with itself; the two-rank case has the other rank's partials written into the
+inbox by the host beforehand as epoch-tagged words (what the peer's kernel
+would have stored), so the launch finds them published; the timeout case
+waits on words nothing writes and must come back with TKV_DEVERR_TIMEOUT.  The real
 two-process exchange over CUDA IPC is in test_sharding_gpu.py.
 """
 
@@ -34,9 +34,25 @@ def _inbox(world, rows, units, d):
     return torch.zeros(n, dtype=torch.uint8, device="cuda")
 
 
-def _layout(world, rows, units, d):
-    flags = (world * units * 4 + 255) // 256 * 256
-    return flags, flags + 2 * rows * world * d * 4
+def _words(box, world, rows, d):
+    """The inbox as its two regions of 64-bit words: o [2][rows][world][d] and
+    lse [2][rows][world] (epoch parity); a word is epoch << 32 | fp32 bits."""
+    o_bytes = 2 * rows * world * d * 8
+    o = box[:o_bytes].view(torch.int64).view(2, rows, world, d)
+    lse = box[o_bytes:o_bytes + 2 * rows * world * 8].view(torch.int64).view(2, rows, world)
+    return o, lse
+
+
+def _tag(values, epoch):
+    bits = values.contiguous().float().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    return bits | (int(epoch) << 32)
+
+
+def _publish(box, world, rows, d, sender, epoch, o, lse):
+    """What rank `sender`'s launch of call `epoch` stores into this inbox."""
+    ow, lw = _words(box, world, rows, d)
+    ow[epoch & 1, :, sender, :] = _tag(o.view(rows, d), epoch)
+    lw[epoch & 1, :, sender] = _tag(lse.view(rows), epoch)
 
 
 def _run(d, case, **kw):
@@ -88,7 +104,6 @@ def test_two_ranks_with_the_peer_already_published(splits):
     box0, box1 = _inbox(world, rows, units, D), _inbox(world, rows, units, D)
     ex = sharding.PeerExchange(rows_cap=rows, units_cap=units, head_dim=D,
                                inboxes=[box0.data_ptr(), box1.data_ptr()], rank=0)
-    flags_b, lse_off = _layout(world, rows, units, D)
     for call in range(3):
         x = ex.next()
         par = x.epoch & 1
@@ -98,21 +113,21 @@ def test_two_ranks_with_the_peer_already_published(splits):
                                         d1["block_lengths"], d1["pools"], nb - cut, case["groups"],
                                         case["scaling"], out=o1, out_dtype=torch.float32,
                                         return_lse=True, num_splits=splits)
-        o_view = box0[flags_b:lse_off].view(torch.float32).view(2, rows, world, D)
-        l_view = box0[lse_off:lse_off + 2 * rows * world * 4].view(torch.float32).view(2, rows, world)
-        o_view[par, :, 1, :] = o1.view(rows, D)
-        l_view[par, :, 1] = l1.view(rows)
+        _publish(box0, world, rows, D, 1, x.epoch, o1, l1)
         torch.cuda.synchronize()
-        box0[:flags_b].view(torch.int32)[units:2 * units] = x.epoch  # flags [sender 1][unit]
         out, scores, lse = _run(d0, shards[0], num_splits=splits, return_scores=True,
                                 return_lse=True, exchange=x)
         torch.cuda.synchronize()
         np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
         # rank 0's scores are normalised over the whole contexts
         np.testing.assert_allclose(scores.cpu().numpy(), ref_scores[:, :, :cut], atol=1e-4, rtol=1e-3)
-        # rank 0 published to "rank 1": its partial and its flags
-        f1 = box1[:flags_b].view(torch.int32)[:units].cpu().numpy()
-        assert (f1 == x.epoch).all()
+        # rank 0 published its partial to "rank 1", every word tagged with the epoch
+        ow1, lw1 = _words(box1, world, rows, D)
+        assert ((ow1[par, :, 0, :] >> 32) == x.epoch).all()
+        assert ((lw1[par, :, 0] >> 32) == x.epoch).all()
+        # and to itself: the words it merged, equal in value to its own LSE output
+        ow0, lw0 = _words(box0, world, rows, D)
+        assert ((lw0[par, :, 0] >> 32) == x.epoch).all()
         assert ops.read_device_errors() == 0
 
 
@@ -166,18 +181,13 @@ def test_timeout_raises_from_the_sharding_api_and_resync_recovers():
     ex.resync()
     x_epoch = ex.epoch + 1  # the epoch the next call uses
     assert x_epoch >= 3
-    flags_b, lse_off = _layout(world, rows, units, D)
     o1 = torch.empty((1, 32, D), dtype=torch.float32, device="cuda")
     from paged_tierkv_b200 import ops as o
     _, _, l1 = o.decode_attention(d1["query"], d1["block_table"], d1["block_states"],
                                   d1["block_lengths"], d1["pools"], nb - cut, case["groups"],
                                   case["scaling"], out=o1, out_dtype=torch.float32, return_lse=True)
-    par = x_epoch & 1
-    box0[flags_b:lse_off].view(torch.float32).view(2, rows, world, D)[par, :, 1, :] = o1.view(rows, D)
-    box0[lse_off:lse_off + 2 * rows * world * 4].view(torch.float32).view(2, rows, world)[par, :, 1] = \
-        l1.view(rows)
+    _publish(box0, world, rows, D, 1, x_epoch, o1, l1)
     torch.cuda.synchronize()
-    box0[:flags_b].view(torch.int32)[units:2 * units] = x_epoch
     res = dec(*args(d0))
     dec.check()
     np.testing.assert_allclose(res.out.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
@@ -231,5 +241,7 @@ def test_device_epoch_under_graph_replay():
         torch.testing.assert_close(out.float(), ref.float(), atol=2e-4, rtol=2e-3)
     # the warm-up call, the capture (not run) and four replays: epoch 1 + 1 + 4
     assert int(ex.epoch_t.item()) == 6
-    flags = box[:256].view(torch.int32)[:units]
-    assert (flags.cpu().numpy() == 5).all()
+    # the last replay (epoch 5, odd parity) stamped every word it wrote
+    ow, lw = _words(box, 1, rows, 128)
+    assert ((ow[1] >> 32) == 5).all() and ((lw[1] >> 32) == 5).all()
+    assert ((ow[0] >> 32) == 4).all()
