@@ -391,11 +391,11 @@ __device__ __forceinline__ void merge_parts(const float* po, const float* plse, 
 }
 
 // The world partials of the G rows row0.. (this rank's inbox, epoch parity)
-// merged into the output: one warp per head.  Lane q < world polls rank q's
-// LSE word, then every lane polls the words of its 4 dims of each rank's
-// partial and accumulates them.  All polls share one deadline (timeout_ns,
-// 2 s by default); past it they give up, record TKV_DEVERR_TIMEOUT and treat
-// the missing partials as empty.
+// merged into the output: one warp per head.  Every lane requests, in one
+// round, its 4 dims of every rank's partial (and lane q < world rank q's LSE
+// word); only words that do not carry the call's epoch yet are polled again.
+// All polls share one deadline (timeout_ns, 2 s by default); past it they
+// give up, record TKV_DEVERR_TIMEOUT and count the missing partials as empty.
 template <int D, int NT>
 __device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int G, uint32_t epoch) {
   constexpr int kVecs = D / 4;                 // float4 per row
@@ -412,20 +412,30 @@ __device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int 
   bool late = false;  // this lane gave up on a word
   for (int h = warp; h < G; h += NT / 32) {
     const size_t row = row0 + h;
-    float lq = -INFINITY;
+    const uint64_t* lsrc = xl + row * W + lane;
+    uint64_t lw = lane < W ? ld_relaxed_sys(lsrc) : 0;
+    uint64_t a[8][4];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q < W && (q % kSplitLanes) == q0) {
+        const uint64_t* src = xo + (row * W + q) * D + 4 * v;
+        ld_relaxed_sys_v2(src, a[q][0], a[q][1]);
+        ld_relaxed_sys_v2(src + 2, a[q][2], a[q][3]);
+      } else {
+        a[q][0] = a[q][1] = a[q][2] = a[q][3] = 0;
+      }
+    }
     if (lane < W) {
-      const uint64_t* src = xl + row * W + lane;
-      uint64_t w = ld_relaxed_sys(src);
-      while (!x_valid(w, epoch) && !late) {
+      while (!x_valid(lw, epoch) && !late) {
         if (globaltimer() - t0 > limit) {
           late = true;
         } else {
           __nanosleep(32);
-          w = ld_relaxed_sys(src);
+          lw = ld_relaxed_sys(lsrc);
         }
       }
-      if (x_valid(w, epoch)) lq = x_value(w);
     }
+    const float lq = (lane < W && x_valid(lw, epoch)) ? x_value(lw) : -INFINITY;
     float M = lq;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
@@ -438,26 +448,23 @@ __device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int 
     for (int q = 0; q < 8; ++q) {
       const float w = __shfl_sync(0xffffffffu, wq, q);  // 0 for absent / empty partials
       if (q < W && (q % kSplitLanes) == q0 && w > 0.f) {
-        const uint64_t* src = xo + (row * W + q) * D + 4 * v;
-        uint64_t a0, a1, a2, a3;
-        ld_relaxed_sys_v2(src, a0, a1);
-        ld_relaxed_sys_v2(src + 2, a2, a3);
-        bool ok = x_valid(a0, epoch) && x_valid(a1, epoch) && x_valid(a2, epoch) &&
-                  x_valid(a3, epoch);
+        bool ok = x_valid(a[q][0], epoch) && x_valid(a[q][1], epoch) &&
+                  x_valid(a[q][2], epoch) && x_valid(a[q][3], epoch);
         while (!ok && !late) {
           if (globaltimer() - t0 > limit) {
             late = true;
           } else {
             __nanosleep(32);
-            ld_relaxed_sys_v2(src, a0, a1);
-            ld_relaxed_sys_v2(src + 2, a2, a3);
-            ok = x_valid(a0, epoch) && x_valid(a1, epoch) && x_valid(a2, epoch) &&
-                 x_valid(a3, epoch);
+            const uint64_t* src = xo + (row * W + q) * D + 4 * v;
+            ld_relaxed_sys_v2(src, a[q][0], a[q][1]);
+            ld_relaxed_sys_v2(src + 2, a[q][2], a[q][3]);
+            ok = x_valid(a[q][0], epoch) && x_valid(a[q][1], epoch) &&
+                 x_valid(a[q][2], epoch) && x_valid(a[q][3], epoch);
           }
         }
         if (ok) {
-          acc.x += w * x_value(a0); acc.y += w * x_value(a1);
-          acc.z += w * x_value(a2); acc.w += w * x_value(a3);
+          acc.x += w * x_value(a[q][0]); acc.y += w * x_value(a[q][1]);
+          acc.z += w * x_value(a[q][2]); acc.w += w * x_value(a[q][3]);
         }
       }
     }

@@ -85,49 +85,59 @@ def test_one_rank_exchange_equals_plain_decode(splits):
             torch.testing.assert_close(s, ref_s, atol=1e-6, rtol=1e-4)
 
 
+@pytest.mark.parametrize("world", [2, 8])
 @pytest.mark.parametrize("splits", [1, 4])
-def test_two_ranks_with_the_peer_already_published(splits):
+def test_ranks_with_the_peers_already_published(splits, world):
+    """Rank 0 of `world` ranks runs; the other ranks' partials of its calls are
+    computed from their block ranges and written into rank 0's inbox by the
+    host beforehand."""
     from paged_tierkv_b200 import ops, sharding
     nb = 70
-    case = make_case(seed=80 + splits, batch=2, q_heads=32, kv_heads=8, head_dim=128, num_blocks=nb,
-                     max_blocks=nb)
+    case = make_case(seed=80 + splits + world, batch=2, q_heads=32, kv_heads=8, head_dim=128,
+                     num_blocks=nb, max_blocks=nb)
     ref, _, ref_scores = oracle_decode(case)
-    cut = 33
+    cuts = [0, 33, nb] if world == 2 else [0, 9, 17, 26, 35, 44, 52, 61, nb]
     shards = []
-    for sl in (slice(0, cut), slice(cut, nb)):
-        shards.append(dict(case, block_table=np.ascontiguousarray(case["block_table"][:, sl]),
-                           block_states=np.ascontiguousarray(case["block_states"][:, sl]),
-                           block_lengths=np.ascontiguousarray(case["block_lengths"][:, sl])))
-    d0, d1 = to_device(shards[0]), to_device(shards[1])
-    d0["num_blocks"], d1["num_blocks"] = cut, nb - cut
-    rows, units, world, D = 2 * 32, 2 * 8, 2, 128
-    box0, box1 = _inbox(world, rows, units, D), _inbox(world, rows, units, D)
+    for r in range(world):
+        sl = slice(cuts[r], cuts[r + 1])
+        sh = dict(case, block_table=np.ascontiguousarray(case["block_table"][:, sl]),
+                  block_states=np.ascontiguousarray(case["block_states"][:, sl]),
+                  block_lengths=np.ascontiguousarray(case["block_lengths"][:, sl]))
+        dd = to_device(sh)
+        dd["num_blocks"] = cuts[r + 1] - cuts[r]
+        shards.append((sh, dd))
+    rows, units, D = 2 * 32, 2 * 8, 128
+    boxes = [_inbox(world, rows, units, D) for _ in range(world)]
     ex = sharding.PeerExchange(rows_cap=rows, units_cap=units, head_dim=D,
-                               inboxes=[box0.data_ptr(), box1.data_ptr()], rank=0)
+                               inboxes=[b.data_ptr() for b in boxes], rank=0)
     for call in range(3):
         x = ex.next()
         par = x.epoch & 1
-        # what rank 1's launch would have stored into rank 0's inbox
-        o1 = torch.empty((2, 32, D), dtype=torch.float32, device="cuda")
-        _, _, l1 = ops.decode_attention(d1["query"], d1["block_table"], d1["block_states"],
-                                        d1["block_lengths"], d1["pools"], nb - cut, case["groups"],
-                                        case["scaling"], out=o1, out_dtype=torch.float32,
-                                        return_lse=True, num_splits=splits)
-        _publish(box0, world, rows, D, 1, x.epoch, o1, l1)
+        # what ranks 1.. would have stored into rank 0's inbox
+        for r in range(1, world):
+            dr = shards[r][1]
+            o_r = torch.empty((2, 32, D), dtype=torch.float32, device="cuda")
+            _, _, l_r = ops.decode_attention(dr["query"], dr["block_table"], dr["block_states"],
+                                             dr["block_lengths"], dr["pools"], dr["num_blocks"],
+                                             case["groups"], case["scaling"], out=o_r,
+                                             out_dtype=torch.float32, return_lse=True,
+                                             num_splits=splits)
+            _publish(boxes[0], world, rows, D, r, x.epoch, o_r, l_r)
         torch.cuda.synchronize()
-        out, scores, lse = _run(d0, shards[0], num_splits=splits, return_scores=True,
+        d0 = shards[0][1]
+        out, scores, lse = _run(d0, shards[0][0], num_splits=splits, return_scores=True,
                                 return_lse=True, exchange=x)
         torch.cuda.synchronize()
         np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
         # rank 0's scores are normalised over the whole contexts
-        np.testing.assert_allclose(scores.cpu().numpy(), ref_scores[:, :, :cut], atol=1e-4, rtol=1e-3)
-        # rank 0 published its partial to "rank 1", every word tagged with the epoch
-        ow1, lw1 = _words(box1, world, rows, D)
-        assert ((ow1[par, :, 0, :] >> 32) == x.epoch).all()
-        assert ((lw1[par, :, 0] >> 32) == x.epoch).all()
-        # and to itself: the words it merged, equal in value to its own LSE output
-        ow0, lw0 = _words(box0, world, rows, D)
-        assert ((lw0[par, :, 0] >> 32) == x.epoch).all()
+        np.testing.assert_allclose(scores.cpu().numpy(), ref_scores[:, :, :cuts[1]], atol=1e-4,
+                                   rtol=1e-3)
+        # rank 0 published its partial to every rank (itself included), every
+        # word tagged with the epoch
+        for r in range(world):
+            ow, lw = _words(boxes[r], world, rows, D)
+            assert ((ow[par, :, 0, :] >> 32) == x.epoch).all()
+            assert ((lw[par, :, 0] >> 32) == x.epoch).all()
         assert ops.read_device_errors() == 0
 
 
