@@ -496,10 +496,8 @@ __device__ __forceinline__ void x_merge(const DecodeParams& p, size_t row0, int 
 // into every rank's inbox) and, with a device epoch, advances the epoch once
 // the launch's last unit is done.
 template <int D, int NT>
-__device__ __forceinline__ void x_finish(const DecodeParams& p, size_t unit, size_t row0, int G,
-                                         float* wsl, uint32_t epoch) {
-  (void)unit;
-  (void)wsl;
+__device__ __forceinline__ void x_finish(const DecodeParams& p, size_t row0, int G,
+                                         uint32_t epoch) {
   x_merge<D, NT>(p, row0, G, epoch);
   // A device epoch advances when the last unit of the launch is done: every
   // CTA of the launch has read the epoch by then (at its start).
@@ -1244,8 +1242,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   }
   if (nsplit == 1) {
     if (p.x_world > 0)
-      x_finish<D, Cfg::kThreads>(p, unit, (size_t)seq * Hq + (size_t)kvh * G, G,
-                                 reinterpret_cast<float*>(stages), (uint32_t)misc[2]);
+      x_finish<D, Cfg::kThreads>(p, (size_t)seq * Hq + (size_t)kvh * G, G, (uint32_t)misc[2]);
     return;
   }
 
@@ -1282,7 +1279,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
     const uint32_t epoch = (uint32_t)misc[2];
     merge_parts<D, Cfg::kThreads>(p.part_o, p.part_lse, nsplit, 0, nsplit, row0, G, wsl, p,
                                   nullptr, nullptr, 0, 0, p.x_world > 0, epoch);
-    if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl, epoch);
+    if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, row0, G, epoch);
     return;
   }
   if (threadIdx.x == 0) atomicExch(ticket, 0u);
@@ -1302,7 +1299,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, BS, FMT, QT>::kThreads, TKV_MIN_C
   const uint32_t epoch = (uint32_t)misc[2];
   merge_parts<D, Cfg::kThreads>(p.gpart_o, p.gpart_lse, ngroups, 0, ngroups, row0, G, wsl, p,
                                 nullptr, nullptr, 0, 0, p.x_world > 0, epoch);
-  if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, unit, row0, G, wsl, epoch);
+  if (p.x_world > 0) x_finish<D, Cfg::kThreads>(p, row0, G, epoch);
 }
 
 // ---------------------------------------------------------------- dispatch
