@@ -23,7 +23,7 @@ fractions at block 16 and 32); `--no-single-extras` leaves them out.
 The same line carries two strong-scaling objects (fixed total work split over
 the N ranks, each replayed from a CUDA graph, max over ranks):
   c4 -- configuration 4, one 131072-token context over 32 layers, each layer's
-        blocks split into byte-balanced contiguous ranges; ms per step with
+        blocks split into time-balanced contiguous ranges; ms per step with
         the partials exchanged inside the decode launch over peer memory,
         the NCCL all-gather + merge variant beside it, the local shard decode
         alone, and layer-0 parity against the unsharded one-rank output;
@@ -543,10 +543,11 @@ def run_ours(a, rank, world, dist_on, device):
     print(json.dumps(line), flush=True)
 
 
-def _timed_graph(step, steps, warmup, dist_on, device, graph=True, side=None):
+def _timed_graph(step, steps, warmup, dist_on, device, graph=True, side=None, per_rank=False):
     """Device ms per call of `step`, captured once in a CUDA graph on a side
     stream (warm-up first, so nothing is allocated during capture) and
-    replayed; max over ranks.  Every rank makes the same collective calls."""
+    replayed; max over ranks (with `per_rank`, also every rank's own time).
+    Every rank makes the same collective calls."""
     side = side or torch.cuda.Stream(device=device)
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -577,13 +578,19 @@ def _timed_graph(step, steps, warmup, dist_on, device, graph=True, side=None):
         torch.distributed.barrier()
     del g
     t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=device)
+    ranks = [float(t[0])]
     if dist_on:
+        if per_rank:
+            allt = torch.empty(torch.distributed.get_world_size(), dtype=torch.float64,
+                               device=device)
+            torch.distributed.all_gather_into_tensor(allt, t)
+            ranks = allt.tolist()
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t[0])
+    return (float(t[0]), ranks) if per_rank else float(t[0])
 
 
 def c4_layers(a, rank, world, device, layers):
-    """Configuration 4's per-rank shards: for each layer, the byte-balanced
+    """Configuration 4's per-rank shards: for each layer, the time-balanced
     contiguous block range of this rank, materialized as its own pools."""
     from paged_tierkv_b200 import workloads
     ctx, bs, d, hkv, hq = 131072, a.block_size, HEAD_DIM, KV_HEADS, Q_HEADS
@@ -605,7 +612,7 @@ def c4_layers(a, rank, world, device, layers):
 def c4_parity(a, rank, world, device):
     """Layer-0 parity of the sharded decode against one rank: every rank
     builds the whole 131072-token layer from the same seed and decodes its
-    byte-balanced block range with the exchange (or, for one rank, the whole
+    time-balanced block range with the exchange (or, for one rank, the whole
     range); rank 0 also decodes the unsharded layer.  Returns the largest
     difference relative to the output's scale (rank 0), and whether any rank
     recorded a device error."""
@@ -659,7 +666,9 @@ def c4_measure(a, rank, world, dist_on, device, steps, warmup, exchanges):
                              out_dtype=torch.float32 if world > 1 else None,
                              return_lse=lse if world > 1 else False)
 
-    res = {"local_ms": _timed_graph(local, steps, warmup, dist_on, device, not a.no_graph)}
+    local_ms, local_ranks = _timed_graph(local, steps, warmup, dist_on, device, not a.no_graph,
+                                         per_rank=True)
+    res = {"local_ms": local_ms, "local_ms_per_rank": local_ranks}
     for kind in (exchanges if world > 1 else ()):
         ex = None
         if kind == "p2p":
@@ -700,7 +709,7 @@ def c4_object(a, rank, world, dist_on, device, steps=50, warmup=5):
     rel, perr = c4_parity(a, rank, world, device)
     ms = res.get("p2p_ms", res["local_ms"])
     obj = {"workload": f"c4_ctx{ctx}_bs{bs}_l{a.layers}", "hot_blocks": n_hot, "warm_blocks": n_warm,
-           "partition": "byte-balanced contiguous block ranges, one per rank",
+           "partition": "contiguous block ranges balanced by estimated decode time (WARM bytes x 1.19), one per rank",
            "ms_per_step": round(ms, 4), "tokens_per_s": round(1000.0 / ms, 2),
            "GBps_all_gpus": round(all_bytes / (ms * 1e-3) / 1e9, 1),
            "local_decode_ms_per_step": round(res["local_ms"], 4),
@@ -710,6 +719,7 @@ def c4_object(a, rank, world, dist_on, device, steps=50, warmup=5):
         obj.update({
             "exchange": "p2p: epoch-tagged peer-memory stores inside the decode launch",
             "exchange_us_per_layer": round((res["p2p_ms"] - res["local_ms"]) * 1e3 / a.layers, 2),
+            "local_decode_ms_per_step_per_rank": [round(x, 4) for x in res["local_ms_per_rank"]],
             "nccl_ms_per_step": round(res["nccl_ms"], 4),
             "nccl_tokens_per_s": round(1000.0 / res["nccl_ms"], 2),
             "nccl_us_per_layer_over_local": round((res["nccl_ms"] - res["local_ms"]) * 1e3 / a.layers, 2),
@@ -882,13 +892,14 @@ def run_c4(a, rank, world, dist_on, device):
         "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": f"c4_ctx{ctx}_bs{bs}_l{a.layers}", "hot_blocks": n_hot,
-                   "warm_blocks": n_warm, "partition": "byte-balanced contiguous block ranges",
+                   "warm_blocks": n_warm, "partition": "contiguous block ranges balanced by estimated decode time",
                    "exchange": ("none" if world == 1 else
                                 "epoch-tagged peer-memory stores inside the decode launch"
                                 if a.exchange == "p2p" else
                                 "NCCL all_gather of packed (o, lse) per layer"),
                    "cuda_graph": not a.no_graph},
         "local_decode_ms_per_step": round(res["local_ms"], 4),
+        "local_decode_ms_per_step_per_rank": [round(x, 4) for x in res["local_ms_per_rank"]],
         "GBps_all_gpus": round(all_bytes / (ms * 1e-3) / 1e9, 1),
         "gpu_launches": a.steps * a.layers * (1 if (world == 1 or a.exchange == "p2p") else 2),
     }
