@@ -67,3 +67,30 @@ def test_reference_arm_runs_on_the_host_with_our_config():
                                     block_size=16)
     assert line["config"] == bench.bench_config(args, 1)
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_balanced_block_ranges_cover_the_context_with_equal_estimated_time(world):
+    """Configuration 4's partition: contiguous ranges that cover every block
+    once, each rank's estimated decode time within one block of the mean
+    (WARM bytes weighted by the kernel's measured time per byte)."""
+    nb, bs, d = 8192, 16, 128
+    n_hot, n_warm, _ = workloads.tier_counts(nb, 0.10, 0.60)
+    states = workloads.assign_tiers(1, nb, n_hot, n_warm, seed=5000)
+    ranges = workloads.balanced_block_ranges(states, world, bs, d)
+    assert len(ranges) == world and ranges[0][0] == 0 and ranges[-1][1] == nb
+    assert all(ranges[k][1] == ranges[k + 1][0] for k in range(world - 1))
+    st = states.reshape(-1)[:nb].tolist()
+
+    def cost(s):
+        if s == ops.HOT_STATE:
+            return bs * 4 * d + 12
+        if s == ops.WARM_STATE:
+            return bs * (2 * d + 8) * workloads.WARM_TIME_PER_BYTE + 12
+        return 12
+    per = [sum(cost(s) for s in st[a:b]) for a, b in ranges]
+    mean = sum(per) / world
+    assert max(abs(c - mean) for c in per) <= cost(ops.HOT_STATE) + 1e-6
+    if world > 1:  # the HOT window at the end: the last rank holds fewer blocks
+        sizes = [b - a for a, b in ranges]
+        assert sizes[-1] < sizes[0]
