@@ -47,6 +47,40 @@ def block_range(num_blocks: int, rank: int, world: int) -> tuple[int, int]:
     return start, min(start + per, num_blocks)
 
 
+# Time per HBM byte of a WARM tile relative to a HOT tile: the decode
+# kernel's marginal rates measured on B200 over configuration-5 mixes (7.19
+# TB/s all-HOT, 6.04 TB/s WARM-heavy).
+WARM_TIME_PER_BYTE = 7.19 / 6.04
+
+
+def balanced_block_ranges(states: torch.Tensor, world: int, block_size: int, head_dim: int):
+    """Contiguous block ranges [start, end), one per rank, whose estimated
+    decode times are as equal as possible across ``world`` ranks, for the
+    block states of one sequence's layer (``states``: [num_blocks] or
+    [1, num_blocks]; the first row is used): HBM bytes per token (HOT 4*D, WARM
+    2*D + 8, COLD only its table entry) with WARM bytes weighted by
+    ``WARM_TIME_PER_BYTE``, since the consumers make WARM tiles slower per
+    byte than HOT ones.  (Measured on configuration 4 at 2 GPUs: balancing
+    bytes left the WARM-only rank 13 % slower than the rank with the recent
+    HOT window, and the exchange waits for the slower one.)  The LSE merge
+    does not depend on where the boundaries fall."""
+    st = states.reshape(-1, states.shape[-1])[0].tolist()
+    cost = [block_size * (4 * head_dim if s == ops.HOT_STATE else
+                          (2 * head_dim + 8) * WARM_TIME_PER_BYTE if s == ops.WARM_STATE else 0)
+            + 12 for s in st]
+    total = float(sum(cost))
+    bounds, acc, r = [0], 0.0, 1
+    for i, c in enumerate(cost):
+        acc += c
+        while r < world and acc >= total * r / world:
+            bounds.append(i + 1)
+            r += 1
+    while len(bounds) < world + 1:
+        bounds.append(len(st))
+    bounds[-1] = len(st)
+    return [(bounds[k], bounds[k + 1]) for k in range(world)]
+
+
 @dataclass
 class ShardResult:
     out: torch.Tensor                   # [batch, num_heads, head_dim]

@@ -16,7 +16,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import ops
+from . import ops, sharding
 
 
 def tier_counts(num_blocks: int, hot_frac: float, warm_frac: float | None = None):
@@ -150,36 +150,9 @@ def make_workload(*, batch: int, q_heads: int, kv_heads: int, head_dim: int, blo
     return wl
 
 
-# Time per HBM byte of a WARM tile relative to a HOT tile: the decode
-# kernel's marginal rates measured on B200 over configuration-5 mixes (7.19
-# TB/s all-HOT, 6.04 TB/s WARM-heavy).
-WARM_TIME_PER_BYTE = 7.19 / 6.04
-
-
-def balanced_block_ranges(states: torch.Tensor, world: int, block_size: int, head_dim: int):
-    """Contiguous block ranges whose estimated decode times are as equal as
-    possible across ``world`` ranks: HBM bytes per token (HOT 4*D, WARM
-    2*D + 8, COLD only its table entry) with WARM bytes weighted by
-    ``WARM_TIME_PER_BYTE``, since the consumers make WARM tiles slower per
-    byte than HOT ones.  (Measured on configuration 4 at 2 GPUs: balancing
-    bytes left the WARM-only rank 13 % slower than the rank with the recent
-    HOT window, and the exchange waits for the slower one.)  The LSE merge
-    does not depend on where the boundaries fall."""
-    st = states.reshape(-1, states.shape[-1])[0].tolist()
-    cost = [block_size * (4 * head_dim if s == ops.HOT_STATE else
-                          (2 * head_dim + 8) * WARM_TIME_PER_BYTE if s == ops.WARM_STATE else 0)
-            + 12 for s in st]
-    total = float(sum(cost))
-    bounds, acc, r = [0], 0.0, 1
-    for i, c in enumerate(cost):
-        acc += c
-        while r < world and acc >= total * r / world:
-            bounds.append(i + 1)
-            r += 1
-    while len(bounds) < world + 1:
-        bounds.append(len(st))
-    bounds[-1] = len(st)
-    return [(bounds[k], bounds[k + 1]) for k in range(world)]
+# Configuration 4's partition: the sharding module's time-balanced ranges.
+balanced_block_ranges = sharding.balanced_block_ranges
+WARM_TIME_PER_BYTE = sharding.WARM_TIME_PER_BYTE
 
 
 def decode(wl: Workload, **kw):
