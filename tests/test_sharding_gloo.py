@@ -59,7 +59,7 @@ def _oracle_merge(part_o, part_lse, out_dtype):
     return torch.from_numpy(o).to(torch.float32), torch.from_numpy(lse).to(torch.float32)
 
 
-def _worker(rank, world, port, result_q):
+def _worker(rank, world, port, result_q, partition="count"):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
@@ -71,7 +71,12 @@ def _worker(rank, world, port, result_q):
         case = make_case(seed=31, batch=2, q_heads=8, kv_heads=2, head_dim=64, num_blocks=23,
                          max_blocks=23)
         nb = int(case["num_blocks"][0])
-        start, end = sharding.block_range(nb, rank, world)
+        if partition == "time":
+            start, end = sharding.balanced_block_ranges(
+                torch.from_numpy(case["block_states"]), world, case["hot_k"].shape[2],
+                case["hot_k"].shape[3])[rank]
+        else:
+            start, end = sharding.block_range(nb, rank, world)
         sl = slice(start, end)
         pools = {k: case[k] for k in ("hot_k", "hot_v", "warm_k", "warm_v", "k_scale", "k_zero",
                                       "v_scale", "v_zero")}
@@ -87,14 +92,16 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("partition", ["count", "time"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_context_sharded_decode_over_ranks(world):
+def test_context_sharded_decode_over_ranks(world, partition):
     from oracle import tierkv_oracle as orc
     from tierkv_cases import make_case
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, partition))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]
